@@ -1,0 +1,460 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention path: decode KV-read GB/s and prefill attention TFLOP/s.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline (`value`): Qwen3-8B-shaped decode attention -- 32 sequences, one new token each,
+against a bf16 KV cache of 4096 rows per sequence (hidden 4096, 32 q heads, 8 kv heads,
+head_dim 128, per-head QK-RMSNorm eps 1e-6, RoPE theta 1e6).  One step = the fused QKV epilogue
+(QK-norm + RoPE + KV append of the new token) + split-K flash-decode over 4096 rows, i.e. the
+attention step between the q/k/v projections and o_proj.  Metric = algorithmic KV bytes read
+(2 * B * Hkv * L * D * 2 B = 536,870,912 B per step) / step time.  The cache (537 MB) is larger
+than L2 (126 MB), so every step streams it from HBM.
+
+Secondary (`prefill`): Qwen3-8B causal prefill attention, batch 4 x 8192 rows, same head
+geometry; FLOPs = 4 * B * H * D * S(S+1)/2 = 2.199e12 per step.
+
+Multi-GPU (torchrun, one rank per GPU): decode is split by request batches -- every rank owns
+its own 32 sequences (weak scaling, no collective on the data path); prefill is split by
+KV-head groups (H/N query heads and Hkv/N kv heads per rank).  Timing is max over ranks.
+
+`--impl reference` times the reference's own CPU LibTorch path (oracle/_ref, compiled from the
+reference sources) on this host's cores on bounded samples of the same decode workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "prefill attn TFLOP/s & decode KV-read GB/s per B200, 1/2/4/8 GPU vs CPU ref"
+
+# Qwen3-8B attention geometry
+HIDDEN, H, HKV, D = 4096, 32, 8, 128
+THETA, EPS = 1e6, 1e-6
+DEC_B, DEC_L = 32, 4096
+PRE_B, PRE_S = 4, 8192
+
+
+def decode_kv_bytes(b, hkv, L, d):
+    return 2 * b * hkv * L * d * 2
+
+
+def prefill_flops(b, h, d, s):
+    return 4.0 * b * h * d * s * (s + 1) / 2
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def profile_traffic(name):
+    """Per-launch DRAM bytes recorded from an ncu capture in profiles/<name>.md
+    (a line 'traffic_bytes_per_launch: N'), or None."""
+    p = os.path.join(ROOT, "profiles", name + ".md")
+    try:
+        for line in open(p):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.proc = None
+        self.gpu = gpu_index
+        self.t0 = self.t1 = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------
+# CPU reference arm
+# ------------------------------------------------------------------------------------------
+
+def cpu_reference_decode(steps: int, warmup: int, budget_s: float = 90.0):
+    """The reference's fp32 CPU path (Attention::ForwardProjected via oracle/_ref) on a bounded
+    sample of the decode workload: `sample_b` of the 32 sequences, full cache length, all heads
+    (QK-norm prologue included, as TransformerBlock.h runs it).  Falls back to the numpy port of
+    the oracle when the compiled reference is absent.  Returns a dict for the JSON line."""
+    import numpy as np
+    import torch
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    sample_b = 1
+    kind = "reference"
+    try:
+        sys.path.insert(0, os.path.join(ROOT, "oracle", "_ref"))
+        import mllm_ref as R  # compiled from the reference sources
+        R.set_num_threads(cores)
+    except Exception:
+        R = None
+        kind = "port"
+    g = torch.Generator().manual_seed(1234)
+    L = DEC_L
+    kc = torch.randn(sample_b, HKV, L - 1, D, generator=g)
+    vc = torch.randn(sample_b, HKV, L - 1, D, generator=g)
+    h = torch.randn(sample_b, 1, HIDDEN, generator=g)
+    w_q = torch.randn(H * D, HIDDEN, generator=g) * 0.02
+    w_k = torch.randn(HKV * D, HIDDEN, generator=g) * 0.02
+    w_v = torch.randn(HKV * D, HIDDEN, generator=g) * 0.02
+    w_o = torch.randn(HIDDEN, H * D, generator=g) * 0.02
+    gq = 1 + 0.1 * torch.randn(D, generator=g)
+    gk = 1 + 0.1 * torch.randn(D, generator=g)
+    pos = torch.tensor([L - 1])
+
+    def one():
+        if R is not None:
+            q = R.linear(h, w_q).view(sample_b, 1, H, D).transpose(1, 2)
+            q = R.rms_norm(q, gq, EPS)
+            k = R.linear(h, w_k).view(sample_b, 1, HKV, D).transpose(1, 2)
+            k = R.rms_norm(k, gk, EPS)
+            v = R.linear(h, w_v).view(sample_b, 1, HKV, D).transpose(1, 2)
+            R.attention_forward_projected(q, k, v, w_o, H, HKV, D, THETA, pos, kc, vc, True)
+        else:
+            from oracle import attention_oracle as O
+            hn = h.numpy()
+            q, k, v = O.qwen_qkv_prologue(hn, w_q.numpy(), w_k.numpy(), w_v.numpy(), gq.numpy(), gk.numpy(),
+                                          H, HKV, D, EPS)
+            cache = O.KVCache(kc.numpy(), vc.numpy())
+            O.attention_forward_projected(q, k, v, w_o.numpy(), H, HKV, D, THETA, pos.numpy(), cache)
+
+    for _ in range(max(1, min(warmup, 2))):
+        one()
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    med = statistics.median(times)
+    nbytes = decode_kv_bytes(sample_b, HKV, L, D)
+    return {"value": nbytes / med / 1e9, "unit": "GB/s", "cores": cores, "kind": kind,
+            "sample": f"{sample_b} of {DEC_B} sequences (L={L}, all {H} q heads), fp32 CPU, median of "
+                      f"{len(times)} runs", "steps_timed": len(times), "ms_per_step": med * 1e3}
+
+
+# ------------------------------------------------------------------------------------------
+# GPU arm
+# ------------------------------------------------------------------------------------------
+
+def run_gpu(args, rank, world, device):
+    import torch
+    from mllm_b200 import abi, build
+
+    if rank == 0 or not os.path.exists(build.lib_path()):
+        build.build()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    lib = abi.load()
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    gen = torch.Generator(device=device).manual_seed(1000 + rank)
+
+    # ------------------------------- decode workload -------------------------------
+    B, L = DEC_B, DEC_L
+    kbuf = torch.randn(B, HKV, L, D, device=device, generator=gen).bfloat16()
+    vbuf = torch.randn(B, HKV, L, D, device=device, generator=gen).bfloat16()
+    qkv = (torch.randn(B, (H + 2 * HKV) * D, device=device, generator=gen) * 0.5).bfloat16()
+    gq = (1 + 0.1 * torch.randn(D, device=device, generator=gen)).bfloat16()
+    gk = (1 + 0.1 * torch.randn(D, device=device, generator=gen)).bfloat16()
+    pos = torch.full((B,), L - 1, dtype=torch.int64, device=device)
+    start = torch.full((B,), L - 1, dtype=torch.int32, device=device)   # new token -> row L-1
+    lens = torch.full((B,), L, dtype=torch.int32, device=device)        # attend over L rows
+    q_rot = torch.empty(B, H, D, dtype=torch.bfloat16, device=device)
+    out = torch.empty(B, H * D, dtype=torch.bfloat16, device=device)
+    ws_bytes = lib.mllm_decode_attention_workspace_size(B, H, HKV, D, L)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+    csb, csh, cst = kbuf.stride()[:3]
+    row = (H + 2 * HKV) * D
+    scale = 1.0 / math.sqrt(D)
+
+    def epilogue(src):
+        st = lib.mllm_qkv_epilogue_bf16(
+            src.data_ptr(), row, row, D,
+            src.data_ptr() + H * D * 2, row, row, D,
+            src.data_ptr() + (H + HKV) * D * 2, row, row, D,
+            B, 1, H, HKV, D, pos.data_ptr(), 1, 0, THETA, None, None, 0, 0,
+            gq.data_ptr(), gk.data_ptr(), EPS, q_rot.data_ptr(),
+            kbuf.data_ptr(), vbuf.data_ptr(), csb, csh, cst, L, start.data_ptr(), sh)
+        assert st == 0, lib.mllm_attn_last_error()
+
+    def decode(dst):
+        st = lib.mllm_decode_attention_bf16(q_rot.data_ptr(), kbuf.data_ptr(), vbuf.data_ptr(), csb, csh, cst,
+                                            lens.data_ptr(), B, H, HKV, D, L, scale, dst.data_ptr(),
+                                            ws.data_ptr(), ws_bytes, sh)
+        assert st == 0, lib.mllm_attn_last_error()
+
+    nch = None
+    launches_per_step = 3  # epilogue + split + combine (combine only when the cache is split)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        epilogue(qkv)
+        decode(out)
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
+                           else int(os.environ.get("LOCAL_RANK", 0)))
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.3)
+    ev_dec = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    t0.record(stream)
+    for i in range(args.steps):
+        epilogue(qkv)
+        ev_dec[i][0].record(stream)
+        decode(out)
+        ev_dec[i][1].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    elapsed_ms = max_over_ranks(t0.elapsed_time(t1))
+    dec_ms = statistics.mean(a.elapsed_time(b) for a, b in ev_dec)
+    dec_ms = max_over_ranks(dec_ms)
+
+    # ---- e2e through the C ABI with host buffers: H2D of the step's q/k/v, D2H of the output
+    h_in = torch.empty_like(qkv, device="cpu").pin_memory()
+    h_in.copy_(qkv.cpu())
+    h_out = torch.empty(out.shape, dtype=out.dtype, device="cpu").pin_memory()
+    d_in = torch.empty_like(qkv)
+    for _ in range(args.warmup):
+        d_in.copy_(h_in, non_blocking=True)
+        epilogue(d_in)
+        decode(out)
+        h_out.copy_(out, non_blocking=True)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        d_in.copy_(h_in, non_blocking=True)
+        epilogue(d_in)
+        decode(out)
+        h_out.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+
+    # ------------------------------- prefill workload -------------------------------
+    pre = None
+    if not args.skip_prefill and H % world == 0 and HKV % world == 0:
+        Hr, Hkvr = H // world, HKV // world
+        Bp, S = PRE_B, PRE_S
+        qkv_p = (torch.randn(Bp, S, (Hr + 2 * Hkvr) * D, device=device, generator=gen) * 0.5).bfloat16()
+        kp = torch.empty(Bp, Hkvr, S, D, dtype=torch.bfloat16, device=device)
+        vp = torch.empty_like(kp)
+        qp = torch.empty(Bp, Hr, S, D, dtype=torch.bfloat16, device=device)
+        op = torch.empty(Bp, S, Hr * D, dtype=torch.bfloat16, device=device)
+        pos_p = torch.arange(S, dtype=torch.int64, device=device)
+        start_p = torch.zeros(Bp, dtype=torch.int32, device=device)
+        prow = (Hr + 2 * Hkvr) * D
+        psb, psh, pst = kp.stride()[:3]
+
+        def epi_p():
+            st = lib.mllm_qkv_epilogue_bf16(
+                qkv_p.data_ptr(), S * prow, prow, D,
+                qkv_p.data_ptr() + Hr * D * 2, S * prow, prow, D,
+                qkv_p.data_ptr() + (Hr + Hkvr) * D * 2, S * prow, prow, D,
+                Bp, S, Hr, Hkvr, D, pos_p.data_ptr(), 0, 1, THETA, None, None, 0, 0,
+                gq.data_ptr(), gk.data_ptr(), EPS, qp.data_ptr(), kp.data_ptr(), vp.data_ptr(),
+                psb, psh, pst, S, start_p.data_ptr(), sh)
+            assert st == 0, lib.mllm_attn_last_error()
+
+        def attn_p():
+            st = lib.mllm_prefill_attention_bf16(qp.data_ptr(), kp.data_ptr(), vp.data_ptr(), psb, psh, pst,
+                                                 Bp, Hr, Hkvr, D, S, S, scale, op.data_ptr(), sh)
+            assert st == 0, lib.mllm_attn_last_error()
+
+        ksteps = max(3, min(args.steps, 20))
+        for _ in range(args.warmup):
+            epi_p()
+            attn_p()
+        evp = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(ksteps)]
+        p0 = torch.cuda.Event(enable_timing=True)
+        p1 = torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        p0.record(stream)
+        for i in range(ksteps):
+            epi_p()
+            evp[i][0].record(stream)
+            attn_p()
+            evp[i][1].record(stream)
+        p1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        pre_ms = max_over_ranks(p0.elapsed_time(p1)) / ksteps
+        attn_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in evp))
+        pre = {"pre_ms": pre_ms, "attn_ms": attn_ms, "steps": ksteps}
+        del qkv_p, kp, vp, qp, op
+
+    clocks = sampler.stop() if rank == 0 else None
+    return {"elapsed_ms": elapsed_ms, "dec_ms": dec_ms, "e2e_ms": e2e_ms, "pre": pre, "clocks": clocks,
+            "launches_per_step": launches_per_step,
+            "h2d": qkv.numel() * 2, "d2h": out.numel() * 2}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--skip-prefill", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    n = max(args.gpus, world)
+    config = {"workload": f"Qwen3-8B decode attention: batch {DEC_B} x 1 new token, bf16 KV cache "
+                          f"{DEC_L} rows/seq, H={H} Hkv={HKV} D={D}, QK-norm, theta 1e6 (per rank)",
+              "batch": DEC_B, "kv_len": DEC_L, "num_heads": H, "num_kv_heads": HKV, "head_dim": D,
+              "parallelism": f"request-batch replicas x{n} (decode); kv-head groups /{n} (prefill)",
+              "l2": "inputs larger than L2 (537 MB KV cache per rank > 126 MB)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        r = cpu_reference_decode(args.steps, args.warmup)
+        line = {"metric": METRIC, "value": r["value"], "unit": "GB/s", "n_gpus": n, "steps": r["steps_timed"],
+                "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "impl": "reference", "config": config,
+                "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    import torch
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (the attention path has no CPU fallback)")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    res = run_gpu(args, rank, world, device)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    hbm_peak, tf_peak, peak_src = load_peaks()
+    kv_bytes = decode_kv_bytes(DEC_B, HKV, DEC_L, D)
+    ms = res["elapsed_ms"] / args.steps
+    value = kv_bytes * n / (ms * 1e-3) / 1e9
+    achieved = kv_bytes / (res["dec_ms"] * 1e-3) / 1e9
+    e2e_ms = res["e2e_ms"] / args.steps
+    cpu = None
+    if n == 1:
+        r = cpu_reference_decode(5, 1, budget_s=20.0)
+        cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": n, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config,
+            "e2e": {"value": kv_bytes * n / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"],
+                    "ms_per_step": e2e_ms},
+            "gpu_launches": res["launches_per_step"] * args.steps,
+            "roofline": {"bound": "hbm", "kernel": "decode_split_kernel<128> + decode_combine_kernel",
+                         "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                         "peak_source": peak_src, "traffic": profile_traffic("decode_qwen3_8b_b32_l4096")},
+            "cpu_baseline": cpu, "clocks": res["clocks"]}
+    if res["pre"] is not None:
+        p = res["pre"]
+        fl = prefill_flops(PRE_B, H, D, PRE_S)
+        line["prefill"] = {
+            "workload": f"Qwen3-8B causal prefill attention, batch {PRE_B} x {PRE_S}, heads split over {n} GPU(s)",
+            "value": fl / (p["pre_ms"] * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": p["pre_ms"],
+            "steps": p["steps"],
+            "roofline": {"bound": "tensor", "kernel": "prefill_kernel<128>",
+                         "achieved": fl / n / (p["attn_ms"] * 1e-3) / 1e12, "peak": tf_peak, "unit": "TFLOP/s",
+                         "frac": fl / n / (p["attn_ms"] * 1e-3) / 1e12 / tf_peak, "peak_source": peak_src,
+                         "traffic": profile_traffic("prefill_qwen3_8b_b4_s8192")}}
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

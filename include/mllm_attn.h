@@ -1,0 +1,162 @@
+/*
+ * mllm_attn.h -- C ABI of the B200 (sm_100a) attention path for the mLLM runtime.
+ *
+ * The mLLM runtime (pym2282/mLLM) runs attention as a chain of LibTorch calls inside
+ * `mllm::TransformerBlock::Forward` / `mllm::Attention::ForwardProjected`.  This library
+ * replaces that chain with three kernel families behind plain C entry points:
+ *
+ *   mllm_qkv_epilogue_bf16      per-head QK-RMSNorm + RoPE + KV-cache append, one kernel
+ *   mllm_prefill_attention_bf16 causal GQA attention over the cache (tcgen05 / TMEM / TMA)
+ *   mllm_decode_attention_bf16  split-K flash-decode over the cache (HBM-bound)
+ *
+ * plus the RoPE table builder and RoPE apply that back the `mllm::RoPE` facade.
+ *
+ * Conventions
+ *   - All tensor arguments are raw DEVICE pointers (e.g. `tensor.data_ptr()` of a CUDA
+ *     LibTorch tensor) on the current CUDA device; sizes and strides are in ELEMENTS.
+ *   - `head_dim` is the innermost, contiguous dimension of every tensor.
+ *   - Every call is asynchronous on `stream` (NULL = the legacy default stream) and
+ *     returns an mllm_status; no C++ exception crosses this boundary.  Argument errors are
+ *     detected on the host before anything is launched.
+ *   - The library never allocates device memory; callers pass workspaces.
+ *   - Not thread-safe per stream, like the reference runtime (one Generate at a time).
+ */
+#ifndef MLLM_ATTN_H_
+#define MLLM_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MLLM_API __attribute__((visibility("default")))
+#else
+#define MLLM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t / CUstream (the header needs no CUDA include). */
+typedef struct CUstream_st* mllm_stream_t;
+
+typedef enum mllm_status {
+    MLLM_OK = 0,
+    MLLM_ERR_INVALID_ARGUMENT = 1, /* shape, stride, alignment or pointer rejected on the host */
+    MLLM_ERR_UNSUPPORTED = 2,      /* valid request this build does not implement (e.g. head_dim) */
+    MLLM_ERR_CUDA = 3,             /* a CUDA runtime / driver call failed */
+    MLLM_ERR_WORKSPACE = 4,        /* workspace missing or smaller than *_workspace_size() */
+    MLLM_ERR_NO_DEVICE = 5,        /* current device is not sm_100 */
+    MLLM_ERR_DEVICE_TIMEOUT = 6,   /* a kernel's bounded wait expired (see mllm_attn_device_status) */
+    MLLM_ERR_DEVICE_LENGTH = 7     /* a device-side length exceeded its host-given capacity */
+} mllm_status;
+
+/* Version of this ABI (bumped on any signature change). */
+MLLM_API int mllm_attn_abi_version(void);
+
+/* Static description of a status code. */
+MLLM_API const char* mllm_attn_status_string(int status);
+
+/* Detail message of the last failing call on this host thread ("" if none). */
+MLLM_API const char* mllm_attn_last_error(void);
+
+/* Reads and clears the device-side status word of the current device (synchronises
+ * `stream`).  Returns MLLM_OK, MLLM_ERR_DEVICE_TIMEOUT or MLLM_ERR_DEVICE_LENGTH. */
+MLLM_API int mllm_attn_device_status(mllm_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------
+ * RoPE table.  Replaces mllm::RoPE::BuildCosSin (src/core/runtime/RoPE.h:29-59):
+ *   inv_freq[j] = exp(-(2j / D) * ln(theta)),  angle = float(pos) * inv_freq[j],
+ *   cos/sin[s, j] = cos/sin[s, j + D/2] = cos/sin(angle)          all in fp32.
+ * positions: int64 [n]; cos_out / sin_out: fp32 [n, head_dim] (row-major). */
+MLLM_API int mllm_rope_build_cos_sin(const int64_t* positions, int64_t n, int head_dim, double rope_theta,
+                            float* cos_out, float* sin_out, mllm_stream_t stream);
+
+/* RoPE apply.  Replaces mllm::RoPE::Apply (src/core/runtime/RoPE.h:68-89) for bf16 input:
+ *   out = bf16(x*cos + cat(-x2, x1)*sin), each product and the sum rounded in fp32.
+ * x: bf16 [B, H, S, D] with element strides (x_stride_b, x_stride_h, x_stride_s);
+ * cos/sin: fp32 [S, D]; out: bf16 [B, H, S, D] contiguous. */
+MLLM_API int mllm_rope_apply_bf16(const void* x, int64_t x_stride_b, int64_t x_stride_h, int64_t x_stride_s,
+                         int batch, int num_heads, int seq_len, int head_dim, const float* cos,
+                         const float* sin, void* out, mllm_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------
+ * Fused QKV epilogue.  Replaces, in one kernel:
+ *   - the Qwen3 per-head RMSNorm of q and k   (src/core/runtime/TransformerBlock.h:103-107,
+ *     130-134 via RMSNorm::Forward, src/core/runtime/RMSNorm.h:27-64), when the norm weights
+ *     are given;
+ *   - RoPE on q and k                          (src/core/runtime/Attention.h:157-177);
+ *   - the KV-cache append                      (src/core/runtime/Attention.h:183-208): rows
+ *     are written in place instead of torch::cat-ing the whole cache.
+ *
+ * Inputs (token (b, s), head h, element d; all bf16, d contiguous):
+ *   q + b*q_sb + s*q_ss + h*q_sh      h < num_heads        (projected q, pre-norm)
+ *   k + b*k_sb + s*k_ss + h*k_sh      h < num_kv_heads
+ *   v + b*v_sb + s*v_ss + h*v_sh      h < num_kv_heads
+ * RoPE angle source, per token:
+ *   rope_cos/rope_sin != NULL: fp32 tables of row length head_dim (the BuildCosSin layout);
+ *       token (b, s) uses row  b*rope_row_sb + s*rope_row_ss;
+ *   else: computed in-kernel from positions[b*pos_sb + s*pos_ss] and rope_theta with the
+ *       same fp32 steps as mllm_rope_build_cos_sin (bit-identical to that table).
+ * q_norm_weight / k_norm_weight: bf16 [head_dim] (both given, or both NULL for Llama).
+ * Outputs:
+ *   q_out: bf16 [batch, num_heads, seq_len, head_dim] contiguous (post-norm, post-RoPE)
+ *   k_cache/v_cache row for (b, h, slot = cache_start[b] + s) at
+ *       cache + b*cache_sb + h*cache_sh + slot*cache_st
+ *   cache_start: int32 device [batch]; slots must lie below cache_capacity (checked on the
+ *       device: out-of-range rows are skipped and MLLM_ERR_DEVICE_LENGTH is recorded). */
+MLLM_API int mllm_qkv_epilogue_bf16(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh,
+                           const void* k, int64_t k_sb, int64_t k_ss, int64_t k_sh,
+                           const void* v, int64_t v_sb, int64_t v_ss, int64_t v_sh,
+                           int batch, int seq_len, int num_heads, int num_kv_heads, int head_dim,
+                           const int64_t* positions, int64_t pos_sb, int64_t pos_ss, double rope_theta,
+                           const float* rope_cos, const float* rope_sin, int64_t rope_row_sb,
+                           int64_t rope_row_ss,
+                           const void* q_norm_weight, const void* k_norm_weight, double rms_norm_eps,
+                           void* q_out,
+                           void* k_cache, void* v_cache, int64_t cache_sb, int64_t cache_sh,
+                           int64_t cache_st, int64_t cache_capacity, const int32_t* cache_start,
+                           mllm_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------
+ * Causal GQA prefill.  Replaces src/core/runtime/Attention.h:220-316 (repeat_interleave
+ * GQA expand, fp32 scores * scale, triu causal mask, fp32 softmax, bf16 P, P.V, merge heads)
+ * for q_len >= 1 new rows against kv_len >= q_len cached rows; query row s sits at absolute
+ * position kv_len - q_len + s and sees cache rows 0 .. kv_len - q_len + s.
+ *   q:   bf16 [batch, num_heads, q_len, head_dim] contiguous (mllm_qkv_epilogue_bf16 q_out)
+ *   k_cache/v_cache: row (b, kvh, t) at cache + b*cache_sb + kvh*cache_sh + t*cache_st;
+ *        strides multiples of 8 elements, base 16-byte aligned (TMA); at least kv_len rows.
+ *   out: bf16 [batch, q_len, num_heads*head_dim]  (the o_proj input layout)
+ * q head h reads kv head h / (num_heads / num_kv_heads).  head_dim 64 or 128. */
+MLLM_API int mllm_prefill_attention_bf16(const void* q, const void* k_cache, const void* v_cache,
+                                int64_t cache_sb, int64_t cache_sh, int64_t cache_st,
+                                int batch, int num_heads, int num_kv_heads, int head_dim,
+                                int q_len, int kv_len, float softmax_scale, void* out,
+                                mllm_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------
+ * Split-K flash-decode.  Replaces src/core/runtime/Attention.h:183-316 at S == 1 (the
+ * decode step of LlamaRunner.cpp:204-232 / QwenRunner.cpp:301-324), generalised to a
+ * per-sequence cache length (ragged batches).
+ *   q:      bf16 [batch, num_heads, head_dim] contiguous
+ *   caches: as for prefill; max_kv_len = rows addressable per (b, kv head)
+ *   kv_lens: int32 device [batch], the number of valid rows of each sequence (new token
+ *            included); values are clamped to [0, max_kv_len] on the device and an
+ *            out-of-range value records MLLM_ERR_DEVICE_LENGTH.
+ *   out:    bf16 [batch, num_heads*head_dim]
+ *   workspace: device scratch of at least mllm_decode_attention_workspace_size() bytes,
+ *            256-byte aligned; contents need not be initialised. */
+MLLM_API size_t mllm_decode_attention_workspace_size(int batch, int num_heads, int num_kv_heads, int head_dim,
+                                            int max_kv_len);
+
+MLLM_API int mllm_decode_attention_bf16(const void* q, const void* k_cache, const void* v_cache,
+                               int64_t cache_sb, int64_t cache_sh, int64_t cache_st,
+                               const int32_t* kv_lens, int batch, int num_heads, int num_kv_heads,
+                               int head_dim, int max_kv_len, float softmax_scale, void* out,
+                               void* workspace, size_t workspace_bytes, mllm_stream_t stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* MLLM_ATTN_H_ */

@@ -1,0 +1,95 @@
+"""Build the sm_100a attention library in-tree: mllm_b200/lib/libmllm_attn.so.
+
+    python -m mllm_b200.build [--force] [--verbose]
+
+Every .cu file under mllm_b200/csrc is compiled with nvcc for sm_100a (relocatable device
+code, so the device status word is shared across translation units) and linked into one
+shared library with the CUDA runtime linked statically.  The library exports only the
+extern "C" entry points declared in include/mllm_attn.h.
+"""
+from __future__ import annotations
+
+import argparse
+import glob
+import os
+import shutil
+import subprocess
+import sys
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+CSRC = os.path.join(PKG, "csrc")
+LIB_DIR = os.path.join(PKG, "lib")
+OBJ_DIR = os.path.join(PKG, "_build")
+LIB_NAME = "libmllm_attn.so"
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-rdc=true", "-Xcompiler", "-fPIC", "-Xcompiler",
+              "-fvisibility=hidden", "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def lib_path() -> str:
+    return os.path.join(LIB_DIR, LIB_NAME)
+
+
+def _sources():
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+
+
+def _deps():
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cuh")) +
+                  glob.glob(os.path.join(CSRC, "*.h")) + [os.path.join(ROOT, "include", "mllm_attn.h")])
+
+
+def up_to_date() -> bool:
+    out = lib_path()
+    if not os.path.exists(out):
+        return False
+    t = os.path.getmtime(out)
+    return all(os.path.getmtime(d) <= t for d in _deps())
+
+
+def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False) -> str:
+    out = lib_path()
+    if not force and up_to_date():
+        return out
+    os.makedirs(LIB_DIR, exist_ok=True)
+    os.makedirs(OBJ_DIR, exist_ok=True)
+    cc = nvcc()
+    objs = []
+    for src in _sources():
+        obj = os.path.join(OBJ_DIR, os.path.basename(src).replace(".cu", ".o"))
+        cmd = [cc, *ARCH, *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-c", src, "-o", obj]
+        if ptxas_verbose:
+            cmd += ["-Xptxas", "-v"]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        subprocess.run(cmd, check=True)
+        objs.append(obj)
+    tmp = out + ".tmp"
+    cmd = [cc, *ARCH, "-shared", "-rdc=true", "-cudart", "static", *objs, "-o", tmp,
+           "-Xcompiler", "-fPIC", "-Xlinker", "--exclude-libs,ALL"]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, out)
+    return out
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--ptxas-verbose", action="store_true")
+    a = ap.parse_args()
+    print(build(a.force, a.verbose, a.ptxas_verbose))
+
+
+if __name__ == "__main__":
+    main()

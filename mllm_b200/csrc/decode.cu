@@ -1,0 +1,469 @@
+// Split-K flash-decode over the bf16 KV cache (one new query token per sequence).
+//
+// Replaces src/core/runtime/Attention.h:183-316 at S == 1: instead of torch::cat-ing the
+// cache, repeat_interleave-ing it n_rep times and upcasting it to fp32, each KV-head row is
+// streamed from HBM exactly once and shared by its whole GQA group of query heads.
+//
+// Structure (per CTA, persistent over a static, strided list of work items):
+//   work item  = (sequence b, kv head g, chunk c of CH cache rows)
+//   warp 4     = producer: one elected lane issues TMA tile loads (64 rows x head_dim of K
+//                and of V, 128-byte swizzled) into an NSTAGE ring guarded by mbarriers
+//   warps 0-3  = consumers: each owns 16 of the 64 rows of every tile.
+//                S = Q K^T   with mma.sync m16n8k16 (A = the n_rep <= 8 query heads of the
+//                            group as MMA rows, B = K rows via ldmatrix), fp32 accumulate
+//                online softmax in registers (exp2 domain, running max / sum per head)
+//                O += P V    (A = P rounded to bf16, B = V via ldmatrix.trans)
+//   item end   : the four warps' (m, l, O) are merged through shared memory; a sequence
+//                covered by one chunk writes bf16 O / l directly, otherwise the chunk's
+//                unnormalised partial goes to the workspace and decode_combine_kernel
+//                merges the chunks.
+// The tensor-core MMAs only keep the instruction count far below the memory time: the
+// kernel is bound by HBM bandwidth (2 * head_dim * 2 bytes per cached row per kv head).
+//
+// Rows past a sequence's length inside its last tile are masked to -inf in S and zeroed in
+// the V tile (the cache beyond the length may hold any bit pattern).
+#include <algorithm>
+#include <cmath>
+
+#include "common.cuh"
+#include "host_util.h"
+
+namespace mllm_b200 {
+namespace {
+
+constexpr int kTile = 64;         // cache rows per pipeline stage
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kMaxGroup = 8;      // query heads per kv head handled as MMA rows
+constexpr int kBoxBytes = kTile * 128;  // one 64-row x 64-column bf16 TMA box
+
+template <int D>
+struct DecodeCfg {
+    static constexpr int kBoxes = D / 64;                 // TMA boxes per tile row-block
+    static constexpr int kTileBytes = kTile * D * 2;      // K (or V) bytes per stage
+    static constexpr int kStages = (D == 128) ? 3 : 6;
+    static constexpr int kStageBytes = 2 * kTileBytes;
+    static constexpr int kRedFloats = (kConsumerWarps - 1) * kMaxGroup * D;
+    static constexpr int kSmemBytes =
+        kStages * kStageBytes + kRedFloats * 4 + 2 * kConsumerWarps * kMaxGroup * 4 + 2 * kStages * 8 + 1024;
+};
+
+struct DecodeArgs {
+    const __nv_bfloat16* q;     // [B, H, D]
+    const int32_t* kv_lens;     // [B]
+    __nv_bfloat16* out;         // [B, H*D]
+    float* part_o;              // [B*Hkv*nch, n_rep, D]
+    float* part_ml;             // [B*Hkv*nch, n_rep, 2]
+    int B, H, Hkv, n_rep, max_len, chunk, nch, items;
+    float scale_log2;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 2)
+    decode_split_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                        DecodeArgs a) {
+    using Cfg = DecodeCfg<D>;
+    constexpr int NS = Cfg::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float* red_o = reinterpret_cast<float*>(smem + NS * Cfg::kStageBytes);
+    float* red_m = red_o + Cfg::kRedFloats;
+    float* red_l = red_m + kConsumerWarps * kMaxGroup;
+    uint64_t* full = reinterpret_cast<uint64_t*>(red_l + kConsumerWarps * kMaxGroup);
+    uint64_t* empty = full + NS;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    auto item_range = [&](int item, int& b, int& g, int& c, int& t0, int& t1, int& L) {
+        c = item % a.nch;
+        const int bg = item / a.nch;
+        g = bg % a.Hkv;
+        b = bg / a.Hkv;
+        int len = a.kv_lens[b];
+        if (len < 0 || len > a.max_len) {
+            if (threadIdx.x == 0 && c == 0 && g == 0) record_error(kErrBadLength);
+            len = len < 0 ? 0 : a.max_len;
+        }
+        L = len;
+        t0 = c * a.chunk;
+        t1 = min(t0 + a.chunk, L);
+    };
+
+    if (warp == kConsumerWarps) {
+        // ------------------------------ producer ------------------------------
+        if (lane == 0) {
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool alive = true;
+            for (int item = blockIdx.x; item < a.items && alive; item += gridDim.x) {
+                int b, g, c, t0, t1, L;
+                item_range(item, b, g, c, t0, t1, L);
+                for (int t = t0; t < t1; t += kTile) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1)) { alive = false; break; }
+                    mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+                    uint8_t* kdst = smem + stage * Cfg::kStageBytes;
+                    uint8_t* vdst = kdst + Cfg::kTileBytes;
+#pragma unroll
+                    for (int bx = 0; bx < Cfg::kBoxes; ++bx) {
+                        tma_load_4d(kdst + bx * kBoxBytes, &tmK, &full[stage], bx * 64, t, g, b);
+                        tma_load_4d(vdst + bx * kBoxBytes, &tmV, &full[stage], bx * 64, t, g, b);
+                    }
+                    if (++stage == NS) { stage = 0; phase ^= 1; }
+                }
+            }
+        }
+        return;
+    }
+
+    // -------------------------------- consumers --------------------------------
+    const int grp = lane >> 2;   // MMA row = query head within the group
+    const int tig = lane & 3;    // thread in group
+    int stage = 0;
+    uint32_t phase = 0;
+    constexpr int KS = D / 16;   // k-steps of S = Q K^T
+    constexpr int NB = D / 8;    // n-blocks of O
+    bool alive = true;
+
+    for (int item = blockIdx.x; item < a.items && alive; item += gridDim.x) {
+        int b, g, c, t0, t1, L;
+        item_range(item, b, g, c, t0, t1, L);
+        const int nch_b = (L + a.chunk - 1) / a.chunk;
+        if (t1 <= t0) {
+            if (L == 0 && c == 0) {  // empty sequence: the reference would produce no row; emit zeros
+                for (int i = threadIdx.x; i < a.n_rep * D; i += kConsumerWarps * 32)
+                    a.out[(int64_t)b * a.H * D + (int64_t)g * a.n_rep * D + i] = __float2bfloat16_rn(0.f);
+            }
+            continue;
+        }
+        const bool row_ok = grp < a.n_rep;
+
+        // Q fragments (A operand): rows = heads of the group, cols = head_dim.
+        uint32_t qa[KS][2];
+        {
+            const __nv_bfloat16* qrow = a.q + ((int64_t)b * a.H + (int64_t)g * a.n_rep + (row_ok ? grp : 0)) * D;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                const uint32_t lo = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + tig * 2);
+                const uint32_t hi = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + tig * 2 + 8);
+                qa[ks][0] = row_ok ? lo : 0u;
+                qa[ks][1] = row_ok ? hi : 0u;
+            }
+        }
+        float o[NB][4];
+#pragma unroll
+        for (int j = 0; j < NB; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+        float m_run = -INFINITY, l_run = 0.f;
+
+        for (int t = t0; t < t1; t += kTile) {
+            if (!mbar_wait(&full[stage], phase)) { alive = false; break; }
+            uint8_t* kst = smem + stage * Cfg::kStageBytes;
+            uint8_t* vst = kst + Cfg::kTileBytes;
+            const uint32_t kbase = smem_u32(kst);
+            const uint32_t vbase = smem_u32(vst);
+            const int row0 = warp * 16;  // this warp's rows within the tile
+
+            // ---- S = Q K^T over this warp's 16 rows (two n-blocks of 8 rows) ----
+            float sacc[2][4];
+#pragma unroll
+            for (int nb = 0; nb < 2; ++nb) sacc[nb][0] = sacc[nb][1] = sacc[nb][2] = sacc[nb][3] = 0.f;
+            {
+                const int mi = lane >> 3, ri = lane & 7;
+                const int row = row0 + 8 * (mi >> 1) + ri;
+#pragma unroll
+                for (int ks = 0; ks < KS; ++ks) {
+                    const int cc = 2 * ks + (mi & 1);       // 16-byte chunk along head_dim
+                    const uint32_t addr = kbase + (cc >> 3) * kBoxBytes + swz128(row, cc & 7);
+                    uint32_t r0, r1, r2, r3;
+                    ldsm_x4(addr, r0, r1, r2, r3);
+                    mma_bf16_16816(sacc[0], qa[ks][0], 0u, qa[ks][1], 0u, r0, r1);
+                    mma_bf16_16816(sacc[1], qa[ks][0], 0u, qa[ks][1], 0u, r2, r3);
+                }
+            }
+
+            // ---- mask, online softmax (rows = heads; this thread: head grp, 4 rows) ----
+            const int valid_rows = t1 - t;  // rows of this tile inside the sequence chunk
+            float s[4];
+            float mt = -INFINITY;
+#pragma unroll
+            for (int nb = 0; nb < 2; ++nb) {
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int r = row0 + nb * 8 + tig * 2 + e;
+                    const float v = (r < valid_rows) ? sacc[nb][e] * a.scale_log2 : -INFINITY;
+                    s[nb * 2 + e] = v;
+                    mt = fmaxf(mt, v);
+                }
+            }
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+            const float m_new = fmaxf(m_run, mt);
+            const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+            const float alpha = ex2_approx(m_run - m_use);
+            float p[4];
+            float psum = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                p[i] = ex2_approx(s[i] - m_use);
+                psum += p[i];
+            }
+            l_run = l_run * alpha + psum;
+            m_run = m_new;
+#pragma unroll
+            for (int j = 0; j < NB; ++j) {
+                o[j][0] *= alpha;
+                o[j][1] *= alpha;
+            }
+            const uint32_t pa0 = pack_bf16x2(p[0], p[1]);
+            const uint32_t pa2 = pack_bf16x2(p[2], p[3]);
+
+            // ---- rows past the sequence end: zero this warp's V rows (any bit pattern may sit there)
+            if (valid_rows < row0 + 16) {
+                for (int i = lane; i < 16 * (D / 8); i += 32) {
+                    const int r = row0 + i / (D / 8);
+                    const int cc = i % (D / 8);
+                    if (r >= valid_rows)
+                        *reinterpret_cast<uint4*>(vst + (cc >> 3) * kBoxBytes + r * 128 + (cc & 7) * 16) =
+                            make_uint4(0u, 0u, 0u, 0u);
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+            }
+
+            // ---- O += P V ----
+            {
+                const int mi = lane >> 3, ri = lane & 7;
+                const int row = row0 + 8 * (mi & 1) + ri;
+#pragma unroll
+                for (int j = 0; j < NB; j += 2) {
+                    const int cc = j + (mi >> 1);           // 8-column block of head_dim
+                    const uint32_t addr = vbase + (cc >> 3) * kBoxBytes + swz128(row, cc & 7);
+                    uint32_t r0, r1, r2, r3;
+                    ldsm_x4_trans(addr, r0, r1, r2, r3);
+                    mma_bf16_16816(o[j], pa0, 0u, pa2, 0u, r0, r1);
+                    mma_bf16_16816(o[j + 1], pa0, 0u, pa2, 0u, r2, r3);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[stage]);
+            if (++stage == NS) { stage = 0; phase ^= 1; }
+        }
+        if (!alive) break;
+
+        // ---- merge the four warps' states for this item ----
+        l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+        l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+        if (warp > 0 && row_ok) {
+            float* dst = red_o + ((warp - 1) * kMaxGroup + grp) * D;
+#pragma unroll
+            for (int j = 0; j < NB; ++j)
+                *reinterpret_cast<float2*>(dst + j * 8 + tig * 2) = make_float2(o[j][0], o[j][1]);
+            if (tig == 0) {
+                red_m[warp * kMaxGroup + grp] = m_run;
+                red_l[warp * kMaxGroup + grp] = l_run;
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+        if (warp == 0 && row_ok) {
+            float M = m_run;
+#pragma unroll
+            for (int w = 1; w < kConsumerWarps; ++w) M = fmaxf(M, red_m[w * kMaxGroup + grp]);
+            const float Mu = (M == -INFINITY) ? 0.f : M;
+            float sc[kConsumerWarps];
+            sc[0] = ex2_approx(m_run - Mu);
+            float Ltot = l_run * sc[0];
+#pragma unroll
+            for (int w = 1; w < kConsumerWarps; ++w) {
+                sc[w] = ex2_approx(red_m[w * kMaxGroup + grp] - Mu);
+                Ltot += red_l[w * kMaxGroup + grp] * sc[w];
+            }
+            const int head = g * a.n_rep + grp;
+            if (nch_b == 1) {
+                const float inv = (Ltot > 0.f) ? 1.f / Ltot : 0.f;
+                __nv_bfloat16* orow = a.out + ((int64_t)b * a.H + head) * D;
+#pragma unroll
+                for (int j = 0; j < NB; ++j) {
+                    float x0 = o[j][0] * sc[0], x1 = o[j][1] * sc[0];
+#pragma unroll
+                    for (int w = 1; w < kConsumerWarps; ++w) {
+                        const float2 r = *reinterpret_cast<const float2*>(red_o + ((w - 1) * kMaxGroup + grp) * D +
+                                                                          j * 8 + tig * 2);
+                        x0 += r.x * sc[w];
+                        x1 += r.y * sc[w];
+                    }
+                    *reinterpret_cast<uint32_t*>(orow + j * 8 + tig * 2) = pack_bf16x2(x0 * inv, x1 * inv);
+                }
+            } else {
+                const int64_t pidx = (int64_t)item * a.n_rep + grp;
+                float* prow = a.part_o + pidx * D;
+#pragma unroll
+                for (int j = 0; j < NB; ++j) {
+                    float x0 = o[j][0] * sc[0], x1 = o[j][1] * sc[0];
+#pragma unroll
+                    for (int w = 1; w < kConsumerWarps; ++w) {
+                        const float2 r = *reinterpret_cast<const float2*>(red_o + ((w - 1) * kMaxGroup + grp) * D +
+                                                                          j * 8 + tig * 2);
+                        x0 += r.x * sc[w];
+                        x1 += r.y * sc[w];
+                    }
+                    *reinterpret_cast<float2*>(prow + j * 8 + tig * 2) = make_float2(x0, x1);
+                }
+                if (tig == 0) {
+                    a.part_ml[pidx * 2 + 0] = M;
+                    a.part_ml[pidx * 2 + 1] = Ltot;
+                }
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+    }
+}
+
+// Merges the per-chunk partials of every (sequence, query head) whose cache spans more
+// than one chunk.  One CTA per (kv head, sequence); thread d owns column d.
+template <int D>
+__global__ void __launch_bounds__(128) decode_combine_kernel(DecodeArgs a) {
+    const int g = blockIdx.x, b = blockIdx.y;
+    int L = a.kv_lens[b];
+    L = L < 0 ? 0 : (L > a.max_len ? a.max_len : L);
+    const int nch_b = (L + a.chunk - 1) / a.chunk;
+    if (nch_b <= 1) return;  // written directly by the split kernel
+    const int d = threadIdx.x;
+    if (d >= D) return;
+    const int64_t item0 = ((int64_t)b * a.Hkv + g) * a.nch;
+    for (int r = 0; r < a.n_rep; ++r) {
+        float M = -INFINITY;
+        for (int c = 0; c < nch_b; ++c) M = fmaxf(M, a.part_ml[((item0 + c) * a.n_rep + r) * 2]);
+        const float Mu = (M == -INFINITY) ? 0.f : M;
+        float Lt = 0.f, acc = 0.f;
+        for (int c = 0; c < nch_b; ++c) {
+            const int64_t pidx = (item0 + c) * a.n_rep + r;
+            const float sc = ex2_approx(a.part_ml[pidx * 2] - Mu);
+            Lt += a.part_ml[pidx * 2 + 1] * sc;
+            acc += a.part_o[pidx * D + d] * sc;
+        }
+        const float res = (Lt > 0.f) ? acc / Lt : 0.f;
+        a.out[((int64_t)b * a.H + (int64_t)g * a.n_rep + r) * D + d] = __float2bfloat16_rn(res);
+    }
+}
+
+// Chunking of the cache rows into work items: aim for ~16 items per SM so the persistent
+// grid stays balanced, with chunks of at least 256 rows (amortises the per-item merge).
+constexpr int kMinChunk = 256;
+
+int max_chunks(int max_len) { return std::max(1, (max_len + kMinChunk - 1) / kMinChunk); }
+
+void plan_chunks(int B, int Hkv, int max_len, int num_sms, int& chunk, int& nch) {
+    const int64_t pairs = (int64_t)B * Hkv;
+    int64_t want = (16LL * num_sms + pairs - 1) / pairs;
+    want = std::max<int64_t>(1, std::min<int64_t>(want, max_chunks(max_len)));
+    int64_t ch = (max_len + want - 1) / want;
+    ch = ((ch + kTile - 1) / kTile) * kTile;
+    chunk = (int)std::max<int64_t>(ch, kTile);
+    nch = (max_len + chunk - 1) / chunk;
+}
+
+size_t workspace_bytes_for(int B, int H, int Hkv, int D, int max_len) {
+    const int n_rep = H / Hkv;
+    const size_t parts = (size_t)B * Hkv * max_chunks(max_len) * n_rep;
+    const size_t bytes = parts * D * 4 + parts * 2 * 4;
+    return (bytes + 255) & ~size_t(255);
+}
+
+}  // namespace
+}  // namespace mllm_b200
+
+using namespace mllm_b200;
+
+extern "C" size_t mllm_decode_attention_workspace_size(int batch, int num_heads, int num_kv_heads, int head_dim,
+                                                       int max_kv_len) {
+    if (batch <= 0 || num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads || max_kv_len <= 0 ||
+        head_dim <= 0)
+        return 0;
+    return workspace_bytes_for(batch, num_heads, num_kv_heads, head_dim, max_kv_len);
+}
+
+extern "C" int mllm_decode_attention_bf16(const void* q, const void* k_cache, const void* v_cache,
+                                          int64_t cache_sb, int64_t cache_sh, int64_t cache_st,
+                                          const int32_t* kv_lens, int batch, int num_heads, int num_kv_heads,
+                                          int head_dim, int max_kv_len, float softmax_scale, void* out,
+                                          void* workspace, size_t workspace_bytes, mllm_stream_t stream) {
+    if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_kv_len <= 0)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention: bad sizes");
+    if (num_heads % num_kv_heads != 0)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "Attention: num_heads must be divisible by num_kv_heads.");
+    if (head_dim != 64 && head_dim != 128)
+        return fail(MLLM_ERR_UNSUPPORTED, "decode_attention: head_dim must be 64 or 128");
+    const int n_rep = num_heads / num_kv_heads;
+    if (n_rep > kMaxGroup) return fail(MLLM_ERR_UNSUPPORTED, "decode_attention: GQA group larger than 8");
+    if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale))
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention: softmax_scale must be positive");
+    if (batch == 0) return ok();
+    if (!q || !k_cache || !v_cache || !kv_lens || !out)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention: null pointer");
+    if (!aligned(q, 4) || !aligned(out, 4)) return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention: q/out misaligned");
+    const size_t need = workspace_bytes_for(batch, num_heads, num_kv_heads, head_dim, max_kv_len);
+    if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+        return fail(MLLM_ERR_WORKSPACE, "decode_attention: workspace missing, misaligned or smaller than "
+                                        "mllm_decode_attention_workspace_size()");
+    int num_sms = 0;
+    if (int st = require_sm100(&num_sms)) return st;
+
+    CUtensorMap tmK, tmV;
+    if (int st = encode_kv_map(&tmK, k_cache, head_dim, max_kv_len, num_kv_heads, batch, cache_st, cache_sh, cache_sb,
+                               64, kTile))
+        return st;
+    if (int st = encode_kv_map(&tmV, v_cache, head_dim, max_kv_len, num_kv_heads, batch, cache_st, cache_sh, cache_sb,
+                               64, kTile))
+        return st;
+
+    DecodeArgs a;
+    a.q = (const __nv_bfloat16*)q;
+    a.kv_lens = kv_lens;
+    a.out = (__nv_bfloat16*)out;
+    a.B = batch;
+    a.H = num_heads;
+    a.Hkv = num_kv_heads;
+    a.n_rep = n_rep;
+    a.max_len = max_kv_len;
+    plan_chunks(batch, num_kv_heads, max_kv_len, num_sms, a.chunk, a.nch);
+    const size_t parts = (size_t)batch * num_kv_heads * a.nch * n_rep;
+    a.part_o = reinterpret_cast<float*>(workspace);
+    a.part_ml = a.part_o + parts * head_dim;
+    a.items = batch * num_kv_heads * a.nch;
+    a.scale_log2 = (float)((double)softmax_scale * 1.4426950408889634);
+
+    const int grid = std::min(a.items, 2 * num_sms);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (head_dim == 128) {
+        auto kern = decode_split_kernel<128>;
+        const int smem = DecodeCfg<128>::kSmemBytes;
+        if (int st = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                                "decode smem attribute"))
+            return st;
+        kern<<<grid, kThreads, smem, s>>>(tmK, tmV, a);
+        if (int st = check_cuda(cudaGetLastError(), "decode_split_kernel launch")) return st;
+        if (a.nch > 1) decode_combine_kernel<128><<<dim3(num_kv_heads, batch), 128, 0, s>>>(a);
+    } else {
+        auto kern = decode_split_kernel<64>;
+        const int smem = DecodeCfg<64>::kSmemBytes;
+        if (int st = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                                "decode smem attribute"))
+            return st;
+        kern<<<grid, kThreads, smem, s>>>(tmK, tmV, a);
+        if (int st = check_cuda(cudaGetLastError(), "decode_split_kernel launch")) return st;
+        if (a.nch > 1) decode_combine_kernel<64><<<dim3(num_kv_heads, batch), 128, 0, s>>>(a);
+    }
+    if (int st = check_cuda(cudaGetLastError(), "decode_combine_kernel launch")) return st;
+    return ok();
+}

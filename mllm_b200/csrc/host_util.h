@@ -1,0 +1,34 @@
+// Host-side helpers shared by the C-ABI entry points: error reporting, device checks and
+// TMA tensor-map encoding.  Nothing here throws across the C boundary.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/mllm_attn.h"
+
+namespace mllm_b200 {
+
+// Records `msg` as this thread's last error and returns `status`.
+int fail(int status, const std::string& msg);
+// Clears the thread's last error and returns MLLM_OK.
+int ok();
+
+// Checks a CUDA runtime result; on failure records it and returns MLLM_ERR_CUDA.
+int check_cuda(cudaError_t e, const char* what);
+
+// Returns MLLM_OK if the current device is sm_100 (B200 class), else a failure status.
+int require_sm100(int* num_sms = nullptr);
+
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Encodes a 4-D bf16 tensor map {d (inner), rows, heads, batch} with 128-byte swizzle and a
+// {box_d, box_rows, 1, 1} box.  Strides are in elements.  Returns MLLM_OK or an error.
+int encode_kv_map(CUtensorMap* map, const void* base, int64_t d, int64_t rows, int64_t heads, int64_t batch,
+                  int64_t stride_row, int64_t stride_head, int64_t stride_batch, uint32_t box_d,
+                  uint32_t box_rows);
+
+}  // namespace mllm_b200

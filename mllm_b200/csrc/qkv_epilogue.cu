@@ -1,0 +1,238 @@
+// Fused QKV epilogue: per-head RMSNorm (Qwen3) + RoPE + KV-cache append, one kernel.
+//
+// Replaces, for each token (b, s):
+//   TransformerBlock.h:103-107,130-134  q/k per-head RMSNorm (RMSNorm.h:27-64), fp32, cast bf16
+//   Attention.h:157-177                 RoPE on q and k (RoPE.h:68-89), fp32, cast bf16
+//   Attention.h:183-208                 KV append -- rows written in place (no torch::cat)
+//
+// Work split: one warp per (token, head).  Lane L holds the elements d = L + 32*i
+// (i < D/32).  That layout gives two things at once:
+//   * RMSNorm's fp32 sum of squares in exactly the reference CPU LibTorch order
+//     (8-wide vectors with 4 interleaved accumulators: lane L = 8k + j holds accumulator
+//     P_k[j]; then ((P0+P1)+P2)+P3 per j, then j = 0..7 in sequence), so the bf16 result is
+//     bit-identical to the reference;
+//   * both halves of every RoPE pair (d, d + D/2) in the same lane: no shuffles.
+// Every fp32 step uses explicit round-to-nearest intrinsics so no FMA contraction occurs.
+//
+// Memory: each head row is read once (D*2 bytes) and written once (q_out or the cache row).
+#include "common.cuh"
+#include "host_util.h"
+#include "rope_math.cuh"
+
+namespace mllm_b200 {
+namespace {
+
+struct EpilogueArgs {
+    const __nv_bfloat16* q;
+    const __nv_bfloat16* k;
+    const __nv_bfloat16* v;
+    int64_t q_sb, q_ss, q_sh, k_sb, k_ss, k_sh, v_sb, v_ss, v_sh;
+    int B, S, H, Hkv;
+    const int64_t* positions;
+    int64_t pos_sb, pos_ss;
+    float log_theta;
+    const float* rope_cos;
+    const float* rope_sin;
+    int64_t rope_row_sb, rope_row_ss;
+    const __nv_bfloat16* q_gamma;
+    const __nv_bfloat16* k_gamma;
+    float eps;
+    __nv_bfloat16* q_out;
+    __nv_bfloat16* k_cache;
+    __nv_bfloat16* v_cache;
+    int64_t c_sb, c_sh, c_st, capacity;
+    const int32_t* cache_start;
+};
+
+constexpr int kWarps = 8;
+
+// Sum of squares of a head row in the reference's reduction order (see file comment).
+template <int NI>
+__device__ __forceinline__ float row_sum_squares(const float (&x)[NI], int lane) {
+    float p = 0.f;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) p = __fadd_rn(p, __fmul_rn(x[i], x[i]));
+    const int j = lane & 7;
+    const float p0 = __shfl_sync(0xffffffffu, p, j);
+    const float p1 = __shfl_sync(0xffffffffu, p, j + 8);
+    const float p2 = __shfl_sync(0xffffffffu, p, j + 16);
+    const float p3 = __shfl_sync(0xffffffffu, p, j + 24);
+    const float acc = __fadd_rn(__fadd_rn(__fadd_rn(p0, p1), p2), p3);
+    float total = 0.f;
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) total = __fadd_rn(total, __shfl_sync(0xffffffffu, acc, jj));
+    return total;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kWarps * 32) qkv_epilogue_kernel(EpilogueArgs a) {
+    constexpr int NI = D / 32;     // elements per lane
+    constexpr int HALF = D / 2;
+    constexpr int PAIR = NI / 2;   // slot i pairs with slot i + PAIR (distance D/2)
+    __shared__ float s_cos[D];
+    __shared__ float s_sin[D];
+
+    const int token = blockIdx.x;
+    const int b = token / a.S;
+    const int s = token - b * a.S;
+    const int tid = threadIdx.x;
+
+    // Angles for this token: from the caller's table, or computed (bit-identical to the
+    // table that mllm_rope_build_cos_sin would produce for the same position).
+    if (a.rope_cos != nullptr) {
+        const int64_t row = (int64_t)b * a.rope_row_sb + (int64_t)s * a.rope_row_ss;
+        for (int d = tid; d < D; d += blockDim.x) {
+            s_cos[d] = a.rope_cos[row * D + d];
+            s_sin[d] = a.rope_sin[row * D + d];
+        }
+    } else {
+        const int64_t pos = a.positions[(int64_t)b * a.pos_sb + (int64_t)s * a.pos_ss];
+        for (int j = tid; j < HALF; j += blockDim.x) {
+            float c, sn;
+            rope_angle_cos_sin(pos, j, D, a.log_theta, c, sn);
+            s_cos[j] = c;
+            s_cos[j + HALF] = c;
+            s_sin[j] = sn;
+            s_sin[j + HALF] = sn;
+        }
+    }
+    __syncthreads();
+
+    const int lane = tid & 31;
+    const int head = blockIdx.y * kWarps + (tid >> 5);
+    const int total_heads = a.H + 2 * a.Hkv;
+    if (head >= total_heads) return;
+
+    const __nv_bfloat16* src;
+    const __nv_bfloat16* gamma = nullptr;
+    int kind;  // 0 = q, 1 = k, 2 = v
+    int h;
+    if (head < a.H) {
+        kind = 0;
+        h = head;
+        src = a.q + b * a.q_sb + s * a.q_ss + h * a.q_sh;
+        gamma = a.q_gamma;
+    } else if (head < a.H + a.Hkv) {
+        kind = 1;
+        h = head - a.H;
+        src = a.k + b * a.k_sb + s * a.k_ss + h * a.k_sh;
+        gamma = a.k_gamma;
+    } else {
+        kind = 2;
+        h = head - a.H - a.Hkv;
+        src = a.v + b * a.v_sb + s * a.v_ss + h * a.v_sh;
+    }
+
+    float x[NI];
+#pragma unroll
+    for (int i = 0; i < NI; ++i) x[i] = __bfloat162float(src[lane + 32 * i]);
+
+    __nv_bfloat16 y[NI];
+    if (kind == 2) {
+#pragma unroll
+        for (int i = 0; i < NI; ++i) y[i] = src[lane + 32 * i];
+    } else {
+        if (gamma != nullptr) {
+            // RMSNorm.h:48-63: var = mean(x^2); x * rsqrt(var + eps) * w; cast to bf16.
+            const float var = __fdiv_rn(row_sum_squares<NI>(x, lane), (float)D);
+            const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));
+#pragma unroll
+            for (int i = 0; i < NI; ++i) {
+                const float w = __bfloat162float(gamma[lane + 32 * i]);
+                x[i] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[i], r), w)));
+            }
+        }
+        // RoPE.h:77-88 on the pairs (d, d + D/2).
+#pragma unroll
+        for (int i = 0; i < PAIR; ++i) {
+            const int j = lane + 32 * i;
+            float lo, hi;
+            rope_rotate_pair(x[i], x[i + PAIR], s_cos[j], s_sin[j], s_cos[j + HALF], s_sin[j + HALF], lo, hi);
+            y[i] = __float2bfloat16_rn(lo);
+            y[i + PAIR] = __float2bfloat16_rn(hi);
+        }
+    }
+
+    __nv_bfloat16* dst;
+    if (kind == 0) {
+        dst = a.q_out + (((int64_t)b * a.H + h) * a.S + s) * D;
+    } else {
+        const int64_t slot = (int64_t)a.cache_start[b] + s;
+        if (slot < 0 || slot >= a.capacity) {
+            if (lane == 0) record_error(kErrBadLength);
+            return;
+        }
+        __nv_bfloat16* base = (kind == 1) ? a.k_cache : a.v_cache;
+        dst = base + b * a.c_sb + h * a.c_sh + slot * a.c_st;
+    }
+#pragma unroll
+    for (int i = 0; i < NI; ++i) dst[lane + 32 * i] = y[i];
+}
+
+}  // namespace
+}  // namespace mllm_b200
+
+using namespace mllm_b200;
+
+extern "C" int mllm_qkv_epilogue_bf16(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh,
+                                      const void* k, int64_t k_sb, int64_t k_ss, int64_t k_sh,
+                                      const void* v, int64_t v_sb, int64_t v_ss, int64_t v_sh,
+                                      int batch, int seq_len, int num_heads, int num_kv_heads, int head_dim,
+                                      const int64_t* positions, int64_t pos_sb, int64_t pos_ss, double rope_theta,
+                                      const float* rope_cos, const float* rope_sin, int64_t rope_row_sb,
+                                      int64_t rope_row_ss, const void* q_norm_weight, const void* k_norm_weight,
+                                      double rms_norm_eps, void* q_out, void* k_cache, void* v_cache,
+                                      int64_t cache_sb, int64_t cache_sh, int64_t cache_st, int64_t cache_capacity,
+                                      const int32_t* cache_start, mllm_stream_t stream) {
+    if (batch < 0 || seq_len < 0 || num_heads <= 0 || num_kv_heads <= 0)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "qkv_epilogue: bad sizes");
+    if (num_heads % num_kv_heads != 0)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "Attention: num_heads must be divisible by num_kv_heads.");
+    if (head_dim != 64 && head_dim != 128)
+        return fail(MLLM_ERR_UNSUPPORTED, "qkv_epilogue: head_dim must be 64 or 128");
+    if ((q_norm_weight == nullptr) != (k_norm_weight == nullptr))
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "qkv_epilogue: give both q/k norm weights or neither");
+    if ((rope_cos == nullptr) != (rope_sin == nullptr))
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "qkv_epilogue: give both rope tables or neither");
+    if (rope_cos == nullptr && positions == nullptr)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "qkv_epilogue: positions or rope tables required");
+    if (rope_cos == nullptr && !(rope_theta > 0.0))
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "qkv_epilogue: rope_theta must be positive");
+    if (batch == 0 || seq_len == 0) return ok();
+    if (!q || !k || !v || !q_out || !k_cache || !v_cache || !cache_start)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "qkv_epilogue: null pointer");
+    if (cache_capacity <= 0) return fail(MLLM_ERR_INVALID_ARGUMENT, "qkv_epilogue: cache_capacity must be > 0");
+    if ((int64_t)batch * seq_len > 0x7fffffffLL) return fail(MLLM_ERR_INVALID_ARGUMENT, "qkv_epilogue: too many tokens");
+    if (int st = require_sm100()) return st;
+
+    EpilogueArgs a;
+    a.q = (const __nv_bfloat16*)q;
+    a.k = (const __nv_bfloat16*)k;
+    a.v = (const __nv_bfloat16*)v;
+    a.q_sb = q_sb; a.q_ss = q_ss; a.q_sh = q_sh;
+    a.k_sb = k_sb; a.k_ss = k_ss; a.k_sh = k_sh;
+    a.v_sb = v_sb; a.v_ss = v_ss; a.v_sh = v_sh;
+    a.B = batch; a.S = seq_len; a.H = num_heads; a.Hkv = num_kv_heads;
+    a.positions = positions; a.pos_sb = pos_sb; a.pos_ss = pos_ss;
+    a.log_theta = rope_cos ? 0.f : rope_log_theta(rope_theta);
+    a.rope_cos = rope_cos; a.rope_sin = rope_sin;
+    a.rope_row_sb = rope_row_sb; a.rope_row_ss = rope_row_ss;
+    a.q_gamma = (const __nv_bfloat16*)q_norm_weight;
+    a.k_gamma = (const __nv_bfloat16*)k_norm_weight;
+    a.eps = (float)rms_norm_eps;  // the reference adds the double eps to a float tensor
+    a.q_out = (__nv_bfloat16*)q_out;
+    a.k_cache = (__nv_bfloat16*)k_cache;
+    a.v_cache = (__nv_bfloat16*)v_cache;
+    a.c_sb = cache_sb; a.c_sh = cache_sh; a.c_st = cache_st; a.capacity = cache_capacity;
+    a.cache_start = cache_start;
+
+    const int total_heads = num_heads + 2 * num_kv_heads;
+    dim3 grid((unsigned)(batch * seq_len), (unsigned)((total_heads + kWarps - 1) / kWarps));
+    if (grid.y > 65535) return fail(MLLM_ERR_UNSUPPORTED, "qkv_epilogue: too many heads");
+    if (head_dim == 128)
+        qkv_epilogue_kernel<128><<<grid, kWarps * 32, 0, (cudaStream_t)stream>>>(a);
+    else
+        qkv_epilogue_kernel<64><<<grid, kWarps * 32, 0, (cudaStream_t)stream>>>(a);
+    if (int st = check_cuda(cudaGetLastError(), "qkv_epilogue launch")) return st;
+    return ok();
+}

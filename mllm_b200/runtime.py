@@ -1,0 +1,277 @@
+"""Python mirror of mLLM's stateless runtime API for the attention path, on the B200 kernels.
+
+Same names, argument meaning and error behaviour as the reference's C++ classes
+(src/core/runtime/{KVCache,RoPE,Attention,TransformerBlock}.h); every device computation goes
+through the C ABI of libmllm_attn.so (include/mllm_attn.h).  Projections (Linear) stay torch
+GEMMs, exactly as the reference keeps them in LibTorch.  There is no CPU path: CUDA bf16
+tensors are required and anything else raises RuntimeError, like the reference's checks.
+
+  KVCache                 src/core/runtime/KVCache.h:9-28  -- preallocated bf16 rows instead of
+                          a tensor grown by torch::cat; .key/.value are views of the valid rows
+  RoPE.build_cos_sin      src/core/runtime/RoPE.h:29-59
+  RoPE.apply              src/core/runtime/RoPE.h:68-89
+  Attention.forward       src/core/runtime/Attention.h:29-86
+  Attention.forward_projected  src/core/runtime/Attention.h:100-326 (+ optional fused QK-norm,
+                          which the reference does in TransformerBlock.h:103-134)
+  attention_block         the attention half of TransformerBlock::Forward (h -> attention out)
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import abi
+
+BF16 = torch.bfloat16
+
+
+def _check_cuda_bf16(name: str, t: torch.Tensor) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name}: the B200 attention path needs CUDA tensors (no CPU fallback)")
+    if t.dtype != BF16:
+        raise RuntimeError(f"{name}: expected bfloat16, got {t.dtype}")
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+class KVCache:
+    """Per-layer KV cache: bf16 rows [batch, num_kv_heads, capacity, head_dim] written in place.
+
+    Mirrors KVCache.h:9-28: `key`/`value` are the valid rows [B, Hkv, L, D] (views), so callers
+    that read `key.size(2)` (the runners' decode position, QwenRunner.cpp:301-310) see the
+    cache length.  `lengths` holds per-sequence lengths for ragged batches."""
+
+    def __init__(self, batch: int, num_kv_heads: int, head_dim: int, capacity: int,
+                 device="cuda", zero: bool = True):
+        alloc = torch.zeros if zero else torch.empty
+        self.key_buf = alloc((batch, num_kv_heads, capacity, head_dim), dtype=BF16, device=device)
+        self.value_buf = alloc((batch, num_kv_heads, capacity, head_dim), dtype=BF16, device=device)
+        self.capacity = capacity
+        self.lengths = torch.zeros(batch, dtype=torch.int32, device=device)
+        self._host_lengths = [0] * batch
+
+    # -- reference API --
+    def is_initialized(self) -> bool:
+        return max(self._host_lengths) > 0
+
+    def clear(self) -> None:
+        self.lengths.zero_()
+        self._host_lengths = [0] * len(self._host_lengths)
+
+    @property
+    def length(self) -> int:
+        if len(set(self._host_lengths)) != 1:
+            raise RuntimeError("KVCache: ragged batch has no single length")
+        return self._host_lengths[0]
+
+    @property
+    def key(self) -> torch.Tensor:
+        return self.key_buf[:, :, : self.length]
+
+    @property
+    def value(self) -> torch.Tensor:
+        return self.value_buf[:, :, : self.length]
+
+    # -- layout for the kernels --
+    @property
+    def strides(self):
+        s = self.key_buf.stride()
+        return s[0], s[1], s[2]
+
+    def host_lengths(self) -> list[int]:
+        return list(self._host_lengths)
+
+    def advance(self, n: int | list[int]) -> None:
+        add = n if isinstance(n, list) else [n] * len(self._host_lengths)
+        self._host_lengths = [a + b for a, b in zip(self._host_lengths, add)]
+        if max(self._host_lengths) > self.capacity:
+            raise RuntimeError("KVCache: capacity exceeded")
+        self.lengths.copy_(torch.tensor(self._host_lengths, dtype=torch.int32), non_blocking=True)
+
+    def set_lengths(self, lens: list[int]) -> None:
+        if max(lens) > self.capacity:
+            raise RuntimeError("KVCache: capacity exceeded")
+        self._host_lengths = list(lens)
+        self.lengths.copy_(torch.tensor(lens, dtype=torch.int32), non_blocking=True)
+
+
+class RoPE:
+    @staticmethod
+    def build_cos_sin(positions: torch.Tensor, head_dim: int, rope_theta: float):
+        """RoPE::BuildCosSin: (cos, sin) fp32 [S, D] on the positions' device."""
+        if head_dim % 2 != 0:
+            raise RuntimeError("RoPE: head_dim must be even.")
+        if not positions.is_cuda:
+            raise RuntimeError("RoPE: positions must be a CUDA tensor (no CPU fallback)")
+        pos = positions.to(torch.int64).contiguous()
+        n = pos.numel()
+        cos = torch.empty((n, head_dim), dtype=torch.float32, device=pos.device)
+        sin = torch.empty_like(cos)
+        abi.call("mllm_rope_build_cos_sin", _ptr(pos), n, head_dim, float(rope_theta), _ptr(cos),
+                 _ptr(sin), abi.stream_handle())
+        return cos, sin
+
+    @staticmethod
+    def apply(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        """RoPE::Apply for bf16 x [B, H, S, D] (any strides with D contiguous)."""
+        _check_cuda_bf16("RoPE", x)
+        if x.dim() != 4 or x.stride(3) != 1:
+            raise RuntimeError("RoPE: x must be [B, H, S, D] with D contiguous")
+        B, H, S, D = x.shape
+        cos = cos.to(torch.float32).contiguous()
+        sin = sin.to(torch.float32).contiguous()
+        out = torch.empty((B, H, S, D), dtype=BF16, device=x.device)
+        abi.call("mllm_rope_apply_bf16", _ptr(x), x.stride(0), x.stride(1), x.stride(2), B, H, S, D,
+                 _ptr(cos), _ptr(sin), _ptr(out), abi.stream_handle())
+        return out
+
+
+class DecodeWorkspace:
+    """Grow-only device scratch for the split-K decode partials (the C ABI never allocates)."""
+
+    def __init__(self):
+        self.buf = None
+
+    def get(self, nbytes: int, device) -> torch.Tensor:
+        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != torch.device(device):
+            self.buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+        return self.buf
+
+
+_WS = DecodeWorkspace()
+
+
+def qkv_epilogue(q, k, v, kv_cache: KVCache, positions: torch.Tensor, rope_theta: float,
+                 q_norm_weight=None, k_norm_weight=None, eps: float = 1e-6,
+                 rope_table=None) -> torch.Tensor:
+    """Fused per-head QK-RMSNorm (optional) + RoPE + KV append.  q [B,H,S,D], k/v [B,Hkv,S,D]
+    as strided views of the projections; positions int64 [S] (shared) or [B, S].  Rows go to
+    cache slots lengths[b] + s; the cache lengths advance by S.  Returns Q [B,H,S,D] (rotated)."""
+    for n, t in (("q", q), ("k", k), ("v", v)):
+        _check_cuda_bf16(n, t)
+        if t.dim() != 4 or t.stride(3) != 1:
+            raise RuntimeError(f"Attention: {n} must be rank-4 [B, h, S, D] with D contiguous")
+    B, H, S, D = q.shape
+    Hkv = k.shape[1]
+    if H % Hkv != 0:
+        raise RuntimeError("Attention: num_heads must be divisible by num_kv_heads.")
+    q_out = torch.empty((B, H, S, D), dtype=BF16, device=q.device)
+    pos = positions.to(torch.int64)
+    if pos.dim() == 1:
+        pos_sb, pos_ss = 0, pos.stride(0)
+    else:
+        pos_sb, pos_ss = pos.stride(0), pos.stride(1)
+    cos = sin = None
+    rsb = rss = 0
+    if rope_table is not None:
+        cos, sin = (t.to(torch.float32).contiguous() for t in rope_table)
+        rsb, rss = (0, 1) if cos.shape[0] == S else (S, 1)
+    qn = kn = None
+    if q_norm_weight is not None:
+        qn = q_norm_weight.to(BF16).contiguous()
+        kn = k_norm_weight.to(BF16).contiguous()
+    csb, csh, cst = kv_cache.strides
+    abi.call("mllm_qkv_epilogue_bf16",
+             _ptr(q), q.stride(0), q.stride(2), q.stride(1),
+             _ptr(k), k.stride(0), k.stride(2), k.stride(1),
+             _ptr(v), v.stride(0), v.stride(2), v.stride(1),
+             B, S, H, Hkv, D, _ptr(pos), pos_sb, pos_ss, float(rope_theta),
+             _ptr(cos), _ptr(sin), rsb, rss, _ptr(qn), _ptr(kn), float(eps), _ptr(q_out),
+             _ptr(kv_cache.key_buf), _ptr(kv_cache.value_buf), csb, csh, cst, kv_cache.capacity,
+             _ptr(kv_cache.lengths), abi.stream_handle())
+    kv_cache.advance(S)
+    return q_out
+
+
+def prefill_attention(q: torch.Tensor, kv_cache: KVCache, num_kv_heads: int) -> torch.Tensor:
+    """Causal attention of Q [B,H,S,D] (the newest S rows) over the cache -> [B, S, H*D]."""
+    B, H, S, D = q.shape
+    kv_len = kv_cache.length
+    out = torch.empty((B, S, H * D), dtype=BF16, device=q.device)
+    csb, csh, cst = kv_cache.strides
+    abi.call("mllm_prefill_attention_bf16", _ptr(q), _ptr(kv_cache.key_buf), _ptr(kv_cache.value_buf),
+             csb, csh, cst, B, H, num_kv_heads, D, S, kv_len, 1.0 / math.sqrt(D), _ptr(out),
+             abi.stream_handle())
+    return out
+
+
+def decode_attention(q: torch.Tensor, kv_cache: KVCache, num_kv_heads: int,
+                     max_kv_len: int | None = None) -> torch.Tensor:
+    """One query row per sequence (Q [B,H,1,D] or [B,H,D]) over each sequence's cache rows
+    (per-sequence lengths) -> [B, 1, H*D]."""
+    B, H, D = q.shape[0], q.shape[1], q.shape[-1]
+    qq = q.reshape(B, H, D)
+    if not qq.is_contiguous():
+        qq = qq.contiguous()
+    L = max_kv_len or max(kv_cache.host_lengths())
+    L = min(L, kv_cache.capacity)
+    out = torch.empty((B, 1, H * D), dtype=BF16, device=q.device)
+    lib = abi.load()
+    nbytes = lib.mllm_decode_attention_workspace_size(B, H, num_kv_heads, D, L)
+    ws = _WS.get(nbytes, q.device)
+    csb, csh, cst = kv_cache.strides
+    abi.call("mllm_decode_attention_bf16", _ptr(qq), _ptr(kv_cache.key_buf), _ptr(kv_cache.value_buf),
+             csb, csh, cst, _ptr(kv_cache.lengths), B, H, num_kv_heads, D, L, 1.0 / math.sqrt(D),
+             _ptr(out), _ptr(ws), ws.numel(), abi.stream_handle())
+    return out
+
+
+def _linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """Linear::Forward (Linear.h:33-68): x @ w.T in the input dtype (a cuBLAS GEMM)."""
+    if x.size(-1) != w.size(1):
+        raise RuntimeError("Linear: last dim of x must match weight in_features.")
+    return torch.nn.functional.linear(x, w)
+
+
+class Attention:
+    @staticmethod
+    def forward_projected(q, k, v, w_o, num_heads: int, num_kv_heads: int, head_dim: int,
+                          rope_theta: float, position_ids: torch.Tensor, kv_cache: KVCache | None,
+                          q_norm_weight=None, k_norm_weight=None, rms_norm_eps: float = 1e-6):
+        """Attention::ForwardProjected (Attention.h:100-326).  q [B,H,S,D], k/v [B,Hkv,S,D]
+        (views of the projections).  With norm weights, the per-head QK-RMSNorm that the
+        reference runs in TransformerBlock.h:103-134 is fused into the epilogue."""
+        if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+            raise RuntimeError("Attention::ForwardProjected: q/k/v must be rank-4 tensors.")
+        if num_heads % num_kv_heads != 0:
+            raise RuntimeError("Attention: num_heads must be divisible by num_kv_heads.")
+        B, _, S, D = q.shape
+        cache = kv_cache
+        if cache is None:  # no cache: attend over this call's rows only (Attention.h:183 skipped)
+            cache = KVCache(B, num_kv_heads, D, S, device=q.device)
+        pos = position_ids.to(device=q.device)
+        qr = qkv_epilogue(q, k, v, cache, pos, rope_theta, q_norm_weight, k_norm_weight, rms_norm_eps)
+        if S == 1:
+            out = decode_attention(qr, cache, num_kv_heads)
+        else:
+            out = prefill_attention(qr, cache, num_kv_heads)
+        return _linear(out, w_o)
+
+    @staticmethod
+    def forward(hidden, w_q, w_k, w_v, w_o, num_heads: int, num_kv_heads: int, head_dim: int,
+                rope_theta: float, position_ids: torch.Tensor, kv_cache: KVCache | None):
+        """Attention::Forward (Attention.h:29-86): project, view, transpose, then the above."""
+        if hidden.dim() != 3:
+            raise RuntimeError("Attention: hidden must be [B, S, H].")
+        B, S, _ = hidden.shape
+        q = _linear(hidden, w_q).view(B, S, num_heads, head_dim).transpose(1, 2)
+        k = _linear(hidden, w_k).view(B, S, num_kv_heads, head_dim).transpose(1, 2)
+        v = _linear(hidden, w_v).view(B, S, num_kv_heads, head_dim).transpose(1, 2)
+        return Attention.forward_projected(q, k, v, w_o, num_heads, num_kv_heads, head_dim,
+                                           rope_theta, position_ids, kv_cache)
+
+
+def attention_block(h, w_q, w_k, w_v, w_o, num_heads: int, num_kv_heads: int, head_dim: int,
+                    rope_theta: float, position_ids, kv_cache, w_q_norm=None, w_k_norm=None,
+                    rms_norm_eps: float = 1e-6):
+    """The attention half of TransformerBlock::Forward (TransformerBlock.h:77-195) after the
+    input RMSNorm: Qwen3 branch when norm weights are given, Llama branch otherwise."""
+    B, S, _ = h.shape
+    q = _linear(h, w_q).view(B, S, num_heads, head_dim).transpose(1, 2)
+    k = _linear(h, w_k).view(B, S, num_kv_heads, head_dim).transpose(1, 2)
+    v = _linear(h, w_v).view(B, S, num_kv_heads, head_dim).transpose(1, 2)
+    return Attention.forward_projected(q, k, v, w_o, num_heads, num_kv_heads, head_dim, rope_theta,
+                                       position_ids, kv_cache, w_q_norm, w_k_norm, rms_norm_eps)

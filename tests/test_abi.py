@@ -1,0 +1,76 @@
+"""The C-ABI library loads and exports exactly what include/mllm_attn.h declares.  CPU only:
+no compute call is made without a GPU (argument validation runs on the host)."""
+import ctypes as C
+import subprocess
+
+import pytest
+
+from mllm_b200 import abi, build
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return abi.load()
+
+
+def test_header_and_binding_agree():
+    assert abi.header_functions() == sorted(abi.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", build.lib_path()], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    declared = set(abi.header_functions())
+    assert declared <= exported
+    # nothing else leaks out of the library (the CUDA runtime is linked statically and hidden)
+    assert {s for s in exported if s.startswith("mllm_")} == declared
+
+
+def test_status_strings(lib):
+    assert lib.mllm_attn_abi_version() == 1
+    for code in abi.STATUS_NAMES:
+        assert lib.mllm_attn_status_string(code)
+    assert lib.mllm_attn_status_string(99) == b"unknown status"
+
+
+def test_host_side_argument_validation(lib):
+    # head_dim must be even (RoPE.h:34-37) -- rejected before any device call
+    st = lib.mllm_rope_build_cos_sin(None, 4, 7, 1e4, None, None, None)
+    assert st == 1 and b"even" in lib.mllm_attn_last_error()
+    # num_heads % num_kv_heads (Attention.h:139-144)
+    st = lib.mllm_decode_attention_bf16(None, None, None, 0, 0, 0, None, 1, 6, 4, 128, 16, 0.1, None,
+                                        None, 0, None)
+    assert st == 1 and b"divisible" in lib.mllm_attn_last_error()
+    st = lib.mllm_prefill_attention_bf16(None, None, None, 0, 0, 0, 1, 6, 4, 128, 1, 1, 0.1, None, None)
+    assert st == 1
+    # unsupported head_dim
+    st = lib.mllm_decode_attention_bf16(None, None, None, 0, 0, 0, None, 1, 8, 2, 96, 16, 0.1, None,
+                                        None, 0, None)
+    assert st == 2
+    # GQA group above 8 is reported as unsupported
+    st = lib.mllm_decode_attention_bf16(None, None, None, 0, 0, 0, None, 1, 32, 2, 128, 16, 0.1, None,
+                                        None, 0, None)
+    assert st == 2
+
+
+def test_workspace_size(lib):
+    ws = lib.mllm_decode_attention_workspace_size(32, 32, 8, 128, 4096)
+    assert ws > 0 and ws % 256 == 0
+    assert lib.mllm_decode_attention_workspace_size(0, 32, 8, 128, 4096) == 0
+    assert lib.mllm_decode_attention_workspace_size(32, 30, 8, 128, 4096) == 0
+
+
+def test_no_device_is_reported(lib):
+    """In this container there is no GPU: a well-formed call reports NO_DEVICE (or a CUDA error),
+    it never silently succeeds."""
+    buf = (C.c_int64 * 4)()
+    st = lib.mllm_rope_build_cos_sin(C.addressof(buf), 4, 8, 1e4, C.addressof(buf), C.addressof(buf), None)
+    try:
+        import torch
+        has_gpu = torch.cuda.is_available()
+    except Exception:
+        has_gpu = False
+    if not has_gpu:
+        assert st in (3, 5)

@@ -1,0 +1,268 @@
+"""Parity of the sm_100a kernels (called through the C ABI) against the oracle and the
+reference's own golden outputs.  Needs a B200."""
+import math
+import os
+
+import numpy as np
+import pytest
+
+from oracle import attention_oracle as O
+from tests.golden.cases import CASES, GOLDEN_DIR, ROPE_POSITIONS, ROPE_TABLE_CASES, make_inputs
+from tests.helpers import ATOL, RTOL, f32_to_torch_bf16, np_bits_to_torch, torch_to_bits
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def rt(cuda_device):
+    from mllm_b200 import build
+    build.build()
+    from mllm_b200 import runtime
+    return runtime
+
+
+def _golden(name):
+    return np.load(os.path.join(GOLDEN_DIR, name))
+
+
+def _steps(c):
+    return ["prefill"] + [f"decode{i}" for i in range(c.decode_steps)]
+
+
+# ---------------------------------------------------------------------------------------
+# RoPE table
+# ---------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("D,theta", ROPE_TABLE_CASES)
+def test_rope_table_vs_reference(rt, D, theta):
+    g = _golden("rope_tables.npz")
+    pos = torch.from_numpy(ROPE_POSITIONS).cuda()
+    cos, sin = rt.RoPE.build_cos_sin(pos, D, theta)
+    cos, sin = cos.cpu().numpy(), sin.cpu().numpy()
+    np.testing.assert_array_equal(cos[:, : D // 2], cos[:, D // 2:])
+    inv = O.rope_inv_freq(D, theta)
+    angle = ROPE_POSITIONS[:, None].astype(np.float32) * inv[None, :]
+    # device expf/cosf are within 2 ulp; the reference's CPU exp is within 1 ulp: the angle can
+    # differ by pos * 2 ulp(inv_freq) + 1 ulp(angle)
+    bound = (ROPE_POSITIONS[:, None] * np.spacing(inv)[None, :] * 2.02 + np.spacing(angle) + 5e-7)
+    key = f"d{D}_t{int(theta)}"
+    for name, ours in (("cos_", cos), ("sin_", sin)):
+        err = np.abs(ours[:, : D // 2].astype(np.float64) - g[name + key])
+        assert (err <= bound).all(), (name, float(err.max()))
+
+
+def test_rope_inline_equals_table(rt):
+    """The epilogue's in-kernel angles are bit-identical to mllm_rope_build_cos_sin's table."""
+    B, H, Hkv, S, D = 2, 4, 2, 33, 128
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    q = torch.randn(B, H, S, D, device="cuda", generator=gen).bfloat16()
+    k = torch.randn(B, Hkv, S, D, device="cuda", generator=gen).bfloat16()
+    v = torch.randn(B, Hkv, S, D, device="cuda", generator=gen).bfloat16()
+    pos = torch.arange(4000, 4000 + S, device="cuda")
+    c1 = rt.KVCache(B, Hkv, D, 64)
+    c2 = rt.KVCache(B, Hkv, D, 64)
+    q1 = rt.qkv_epilogue(q, k, v, c1, pos, 1e6)
+    table = rt.RoPE.build_cos_sin(pos, D, 1e6)
+    q2 = rt.qkv_epilogue(q, k, v, c2, pos, 1e6, rope_table=table)
+    assert torch.equal(q1, q2)
+    assert torch.equal(c1.key, c2.key) and torch.equal(c1.value, c2.value)
+    # RoPE.apply with the same table gives the same rotation
+    assert torch.equal(rt.RoPE.apply(q, *table), q1)
+
+
+# ---------------------------------------------------------------------------------------
+# Fused QKV epilogue: bit-exact KV cache against the reference (bf16 run)
+# ---------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("c", CASES, ids=lambda c: c.name)
+def test_epilogue_kv_cache_bit_exact(rt, c):
+    """Feeding the reference's own bf16 projections and RoPE table, the fused epilogue writes
+    exactly the reference's KVCache::key/value bits (Attention.h:183-208) at every step, and
+    the rotated q equals the pinned oracle's."""
+    g = _golden(f"{c.name}_bf16.npz")
+    inp = make_inputs(c, bf16=True)
+    B, H, Hkv, D = c.batch, c.num_heads, c.num_kv_heads, c.head_dim
+    cap = c.seq + c.decode_steps + 5
+    cache = rt.KVCache(B, Hkv, D, cap, zero=False)   # garbage beyond the rows we write
+    qn = kn = None
+    if c.qk_norm:
+        qn = f32_to_torch_bf16(inp["w_q_norm"], "cuda")
+        kn = f32_to_torch_bf16(inp["w_k_norm"], "cuda")
+    for tag in _steps(c):
+        # projections as [B, S, h, D] -> transposed views, exactly like TransformerBlock.h:91-96
+        qp = np_bits_to_torch(g[f"{tag}_q_proj_bits"], "cuda")       # [B,H,S,D]
+        kp = np_bits_to_torch(g[f"{tag}_k_proj_bits"], "cuda")
+        vp = np_bits_to_torch(g[f"{tag}_v_bits"], "cuda")
+        S = qp.shape[2]
+        qv = qp.transpose(1, 2).contiguous().transpose(1, 2)
+        kv_ = kp.transpose(1, 2).contiguous().transpose(1, 2)
+        vv = vp.transpose(1, 2).contiguous().transpose(1, 2)
+        cos = torch.from_numpy(g[f"{tag}_rope_cos"]).cuda()
+        sin = torch.from_numpy(g[f"{tag}_rope_sin"]).cuda()
+        pos = torch.from_numpy(g[f"{tag}_pos"]).cuda()
+        qr = rt.qkv_epilogue(qv, kv_, vv, cache, pos, c.rope_theta, qn, kn, c.eps, rope_table=(cos, sin))
+        L = cache.length
+        assert L == g[f"{tag}_key_bits"].shape[2]
+        np.testing.assert_array_equal(torch_to_bits(cache.key), g[f"{tag}_key_bits"], err_msg=tag)
+        np.testing.assert_array_equal(torch_to_bits(cache.value), g[f"{tag}_value_bits"], err_msg=tag)
+        # q: oracle (pinned bit-exact) on the same inputs
+        q_in = O.bf16_to_f32(g[f"{tag}_q_proj_bits"])
+        if c.qk_norm:
+            q_in = O.rms_norm(q_in, inp["w_q_norm"], c.eps, "bf16")
+        q_ref = O.rope_apply(q_in, g[f"{tag}_rope_cos"], g[f"{tag}_rope_sin"], "bf16")
+        np.testing.assert_array_equal(torch_to_bits(qr), O.bf16_bits(q_ref), err_msg=tag)
+
+
+def test_epilogue_rejects_bad_slots(rt):
+    """A cache slot past the capacity is not written and is reported on the device status."""
+    from mllm_b200 import abi
+    B, H, Hkv, S, D = 1, 2, 1, 4, 64
+    q = torch.randn(B, H, S, D, device="cuda").bfloat16()
+    k = torch.randn(B, Hkv, S, D, device="cuda").bfloat16()
+    cache = rt.KVCache(B, Hkv, D, 6)
+    cache.set_lengths([4])        # rows 4..7 requested, capacity 6: rows 6 and 7 are refused
+    before = cache.key_buf.clone()
+    lib = abi.load()
+    abi.call("mllm_qkv_epilogue_bf16", q.data_ptr(), q.stride(0), q.stride(2), q.stride(1),
+             k.data_ptr(), k.stride(0), k.stride(2), k.stride(1), k.data_ptr(), k.stride(0), k.stride(2),
+             k.stride(1), B, S, H, Hkv, D, torch.arange(S, device="cuda").data_ptr(), 0, 1, 1e4, None,
+             None, 0, 0, None, None, 1e-6, torch.empty_like(q).data_ptr(), cache.key_buf.data_ptr(),
+             cache.value_buf.data_ptr(), *cache.strides, 6, cache.lengths.data_ptr(), None)
+    st = lib.mllm_attn_device_status(None)
+    assert st == 7  # MLLM_ERR_DEVICE_LENGTH
+    assert torch.equal(cache.key_buf[0, 0, :4], before[0, 0, :4])
+    assert lib.mllm_attn_device_status(None) == 0  # cleared
+
+
+# ---------------------------------------------------------------------------------------
+# Decode
+# ---------------------------------------------------------------------------------------
+
+DECODE_CASES = [
+    # B, H, Hkv, D, lengths (per sequence)
+    (3, 8, 2, 128, [1, 64, 65]),
+    (4, 32, 8, 128, [300, 513, 2048, 4097]),
+    (2, 10, 2, 128, [777, 1]),           # GQA group 5
+    (2, 32, 4, 64, [512, 129]),          # TinyLlama geometry (group 8, D=64)
+    (5, 4, 4, 64, [17, 256, 255, 1000, 3]),   # MHA
+]
+
+
+@pytest.mark.parametrize("B,H,Hkv,D,lens", DECODE_CASES)
+def test_decode_vs_oracle(rt, B, H, Hkv, D, lens):
+    rng = np.random.default_rng(B * 100 + H)
+    cap = max(lens) + 70
+    cache = rt.KVCache(B, Hkv, D, cap, zero=False)
+    cache.key_buf.fill_(float("nan"))     # rows beyond each length must never leak
+    cache.value_buf.fill_(float("nan"))
+    kc = O.round_bf16(rng.standard_normal((B, Hkv, cap, D)).astype(np.float32))
+    vc = O.round_bf16(rng.standard_normal((B, Hkv, cap, D)).astype(np.float32))
+    for b, L in enumerate(lens):
+        cache.key_buf[b, :, :L] = f32_to_torch_bf16(kc[b, :, :L], "cuda")
+        cache.value_buf[b, :, :L] = f32_to_torch_bf16(vc[b, :, :L], "cuda")
+    cache.set_lengths(lens)
+    q = O.round_bf16(rng.standard_normal((B, H, D)).astype(np.float32))
+    out = rt.decode_attention(f32_to_torch_bf16(q, "cuda"), cache, Hkv)
+    got = out.float().cpu().numpy().reshape(B, H * D)
+    ref = O.decode_attention(q, kc, vc, lens, H, Hkv, D)
+    assert np.isfinite(got).all()
+    np.testing.assert_allclose(got, ref, rtol=RTOL, atol=ATOL)
+
+
+# ---------------------------------------------------------------------------------------
+# Prefill
+# ---------------------------------------------------------------------------------------
+
+PREFILL_CASES = [
+    # B, H, Hkv, D, q_len, prefix (cache rows before the new block)
+    (1, 4, 2, 128, 1, 0),
+    (2, 8, 2, 128, 128, 0),
+    (1, 8, 2, 128, 200, 0),
+    (2, 10, 2, 128, 77, 51),     # chunked prefill over an existing prefix, GQA 5
+    (1, 32, 4, 64, 512, 0),      # TinyLlama geometry
+    (1, 4, 4, 64, 300, 200),
+    (1, 8, 8, 128, 384, 1),
+]
+
+
+@pytest.mark.parametrize("B,H,Hkv,D,S,prefix", PREFILL_CASES)
+def test_prefill_vs_oracle(rt, B, H, Hkv, D, S, prefix):
+    rng = np.random.default_rng(S * 7 + prefix)
+    L = prefix + S
+    cache = rt.KVCache(B, Hkv, D, L + 130, zero=False)
+    cache.key_buf.fill_(float("nan"))
+    cache.value_buf.fill_(float("nan"))
+    kc = O.round_bf16(rng.standard_normal((B, Hkv, L, D)).astype(np.float32))
+    vc = O.round_bf16(rng.standard_normal((B, Hkv, L, D)).astype(np.float32))
+    cache.key_buf[:, :, :L] = f32_to_torch_bf16(kc, "cuda")
+    cache.value_buf[:, :, :L] = f32_to_torch_bf16(vc, "cuda")
+    cache.set_lengths([L] * B)
+    q = O.round_bf16(rng.standard_normal((B, H, S, D)).astype(np.float32))
+    out = rt.prefill_attention(f32_to_torch_bf16(q, "cuda"), cache, Hkv)
+    got = out.float().cpu().numpy()
+    ref = O.attention_core(q, kc, vc, H, Hkv, D)
+    assert np.isfinite(got).all()
+    np.testing.assert_allclose(got, ref, rtol=RTOL, atol=ATOL)
+
+
+# ---------------------------------------------------------------------------------------
+# Whole attention layer (projections in torch, the rest on the new kernels) vs the reference
+# ---------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("c", CASES, ids=lambda c: c.name)
+def test_layer_matches_reference_fp32(rt, c):
+    """Prefill then decode steps through the mirror of Attention::Forward / the Qwen3 block,
+    bf16 on the device, against the reference's fp32 CPU outputs (rtol = atol = 2e-2)."""
+    g = _golden(f"{c.name}_f32.npz")
+    inp = make_inputs(c, bf16=True)
+    T = {k: f32_to_torch_bf16(v, "cuda") for k, v in inp.items()}
+    H, Hkv, D = c.num_heads, c.num_kv_heads, c.head_dim
+    cache = rt.KVCache(c.batch, Hkv, D, c.seq + c.decode_steps)
+    steps = [("prefill", T["hidden"])] + [(f"decode{i}", T["decode_hidden"][i]) for i in range(c.decode_steps)]
+    for tag, hid in steps:
+        S = hid.shape[1]
+        pos = (torch.tensor([cache.length], device="cuda") if (cache.is_initialized() and S == 1)
+               else torch.arange(S, device="cuda"))
+        np.testing.assert_array_equal(pos.cpu().numpy(), g[tag + "_pos"])
+        if c.qk_norm:
+            out = rt.attention_block(hid, T["w_q"], T["w_k"], T["w_v"], T["w_o"], H, Hkv, D, c.rope_theta,
+                                     pos, cache, T["w_q_norm"], T["w_k_norm"], c.eps)
+        else:
+            out = rt.Attention.forward(hid, T["w_q"], T["w_k"], T["w_v"], T["w_o"], H, Hkv, D,
+                                       c.rope_theta, pos, cache)
+        np.testing.assert_allclose(out.float().cpu().numpy(), g[tag + "_out"], rtol=RTOL, atol=ATOL,
+                                   err_msg=tag)
+    np.testing.assert_allclose(cache.key.float().cpu().numpy(), g["key"], rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(cache.value.float().cpu().numpy(), g["value"], rtol=RTOL, atol=ATOL)
+
+
+def test_no_cache_path(rt):
+    """kv_cache == nullptr (Attention.h:183): attention over the call's own rows only."""
+    c = CASES[0]
+    inp = make_inputs(c, bf16=True)
+    T = {k: f32_to_torch_bf16(v, "cuda") for k, v in inp.items()}
+    pos = torch.arange(c.seq, device="cuda")
+    out = rt.Attention.forward(T["hidden"], T["w_q"], T["w_k"], T["w_v"], T["w_o"], c.num_heads,
+                               c.num_kv_heads, c.head_dim, c.rope_theta, pos, None)
+    ref = O.attention_forward(inp["hidden"], inp["w_q"], inp["w_k"], inp["w_v"], inp["w_o"], c.num_heads,
+                              c.num_kv_heads, c.head_dim, c.rope_theta, np.arange(c.seq), None)
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref, rtol=RTOL, atol=ATOL)
+
+
+def test_reference_errors_are_kept(rt):
+    with pytest.raises(RuntimeError, match="divisible"):
+        rt.Attention.forward_projected(torch.zeros(1, 6, 2, 64, device="cuda").bfloat16(),
+                                       torch.zeros(1, 4, 2, 64, device="cuda").bfloat16(),
+                                       torch.zeros(1, 4, 2, 64, device="cuda").bfloat16(),
+                                       torch.zeros(64, 384, device="cuda").bfloat16(), 6, 4, 64, 1e4,
+                                       torch.arange(2, device="cuda"), None)
+    with pytest.raises(RuntimeError, match="rank-4"):
+        rt.Attention.forward_projected(torch.zeros(6, 2, 64, device="cuda").bfloat16(),
+                                       torch.zeros(1, 4, 2, 64, device="cuda").bfloat16(),
+                                       torch.zeros(1, 4, 2, 64, device="cuda").bfloat16(),
+                                       torch.zeros(64, 384, device="cuda").bfloat16(), 4, 4, 64, 1e4,
+                                       torch.arange(2, device="cuda"), None)
+    with pytest.raises(RuntimeError, match="CPU fallback"):
+        rt.RoPE.apply(torch.zeros(1, 1, 2, 64).bfloat16(), torch.zeros(2, 64), torch.zeros(2, 64))
