@@ -234,7 +234,7 @@ def run_gpu(args, rank, world, device):
             src.data_ptr() + (H + HKV) * D * 2, row, row, D,
             B, 1, H, HKV, D, pos.data_ptr(), 1, 0, THETA, None, None, 0, 0,
             gq.data_ptr(), gk.data_ptr(), EPS, q_rot.data_ptr(),
-            kbuf.data_ptr(), vbuf.data_ptr(), csb, csh, cst, L, start.data_ptr(), sh)
+            kbuf.data_ptr(), vbuf.data_ptr(), csb, csh, cst, L, start.data_ptr(), 0, sh)
         assert st == 0, lib.mllm_attn_last_error()
 
     def decode(dst):
@@ -335,7 +335,7 @@ def run_gpu(args, rank, world, device):
                 qkv_p.data_ptr() + (Hr + Hkvr) * D * 2, S * prow, prow, D,
                 Bp, S, Hr, Hkvr, D, pos_p.data_ptr(), 0, 1, THETA, None, None, 0, 0,
                 gq.data_ptr(), gk.data_ptr(), EPS, qp.data_ptr(), kp.data_ptr(), vp.data_ptr(),
-                psb, psh, pst, S, start_p.data_ptr(), sh)
+                psb, psh, pst, S, start_p.data_ptr(), 0, sh)
             assert st == 0, lib.mllm_attn_last_error()
 
         def attn_p():

@@ -103,8 +103,9 @@ MLLM_API int mllm_rope_apply_bf16(const void* x, int64_t x_stride_b, int64_t x_s
  *   q_out: bf16 [batch, num_heads, seq_len, head_dim] contiguous (post-norm, post-RoPE)
  *   k_cache/v_cache row for (b, h, slot = cache_start[b] + s) at
  *       cache + b*cache_sb + h*cache_sh + slot*cache_st
- *   cache_start: int32 device [batch]; slots must lie below cache_capacity (checked on the
- *       device: out-of-range rows are skipped and MLLM_ERR_DEVICE_LENGTH is recorded). */
+ *   cache_start: int32 device [batch], or NULL for a batch-uniform start row
+ *       `uniform_cache_start`; slots must lie below cache_capacity (checked on the device:
+ *       out-of-range rows are skipped and MLLM_ERR_DEVICE_LENGTH is recorded). */
 MLLM_API int mllm_qkv_epilogue_bf16(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh,
                            const void* k, int64_t k_sb, int64_t k_ss, int64_t k_sh,
                            const void* v, int64_t v_sb, int64_t v_ss, int64_t v_sh,
@@ -116,7 +117,7 @@ MLLM_API int mllm_qkv_epilogue_bf16(const void* q, int64_t q_sb, int64_t q_ss, i
                            void* q_out,
                            void* k_cache, void* v_cache, int64_t cache_sb, int64_t cache_sh,
                            int64_t cache_st, int64_t cache_capacity, const int32_t* cache_start,
-                           mllm_stream_t stream);
+                           int64_t uniform_cache_start, mllm_stream_t stream);
 
 /* ----------------------------------------------------------------------------------------
  * Causal GQA prefill.  Replaces src/core/runtime/Attention.h:220-316 (repeat_interleave
@@ -142,7 +143,8 @@ MLLM_API int mllm_prefill_attention_bf16(const void* q, const void* k_cache, con
  *   caches: as for prefill; max_kv_len = rows addressable per (b, kv head)
  *   kv_lens: int32 device [batch], the number of valid rows of each sequence (new token
  *            included); values are clamped to [0, max_kv_len] on the device and an
- *            out-of-range value records MLLM_ERR_DEVICE_LENGTH.
+ *            out-of-range value records MLLM_ERR_DEVICE_LENGTH.  NULL: every sequence has
+ *            max_kv_len rows (the batch-uniform cache of the reference runners).
  *   out:    bf16 [batch, num_heads*head_dim]
  *   workspace: device scratch of at least mllm_decode_attention_workspace_size() bytes,
  *            256-byte aligned; contents need not be initialised. */

@@ -41,7 +41,7 @@ SIGNATURES = {
     "mllm_rope_apply_bf16": (_i, [_p, _i64, _i64, _i64, _i, _i, _i, _i, _p, _p, _p, _p]),
     "mllm_qkv_epilogue_bf16": (_i, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64,
                                     _i, _i, _i, _i, _i, _p, _i64, _i64, _d, _p, _p, _i64, _i64,
-                                    _p, _p, _d, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p]),
+                                    _p, _p, _d, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i64, _p]),
     "mllm_prefill_attention_bf16": (_i, [_p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _i, _f, _p, _p]),
     "mllm_decode_attention_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "mllm_decode_attention_bf16": (_i, [_p, _p, _p, _i64, _i64, _i64, _p, _i, _i, _i, _i, _i, _f, _p,

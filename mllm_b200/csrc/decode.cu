@@ -50,7 +50,7 @@ struct DecodeCfg {
 
 struct DecodeArgs {
     const __nv_bfloat16* q;     // [B, H, D]
-    const int32_t* kv_lens;     // [B]
+    const int32_t* kv_lens;     // [B], or NULL: every sequence has max_len rows
     __nv_bfloat16* out;         // [B, H*D]
     float* part_o;              // [B*Hkv*nch, n_rep, D]
     float* part_ml;             // [B*Hkv*nch, n_rep, 2]
@@ -89,7 +89,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int bg = item / a.nch;
         g = bg % a.Hkv;
         b = bg / a.Hkv;
-        int len = a.kv_lens[b];
+        int len = a.kv_lens ? a.kv_lens[b] : a.max_len;
         if (len < 0 || len > a.max_len) {
             if (threadIdx.x == 0 && c == 0 && g == 0) record_error(kErrBadLength);
             len = len < 0 ? 0 : a.max_len;
@@ -334,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 template <int D>
 __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeArgs a) {
     const int g = blockIdx.x, b = blockIdx.y;
-    int L = a.kv_lens[b];
+    int L = a.kv_lens ? a.kv_lens[b] : a.max_len;
     L = L < 0 ? 0 : (L > a.max_len ? a.max_len : L);
     const int nch_b = (L + a.chunk - 1) / a.chunk;
     if (nch_b <= 1) return;  // written directly by the split kernel
@@ -409,7 +409,7 @@ extern "C" int mllm_decode_attention_bf16(const void* q, const void* k_cache, co
     if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale))
         return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention: softmax_scale must be positive");
     if (batch == 0) return ok();
-    if (!q || !k_cache || !v_cache || !kv_lens || !out)
+    if (!q || !k_cache || !v_cache || !out)
         return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention: null pointer");
     if (!aligned(q, 4) || !aligned(out, 4)) return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention: q/out misaligned");
     const size_t need = workspace_bytes_for(batch, num_heads, num_kv_heads, head_dim, max_kv_len);

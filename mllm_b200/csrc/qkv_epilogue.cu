@@ -41,7 +41,8 @@ struct EpilogueArgs {
     __nv_bfloat16* k_cache;
     __nv_bfloat16* v_cache;
     int64_t c_sb, c_sh, c_st, capacity;
-    const int32_t* cache_start;
+    const int32_t* cache_start;   // NULL: uniform_start for every sequence
+    int64_t uniform_start;
 };
 
 constexpr int kWarps = 8;
@@ -157,7 +158,7 @@ __global__ void __launch_bounds__(kWarps * 32) qkv_epilogue_kernel(EpilogueArgs 
     if (kind == 0) {
         dst = a.q_out + (((int64_t)b * a.H + h) * a.S + s) * D;
     } else {
-        const int64_t slot = (int64_t)a.cache_start[b] + s;
+        const int64_t slot = (a.cache_start ? (int64_t)a.cache_start[b] : a.uniform_start) + s;
         if (slot < 0 || slot >= a.capacity) {
             if (lane == 0) record_error(kErrBadLength);
             return;
@@ -183,7 +184,8 @@ extern "C" int mllm_qkv_epilogue_bf16(const void* q, int64_t q_sb, int64_t q_ss,
                                       int64_t rope_row_ss, const void* q_norm_weight, const void* k_norm_weight,
                                       double rms_norm_eps, void* q_out, void* k_cache, void* v_cache,
                                       int64_t cache_sb, int64_t cache_sh, int64_t cache_st, int64_t cache_capacity,
-                                      const int32_t* cache_start, mllm_stream_t stream) {
+                                      const int32_t* cache_start, int64_t uniform_cache_start,
+                                      mllm_stream_t stream) {
     if (batch < 0 || seq_len < 0 || num_heads <= 0 || num_kv_heads <= 0)
         return fail(MLLM_ERR_INVALID_ARGUMENT, "qkv_epilogue: bad sizes");
     if (num_heads % num_kv_heads != 0)
@@ -199,7 +201,7 @@ extern "C" int mllm_qkv_epilogue_bf16(const void* q, int64_t q_sb, int64_t q_ss,
     if (rope_cos == nullptr && !(rope_theta > 0.0))
         return fail(MLLM_ERR_INVALID_ARGUMENT, "qkv_epilogue: rope_theta must be positive");
     if (batch == 0 || seq_len == 0) return ok();
-    if (!q || !k || !v || !q_out || !k_cache || !v_cache || !cache_start)
+    if (!q || !k || !v || !q_out || !k_cache || !v_cache)
         return fail(MLLM_ERR_INVALID_ARGUMENT, "qkv_epilogue: null pointer");
     if (cache_capacity <= 0) return fail(MLLM_ERR_INVALID_ARGUMENT, "qkv_epilogue: cache_capacity must be > 0");
     if ((int64_t)batch * seq_len > 0x7fffffffLL) return fail(MLLM_ERR_INVALID_ARGUMENT, "qkv_epilogue: too many tokens");
@@ -225,6 +227,7 @@ extern "C" int mllm_qkv_epilogue_bf16(const void* q, int64_t q_sb, int64_t q_ss,
     a.v_cache = (__nv_bfloat16*)v_cache;
     a.c_sb = cache_sb; a.c_sh = cache_sh; a.c_st = cache_st; a.capacity = cache_capacity;
     a.cache_start = cache_start;
+    a.uniform_start = uniform_cache_start;
 
     const int total_heads = num_heads + 2 * num_kv_heads;
     dim3 grid((unsigned)(batch * seq_len), (unsigned)((total_heads + kWarps - 1) / kWarps));

@@ -1,0 +1,93 @@
+"""Compile recipes for the C++ drop-in headers (mllm_b200/dropin/core/runtime/*.h).
+
+1. `check_runners()` compiles the reference's UNCHANGED model runners (QwenRunner.cpp,
+   LlamaRunner.cpp) with this directory ahead of the reference's own include path, proving
+   that the drop-in headers keep every symbol and signature the runners use.  It needs the
+   reference tree (build container only) and writes objects under mllm_b200/_build/.
+2. `build_facade_module()` builds tests/facade/mllm_facade*.so, a Python binding of the
+   drop-in headers used by the GPU tests (RMSNorm/Linear/MLP come from the reference tree,
+   unchanged, so this too is built where the reference is present; the .so travels).
+
+The reference tree spells the runner interface header `ImodelRunner.h` but includes it as
+`IModelRunner.h` (works only on case-insensitive file systems), so a one-file shim directory
+with that name is generated under mllm_b200/_build/shim.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+import sysconfig
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.dirname(HERE)
+ROOT = os.path.dirname(PKG)
+BUILD = os.path.join(PKG, "_build")
+REFERENCE = "/root/reference"
+
+
+def _torch_flags():
+    import torch
+    from torch.utils import cpp_extension as ce
+    inc = [f"-I{p}" for p in ce.include_paths()] + ["-I/usr/local/cuda/include"]
+    libs = []
+    for p in ce.library_paths():
+        libs += [f"-L{p}", f"-Wl,-rpath,{p}"]
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    return inc, libs, [f"-D_GLIBCXX_USE_CXX11_ABI={abi}"]
+
+
+def _shim(reference: str) -> str:
+    d = os.path.join(BUILD, "shim", "models", "base")
+    os.makedirs(d, exist_ok=True)
+    link = os.path.join(d, "IModelRunner.h")
+    target = os.path.join(reference, "src", "models", "base", "ImodelRunner.h")
+    if not os.path.exists(link):
+        with open(link, "w") as f:
+            f.write(f'#include "{target}"\n')
+    return os.path.join(BUILD, "shim")
+
+
+def include_flags(reference: str = REFERENCE) -> list[str]:
+    """Drop-in headers first, then the C ABI, then the reference tree."""
+    return [f"-I{HERE}", f"-I{os.path.join(ROOT, 'include')}", f"-I{_shim(reference)}",
+            f"-I{os.path.join(reference, 'src')}", f"-I{os.path.join(reference, 'external')}"]
+
+
+def check_runners(reference: str = REFERENCE, verbose: bool = False) -> list[str]:
+    if not os.path.isdir(os.path.join(reference, "src", "models")):
+        raise FileNotFoundError("reference tree not present")
+    inc, _, defs = _torch_flags()
+    os.makedirs(BUILD, exist_ok=True)
+    outs = []
+    for src in ("models/qwen/QwenRunner.cpp", "models/llama/LlamaRunner.cpp"):
+        obj = os.path.join(BUILD, os.path.basename(src).replace(".cpp", ".o"))
+        cmd = ["g++", "-std=c++17", "-O1", "-fPIC", "-w", "-c", *defs, *include_flags(reference), *inc,
+               os.path.join(reference, "src", src), "-o", obj]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        subprocess.run(cmd, check=True)
+        outs.append(obj)
+    return outs
+
+
+def build_facade_module(reference: str = REFERENCE, verbose: bool = False) -> str:
+    from mllm_b200 import build as libbuild
+    lib = libbuild.build()
+    inc, libs, defs = _torch_flags()
+    src = os.path.join(ROOT, "tests", "facade", "facade_binding.cpp")
+    out_dir = os.path.join(ROOT, "tests", "facade")
+    out = os.path.join(out_dir, "mllm_facade" + sysconfig.get_config_var("EXT_SUFFIX"))
+    cmd = ["g++", "-std=c++17", "-O2", "-shared", "-fPIC", "-w", *defs, "-DTORCH_EXTENSION_NAME=mllm_facade",
+           f"-I{sysconfig.get_paths()['include']}", *include_flags(reference), *inc, src, "-o", out, *libs,
+           f"-L{os.path.dirname(lib)}", f"-Wl,-rpath,$ORIGIN/../../mllm_b200/lib", "-lmllm_attn",
+           "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-lc10", "-lc10_cuda", "-ltorch_python"]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    subprocess.run(cmd, check=True)
+    return out
+
+
+if __name__ == "__main__":
+    print(check_runners(verbose=True))
+    print(build_facade_module(verbose=True))

@@ -181,7 +181,7 @@ def qkv_epilogue(q, k, v, kv_cache: KVCache, positions: torch.Tensor, rope_theta
              B, S, H, Hkv, D, _ptr(pos), pos_sb, pos_ss, float(rope_theta),
              _ptr(cos), _ptr(sin), rsb, rss, _ptr(qn), _ptr(kn), float(eps), _ptr(q_out),
              _ptr(kv_cache.key_buf), _ptr(kv_cache.value_buf), csb, csh, cst, kv_cache.capacity,
-             _ptr(kv_cache.lengths), abi.stream_handle())
+             _ptr(kv_cache.lengths), 0, abi.stream_handle())
     kv_cache.advance(S)
     return q_out
 

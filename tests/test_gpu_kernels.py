@@ -129,7 +129,7 @@ def test_epilogue_rejects_bad_slots(rt):
              k.data_ptr(), k.stride(0), k.stride(2), k.stride(1), k.data_ptr(), k.stride(0), k.stride(2),
              k.stride(1), B, S, H, Hkv, D, torch.arange(S, device="cuda").data_ptr(), 0, 1, 1e4, None,
              None, 0, 0, None, None, 1e-6, torch.empty_like(q).data_ptr(), cache.key_buf.data_ptr(),
-             cache.value_buf.data_ptr(), *cache.strides, 6, cache.lengths.data_ptr(), None)
+             cache.value_buf.data_ptr(), *cache.strides, 6, cache.lengths.data_ptr(), 0, None)
     st = lib.mllm_attn_device_status(None)
     assert st == 7  # MLLM_ERR_DEVICE_LENGTH
     assert torch.equal(cache.key_buf[0, 0, :4], before[0, 0, :4])
