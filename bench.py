@@ -379,6 +379,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--skip-prefill", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg (profiling runs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -428,7 +429,7 @@ def main():
     achieved = kv_bytes / (res["dec_ms"] * 1e-3) / 1e9
     e2e_ms = res["e2e_ms"] / args.steps
     cpu = None
-    if n == 1:
+    if n == 1 and not args.skip_cpu:
         r = cpu_reference_decode(5, 1, budget_s=20.0)
         cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
     line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": n, "steps": args.steps,

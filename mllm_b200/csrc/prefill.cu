@@ -195,26 +195,48 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_before();
             mbar_arrive(&s_free[sb]);
 
-            const int lim = p_row - j * kBN;   // columns <= lim are visible (causal)
-            float mt = -INFINITY;
+            // Causal bound: only tiles reaching past the CTA's first query position need it
+            // (warp-uniform test).  Reductions use 8 independent accumulators so the 128-long
+            // max / sum chains do not serialise on instruction latency.
+            constexpr int kAcc = 8;
+            float mx[kAcc];
 #pragma unroll
-            for (int c = 0; c < kBN; ++c) {
-                const float v = (c <= lim) ? s[c] * a.scale_log2 : -INFINITY;
-                s[c] = v;
-                mt = fmaxf(mt, v);
+            for (int i = 0; i < kAcc; ++i) mx[i] = -INFINITY;
+            if ((j + 1) * kBN - 1 > pos_offset + m0) {
+                const int lim = p_row - j * kBN;   // columns <= lim are visible
+#pragma unroll
+                for (int c = 0; c < kBN; ++c) {
+                    s[c] = (c <= lim) ? s[c] : -INFINITY;
+                    mx[c % kAcc] = fmaxf(mx[c % kAcc], s[c]);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < kBN; ++c) mx[c % kAcc] = fmaxf(mx[c % kAcc], s[c]);
             }
+#pragma unroll
+            for (int w = kAcc / 2; w >= 1; w >>= 1)
+#pragma unroll
+                for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
+            const float mt = mx[0] * a.scale_log2;   // scale > 0: max of scaled = scaled max
             const float m_new = fmaxf(m_run, mt);
             const bool grow = (m_new - m_run) > kRescaleThreshold;   // true on the first tile
             float m_use = grow ? m_new : m_run;
             if (m_use == -INFINITY) m_use = 0.f;
             const float alpha = grow ? ex2_approx(m_run - m_use) : 1.f;
-            float rs = 0.f;
+            const float neg_m = -m_use;
+            float sum[kAcc];
+#pragma unroll
+            for (int i = 0; i < kAcc; ++i) sum[i] = 0.f;
 #pragma unroll
             for (int c = 0; c < kBN; ++c) {
-                s[c] = ex2_approx(s[c] - m_use);
-                rs += s[c];
+                s[c] = ex2_approx(fmaf(s[c], a.scale_log2, neg_m));
+                sum[c % kAcc] += s[c];
             }
-            l_run = l_run * alpha + rs;
+#pragma unroll
+            for (int w = kAcc / 2; w >= 1; w >>= 1)
+#pragma unroll
+                for (int i = 0; i < w; ++i) sum[i] += sum[i + w];
+            l_run = l_run * alpha + sum[0];
             m_run = m_use;
 
             if (j > 0) {
