@@ -157,6 +157,30 @@ MLLM_API int mllm_decode_attention_bf16(const void* q, const void* k_cache, cons
                                int head_dim, int max_kv_len, float softmax_scale, void* out,
                                void* workspace, size_t workspace_bytes, mllm_stream_t stream);
 
+/* ----------------------------------------------------------------------------------------
+ * Split-K flash-decode that allocates nothing and takes no workspace.  It has no counterpart
+ * in the reference: it exists for callers that cannot allocate device memory when they run
+ * decode (a runtime whose device memory is carved up once by its own arena, code running
+ * under another framework's allocator lock, or a path where an allocation would be a
+ * synchronising call).
+ *   Arguments and results are those of mllm_decode_attention_bf16 without the workspace.
+ *   The split-K partials live in one 16 MiB scratch array compiled into this library; each
+ *   GPU that loads the library keeps that array resident until the process exits.  A batch
+ *   whose mllm_decode_attention_workspace_size() exceeds 16 MiB is rejected with
+ *   MLLM_ERR_WORKSPACE (C2-sized work -- 32 sequences x 8 kv heads x 4096 rows at
+ *   head_dim 128 -- needs about 8.1 MiB).
+ *   The first call on each device looks up the array's device address (cudaGetSymbolAddress);
+ *   make that first call before any CUDA stream capture begins.
+ *   All calls on a device share the array, which keeps the previous call's partials (every
+ *   value read within a call is written earlier in that call, so nothing is cleared).  Calls
+ *   that overlap on the GPU -- concurrent streams, or several host threads -- race on it:
+ *   serialise them. */
+MLLM_API int mllm_decode_attention_noalloc_bf16(const void* q, const void* k_cache, const void* v_cache,
+                                                int64_t cache_sb, int64_t cache_sh, int64_t cache_st,
+                                                const int32_t* kv_lens, int batch, int num_heads,
+                                                int num_kv_heads, int head_dim, int max_kv_len,
+                                                float softmax_scale, void* out, mllm_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

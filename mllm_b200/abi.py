@@ -46,6 +46,8 @@ SIGNATURES = {
     "mllm_decode_attention_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "mllm_decode_attention_bf16": (_i, [_p, _p, _p, _i64, _i64, _i64, _p, _i, _i, _i, _i, _i, _f, _p,
                                         _p, _sz, _p]),
+    "mllm_decode_attention_noalloc_bf16": (_i, [_p, _p, _p, _i64, _i64, _i64, _p, _i, _i, _i, _i, _i, _f,
+                                                _p, _p]),
 }
 
 

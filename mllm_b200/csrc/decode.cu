@@ -467,3 +467,134 @@ extern "C" int mllm_decode_attention_bf16(const void* q, const void* k_cache, co
     if (int st = check_cuda(cudaGetLastError(), "decode_combine_kernel launch")) return st;
     return ok();
 }
+
+// ---------------------------------------------------------------------------------------------
+// Decode without a caller workspace.
+//
+// Some callers cannot allocate device memory at the moment they run decode: a runtime whose
+// memory is carved up once at start-up by its own arena (and forbids later cudaMalloc), a
+// kernel-launch hook running inside another framework's allocator lock, or code on a path
+// where an allocation would be a synchronising call.  This entry point serves them: the
+// split-K partials live in a fixed scratch array that is part of this library's device image,
+// so nothing is allocated per call.  The array is kNoAllocScratchBytes (16 MiB) per device and
+// stays resident on every GPU that loads the library until the process exits.
+// ---------------------------------------------------------------------------------------------
+#include <cstdio>
+#include <mutex>
+
+namespace mllm_b200 {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+
+// Device-resident scratch shared by every call of mllm_decode_attention_noalloc_bf16 on a device.
+static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device.  The first call on a device looks
+// it up with cudaGetSymbolAddress (host code cannot use the array's name as a device address).
+int noalloc_scratch(void** out) {
+    int dev = 0;
+    if (int st = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return st;
+    if (dev < 0 || dev >= kMaxDevices) return fail(MLLM_ERR_UNSUPPORTED, "decode_attention_noalloc: device index too large");
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        if (int st = check_cuda(cudaGetSymbolAddress(&p, g_decode_noalloc_scratch), "cudaGetSymbolAddress(scratch)"))
+            return st;
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return MLLM_OK;
+}
+
+}  // namespace
+}  // namespace mllm_b200
+
+extern "C" int mllm_decode_attention_noalloc_bf16(const void* q, const void* k_cache, const void* v_cache,
+                                                  int64_t cache_sb, int64_t cache_sh, int64_t cache_st,
+                                                  const int32_t* kv_lens, int batch, int num_heads,
+                                                  int num_kv_heads, int head_dim, int max_kv_len,
+                                                  float softmax_scale, void* out, mllm_stream_t stream) {
+    if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_kv_len <= 0)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention_noalloc: bad sizes");
+    if (num_heads % num_kv_heads != 0)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "Attention: num_heads must be divisible by num_kv_heads.");
+    if (head_dim != 64 && head_dim != 128)
+        return fail(MLLM_ERR_UNSUPPORTED, "decode_attention_noalloc: head_dim must be 64 or 128");
+    const int n_rep = num_heads / num_kv_heads;
+    if (n_rep > kMaxGroup) return fail(MLLM_ERR_UNSUPPORTED, "decode_attention_noalloc: GQA group larger than 8");
+    if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale))
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention_noalloc: softmax_scale must be positive");
+    if (batch == 0) return ok();
+    if (!q || !k_cache || !v_cache || !out)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention_noalloc: null pointer");
+    if (!aligned(q, 4) || !aligned(out, 4))
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention_noalloc: q/out misaligned");
+    const size_t need = workspace_bytes_for(batch, num_heads, num_kv_heads, head_dim, max_kv_len);
+    if (need > kNoAllocScratchBytes) {
+        char buf[256];
+        snprintf(buf, sizeof(buf),
+                 "decode_attention_noalloc: this batch needs %zu bytes of split-K scratch but the static "
+                 "scratch holds %zu; use mllm_decode_attention_bf16 with a caller workspace",
+                 need, kNoAllocScratchBytes);
+        return fail(MLLM_ERR_WORKSPACE, buf);
+    }
+    int num_sms = 0;
+    if (int st = require_sm100(&num_sms)) return st;
+    void* scratch = nullptr;
+    if (int st = noalloc_scratch(&scratch)) return st;
+
+    CUtensorMap tmK, tmV;
+    if (int st = encode_kv_map(&tmK, k_cache, head_dim, max_kv_len, num_kv_heads, batch, cache_st, cache_sh, cache_sb,
+                               64, kTile))
+        return st;
+    if (int st = encode_kv_map(&tmV, v_cache, head_dim, max_kv_len, num_kv_heads, batch, cache_st, cache_sh, cache_sb,
+                               64, kTile))
+        return st;
+
+    // Every partial the combine step reads is written earlier in the same call, so the scratch
+    // needs no clearing between calls.
+    DecodeArgs a;
+    a.q = (const __nv_bfloat16*)q;
+    a.kv_lens = kv_lens;
+    a.out = (__nv_bfloat16*)out;
+    a.B = batch;
+    a.H = num_heads;
+    a.Hkv = num_kv_heads;
+    a.n_rep = n_rep;
+    a.max_len = max_kv_len;
+    plan_chunks(batch, num_kv_heads, max_kv_len, num_sms, a.chunk, a.nch);
+    const size_t parts = (size_t)batch * num_kv_heads * a.nch * n_rep;
+    a.part_o = reinterpret_cast<float*>(scratch);
+    a.part_ml = a.part_o + parts * head_dim;
+    a.items = batch * num_kv_heads * a.nch;
+    a.scale_log2 = (float)((double)softmax_scale * 1.4426950408889634);
+
+    const int grid = std::min(a.items, 2 * num_sms);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (head_dim == 128) {
+        const int smem = DecodeCfg<128>::kSmemBytes;
+        if (int st = check_cuda(cudaFuncSetAttribute(decode_split_kernel<128>,
+                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                                "decode smem attribute"))
+            return st;
+        decode_split_kernel<128><<<grid, kThreads, smem, s>>>(tmK, tmV, a);
+        if (int st = check_cuda(cudaGetLastError(), "decode_split_kernel launch")) return st;
+        if (a.nch > 1) decode_combine_kernel<128><<<dim3(num_kv_heads, batch), 128, 0, s>>>(a);
+    } else {
+        const int smem = DecodeCfg<64>::kSmemBytes;
+        if (int st = check_cuda(cudaFuncSetAttribute(decode_split_kernel<64>,
+                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                                "decode smem attribute"))
+            return st;
+        decode_split_kernel<64><<<grid, kThreads, smem, s>>>(tmK, tmV, a);
+        if (int st = check_cuda(cudaGetLastError(), "decode_split_kernel launch")) return st;
+        if (a.nch > 1) decode_combine_kernel<64><<<dim3(num_kv_heads, batch), 128, 0, s>>>(a);
+    }
+    if (int st = check_cuda(cudaGetLastError(), "decode_combine_kernel launch")) return st;
+    return ok();
+}
