@@ -65,7 +65,39 @@ __device__ __forceinline__ float row_sum_squares(const float (&x)[NI], int lane)
     return total;
 }
 
-template <int D>
+// Locates head `head` (q heads first, then k, then v) of token (b, s).
+struct HeadRef {
+    const __nv_bfloat16* src;
+    const __nv_bfloat16* gamma;
+    int kind;  // 0 = q, 1 = k, 2 = v
+    int h;
+};
+
+__device__ __forceinline__ HeadRef locate_head(const EpilogueArgs& a, int head, int b, int s) {
+    HeadRef r;
+    if (head < a.H) {
+        r.kind = 0;
+        r.h = head;
+        r.src = a.q + b * a.q_sb + s * a.q_ss + r.h * a.q_sh;
+        r.gamma = a.q_gamma;
+    } else if (head < a.H + a.Hkv) {
+        r.kind = 1;
+        r.h = head - a.H;
+        r.src = a.k + b * a.k_sb + s * a.k_ss + r.h * a.k_sh;
+        r.gamma = a.k_gamma;
+    } else {
+        r.kind = 2;
+        r.h = head - a.H - a.Hkv;
+        r.src = a.v + b * a.v_sb + s * a.v_ss + r.h * a.v_sh;
+        r.gamma = nullptr;
+    }
+    return r;
+}
+
+// HPW heads per warp.  Every warp issues the loads of all its heads before the block waits
+// for the RoPE angles, so several rows per warp are in flight at once (the kernel is
+// HBM-bound at prefill sizes and latency-bound at decode sizes).
+template <int D, int HPW>
 __global__ void __launch_bounds__(kWarps * 32) qkv_epilogue_kernel(EpilogueArgs a) {
     constexpr int NI = D / 32;     // elements per lane
     constexpr int HALF = D / 2;
@@ -77,6 +109,19 @@ __global__ void __launch_bounds__(kWarps * 32) qkv_epilogue_kernel(EpilogueArgs 
     const int b = token / a.S;
     const int s = token - b * a.S;
     const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int total_heads = a.H + 2 * a.Hkv;
+    const int head0 = (blockIdx.y * kWarps + (tid >> 5)) * HPW;
+
+    float x[HPW][NI];
+#pragma unroll
+    for (int t = 0; t < HPW; ++t) {
+        if (head0 + t < total_heads) {
+            const HeadRef r = locate_head(a, head0 + t, b, s);
+#pragma unroll
+            for (int i = 0; i < NI; ++i) x[t][i] = __bfloat162float(r.src[lane + 32 * i]);
+        }
+    }
 
     // Angles for this token: from the caller's table, or computed (bit-identical to the
     // table that mllm_rope_build_cos_sin would produce for the same position).
@@ -99,75 +144,53 @@ __global__ void __launch_bounds__(kWarps * 32) qkv_epilogue_kernel(EpilogueArgs 
     }
     __syncthreads();
 
-    const int lane = tid & 31;
-    const int head = blockIdx.y * kWarps + (tid >> 5);
-    const int total_heads = a.H + 2 * a.Hkv;
-    if (head >= total_heads) return;
-
-    const __nv_bfloat16* src;
-    const __nv_bfloat16* gamma = nullptr;
-    int kind;  // 0 = q, 1 = k, 2 = v
-    int h;
-    if (head < a.H) {
-        kind = 0;
-        h = head;
-        src = a.q + b * a.q_sb + s * a.q_ss + h * a.q_sh;
-        gamma = a.q_gamma;
-    } else if (head < a.H + a.Hkv) {
-        kind = 1;
-        h = head - a.H;
-        src = a.k + b * a.k_sb + s * a.k_ss + h * a.k_sh;
-        gamma = a.k_gamma;
-    } else {
-        kind = 2;
-        h = head - a.H - a.Hkv;
-        src = a.v + b * a.v_sb + s * a.v_ss + h * a.v_sh;
-    }
-
-    float x[NI];
+    const int64_t slot = (a.cache_start ? (int64_t)a.cache_start[b] : a.uniform_start) + s;
 #pragma unroll
-    for (int i = 0; i < NI; ++i) x[i] = __bfloat162float(src[lane + 32 * i]);
-
-    __nv_bfloat16 y[NI];
-    if (kind == 2) {
+    for (int t = 0; t < HPW; ++t) {
+        if (head0 + t >= total_heads) break;
+        const HeadRef r = locate_head(a, head0 + t, b, s);
+        __nv_bfloat16 y[NI];
+        if (r.kind == 2) {
 #pragma unroll
-        for (int i = 0; i < NI; ++i) y[i] = src[lane + 32 * i];
-    } else {
-        if (gamma != nullptr) {
-            // RMSNorm.h:48-63: var = mean(x^2); x * rsqrt(var + eps) * w; cast to bf16.
-            const float var = __fdiv_rn(row_sum_squares<NI>(x, lane), (float)D);
-            const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));
+            for (int i = 0; i < NI; ++i) y[i] = __float2bfloat16_rn(x[t][i]);   // exact: x came from bf16
+        } else {
+            float xv[NI];
 #pragma unroll
-            for (int i = 0; i < NI; ++i) {
-                const float w = __bfloat162float(gamma[lane + 32 * i]);
-                x[i] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[i], r), w)));
+            for (int i = 0; i < NI; ++i) xv[i] = x[t][i];
+            if (r.gamma != nullptr) {
+                // RMSNorm.h:48-63: var = mean(x^2); x * rsqrt(var + eps) * w; cast to bf16.
+                const float var = __fdiv_rn(row_sum_squares<NI>(xv, lane), (float)D);
+                const float rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));
+#pragma unroll
+                for (int i = 0; i < NI; ++i) {
+                    const float w = __bfloat162float(r.gamma[lane + 32 * i]);
+                    xv[i] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(xv[i], rr), w)));
+                }
+            }
+            // RoPE.h:77-88 on the pairs (d, d + D/2).
+#pragma unroll
+            for (int i = 0; i < PAIR; ++i) {
+                const int j = lane + 32 * i;
+                float lo, hi;
+                rope_rotate_pair(xv[i], xv[i + PAIR], s_cos[j], s_sin[j], s_cos[j + HALF], s_sin[j + HALF], lo, hi);
+                y[i] = __float2bfloat16_rn(lo);
+                y[i + PAIR] = __float2bfloat16_rn(hi);
             }
         }
-        // RoPE.h:77-88 on the pairs (d, d + D/2).
-#pragma unroll
-        for (int i = 0; i < PAIR; ++i) {
-            const int j = lane + 32 * i;
-            float lo, hi;
-            rope_rotate_pair(x[i], x[i + PAIR], s_cos[j], s_sin[j], s_cos[j + HALF], s_sin[j + HALF], lo, hi);
-            y[i] = __float2bfloat16_rn(lo);
-            y[i + PAIR] = __float2bfloat16_rn(hi);
+        __nv_bfloat16* dst;
+        if (r.kind == 0) {
+            dst = a.q_out + (((int64_t)b * a.H + r.h) * a.S + s) * D;
+        } else {
+            if (slot < 0 || slot >= a.capacity) {
+                if (lane == 0) record_error(kErrBadLength);
+                continue;
+            }
+            __nv_bfloat16* base = (r.kind == 1) ? a.k_cache : a.v_cache;
+            dst = base + b * a.c_sb + r.h * a.c_sh + slot * a.c_st;
         }
-    }
-
-    __nv_bfloat16* dst;
-    if (kind == 0) {
-        dst = a.q_out + (((int64_t)b * a.H + h) * a.S + s) * D;
-    } else {
-        const int64_t slot = (a.cache_start ? (int64_t)a.cache_start[b] : a.uniform_start) + s;
-        if (slot < 0 || slot >= a.capacity) {
-            if (lane == 0) record_error(kErrBadLength);
-            return;
-        }
-        __nv_bfloat16* base = (kind == 1) ? a.k_cache : a.v_cache;
-        dst = base + b * a.c_sb + h * a.c_sh + slot * a.c_st;
-    }
 #pragma unroll
-    for (int i = 0; i < NI; ++i) dst[lane + 32 * i] = y[i];
+        for (int i = 0; i < NI; ++i) dst[lane + 32 * i] = y[i];
+    }
 }
 
 }  // namespace
@@ -229,13 +252,21 @@ extern "C" int mllm_qkv_epilogue_bf16(const void* q, int64_t q_sb, int64_t q_ss,
     a.cache_start = cache_start;
     a.uniform_start = uniform_cache_start;
 
+    // Many tokens (prefill): 4 heads per warp keeps 4 rows in flight per warp.  Few tokens
+    // (decode): one head per warp spreads the little work over more SMs.
     const int total_heads = num_heads + 2 * num_kv_heads;
-    dim3 grid((unsigned)(batch * seq_len), (unsigned)((total_heads + kWarps - 1) / kWarps));
+    const int64_t tokens = (int64_t)batch * seq_len;
+    const int hpw = tokens >= 1024 ? 4 : 1;
+    dim3 grid((unsigned)tokens, (unsigned)((total_heads + kWarps * hpw - 1) / (kWarps * hpw)));
     if (grid.y > 65535) return fail(MLLM_ERR_UNSUPPORTED, "qkv_epilogue: too many heads");
-    if (head_dim == 128)
-        qkv_epilogue_kernel<128><<<grid, kWarps * 32, 0, (cudaStream_t)stream>>>(a);
-    else
-        qkv_epilogue_kernel<64><<<grid, kWarps * 32, 0, (cudaStream_t)stream>>>(a);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (head_dim == 128) {
+        if (hpw == 4) qkv_epilogue_kernel<128, 4><<<grid, kWarps * 32, 0, st>>>(a);
+        else qkv_epilogue_kernel<128, 1><<<grid, kWarps * 32, 0, st>>>(a);
+    } else {
+        if (hpw == 4) qkv_epilogue_kernel<64, 4><<<grid, kWarps * 32, 0, st>>>(a);
+        else qkv_epilogue_kernel<64, 1><<<grid, kWarps * 32, 0, st>>>(a);
+    }
     if (int st = check_cuda(cudaGetLastError(), "qkv_epilogue launch")) return st;
     return ok();
 }
