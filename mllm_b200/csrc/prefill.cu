@@ -5,19 +5,24 @@
 // fp32 score tensor in HBM (scores live in tensor memory), no materialised mask (the causal
 // bound is applied per element while the scores are read out of TMEM).
 //
-// One CTA computes one 128-row query tile of one (sequence, query head):
-//   warp 0        TMA producer: Q tile once, then K/V tiles of 128 cache rows into a
-//                 2-stage shared-memory ring (128-byte swizzle, 16-byte-aligned coordinates)
-//   warp 1        TMEM allocator + single-thread MMA issuer:
-//                   S_j = Q K_j^T   tcgen05.mma kind::f16, M=128 N=128, fp32 into TMEM
-//                                   (two S buffers, so S_{j+1} runs while softmax reads S_j)
-//                   O  += P_j V_j   tcgen05.mma, A = P_j from shared memory, B = V (MN-major)
-//   warps 2..5    softmax: thread r owns query row r (TMEM lane r).  Per tile it loads its
-//                 S row with tcgen05.ld, applies scale and the causal bound, runs the online
-//                 softmax in the exp2 domain, rescales the O row in TMEM only when its running
-//                 max grew by more than 2^8 (the stale max is exact: the final 1/l uses it
-//                 too), and writes P_j as bf16 into the swizzled P tile.  At the end it reads
-//                 O from TMEM and writes bf16 O / l straight into [B, S, H*D].
+// One CTA computes TWO 128-row query tiles (256 consecutive rows) of one (sequence, q head);
+// both tiles share every K/V tile the CTA loads.
+//   warp 0        TMA producer: both Q tiles once, then K/V tiles of 128 cache rows into a
+//                 shared-memory ring (128-byte swizzle; innermost coordinates multiples of 64)
+//   warp 1        TMEM allocator + single-thread MMA issuer (tcgen05.mma kind::f16, M=128):
+//                   S_i   = Q_i K_j^T    A, B from shared memory, fp32 into TMEM columns S_i
+//                   O_i  += P_i V_j      A = P_i from TMEM (written over S_i), B = V (MN-major)
+//                 per tile j it issues PV_0(j), S_0(j+1), PV_1(j), S_1(j+1): while one softmax
+//                 group works on its tile, the tensor pipe runs the other tile's products
+//   warps 4-7     softmax of query tile 0, warps 8-11 of tile 1.  Thread r owns row r (TMEM
+//                 lane r).  Pass 1 reads its S row from TMEM for the row max (causal bound
+//                 applied per element on diagonal tiles); the O row is rescaled in TMEM only
+//                 when the max grows by more than 2^8 (the stale max stays exact because the
+//                 final 1/l uses it too); pass 2 re-reads S, forms P = exp2(S*scale - m) in
+//                 bf16 and writes it back over the consumed S columns for the next P.V.
+//                 Seeing S_i(j+1) complete also proves P_i(j) V_j completed (one issuing
+//                 thread, in-order tensor pipe), so O_i may be rescaled without another wait.
+//                 At the end the group reads O from TMEM and writes bf16 O / l into [B,S,H*D].
 // Numerics follow the reference: bf16 Q/K/V, fp32 scores scaled by 1/sqrt(D), fp32
 // softmax, P rounded to bf16 for the P.V product, fp32 accumulation.
 #include <algorithm>
@@ -30,23 +35,23 @@
 namespace mllm_b200 {
 namespace {
 
-constexpr int kBM = 128;            // query rows per CTA
-constexpr int kBN = 128;            // cache rows per tile
-constexpr int kThreads = 192;       // 6 warps
+constexpr int kBM = 128;            // query rows per tile
+constexpr int kQTiles = 2;          // query tiles per CTA
+constexpr int kBN = 128;            // cache rows per K/V tile
+constexpr int kThreads = 384;       // 12 warps: producer, MMA, 2 idle, 2 softmax groups of 4
 constexpr int kBox = kBN * 128;     // one 128-row x 64-column bf16 box (16 KB)
-constexpr uint32_t kTmemCols = 512; // S0 [0,128)  S1 [128,256)  O [256, 256 + D)
+constexpr uint32_t kTmemCols = 512; // S_0 [0,128) S_1 [128,256) O_0 [256,384) O_1 [384,512)
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows > 2^8
 
 template <int D>
 struct PrefillCfg {
     static constexpr int kBoxes = D / 64;
-    static constexpr int kQBytes = kBoxes * kBox;
+    static constexpr int kQBytes = kBoxes * kBox;      // one 128-row Q tile
     static constexpr int kKVBytes = kBoxes * kBox;     // one K (or V) tile
     static constexpr int kStages = (D == 128) ? 2 : 4;
     static constexpr int kStageBytes = 2 * kKVBytes;
-    static constexpr int kPBytes = 2 * kBox;           // 128 rows x 128 bf16 columns
     static constexpr int kBarBytes = 256;
-    static constexpr int kSmemBytes = kQBytes + kStages * kStageBytes + kPBytes + kBarBytes + 1024;
+    static constexpr int kSmemBytes = kQTiles * kQBytes + kStages * kStageBytes + kBarBytes + 1024;
 };
 
 struct PrefillArgs {
@@ -54,6 +59,9 @@ struct PrefillArgs {
     int B, H, Hkv, n_rep, q_len, kv_len, n_mblocks;
     float scale_log2;
 };
+
+__device__ __forceinline__ uint32_t col_s(int i) { return (uint32_t)(i * kBN); }
+__device__ __forceinline__ uint32_t col_o(int i) { return (uint32_t)(2 * kBN + i * 128); }
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -63,29 +71,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int ST = Cfg::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sQ = smem;
-    uint8_t* sKV = sQ + Cfg::kQBytes;
-    uint8_t* sP = sKV + ST * Cfg::kStageBytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + Cfg::kPBytes);
+    uint8_t* sQ = smem;                                  // [kQTiles][kQBytes]
+    uint8_t* sKV = sQ + kQTiles * Cfg::kQBytes;          // [ST][K | V]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + ST * Cfg::kStageBytes);
     uint64_t* q_full = bars;
     uint64_t* kv_full = bars + 1;
     uint64_t* kv_empty = kv_full + ST;
-    uint64_t* s_full = kv_empty + ST;   // [2]
-    uint64_t* s_free = s_full + 2;      // [2]
-    uint64_t* p_full = s_free + 2;
-    uint64_t* pv_done = p_full + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 1);
+    uint64_t* s_full = kv_empty + ST;   // [2]  S_i(j) complete
+    uint64_t* p_full = s_full + 2;      // [2]  P_i(j) written (128 arrivals)
+    uint64_t* o_done = p_full + 2;      // [2]  last P_i V complete
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int mb = a.n_mblocks - 1 - (int)blockIdx.x;  // longest (most causal work) tiles first
+    const int mb = a.n_mblocks - 1 - (int)blockIdx.x;  // longest (most causal work) blocks first
     const int h = blockIdx.y;
     const int b = blockIdx.z;
     const int g = h / a.n_rep;
-    const int m0 = mb * kBM;
-    const int q_last = min(m0 + kBM - 1, a.q_len - 1);
+    const int m0 = mb * (kQTiles * kBM);
     const int pos_offset = a.kv_len - a.q_len;          // absolute position of query row 0
-    const int nb = (pos_offset + q_last) / kBN + 1;     // cache tiles this query tile can see
+    int n_tiles[kQTiles];                                // cache tiles each query tile can see
+#pragma unroll
+    for (int i = 0; i < kQTiles; ++i) {
+        const int r0 = m0 + i * kBM;
+        n_tiles[i] = (r0 < a.q_len) ? (pos_offset + min(r0 + kBM - 1, a.q_len - 1)) / kBN + 1 : 0;
+    }
+    const int n_max = max(n_tiles[0], n_tiles[1]);
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
@@ -95,10 +106,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], 128);
+            mbar_init(&p_full[i], 128);
+            mbar_init(&o_done[i], 1);
         }
-        mbar_init(p_full, 128);
-        mbar_init(pv_done, 1);
         mbar_fence_init();
     }
     if (warp == 1) {
@@ -116,10 +126,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_desc(&tmQ);
             tma_prefetch_desc(&tmK);
             tma_prefetch_desc(&tmV);
-            mbar_arrive_expect_tx(q_full, Cfg::kQBytes);
+            mbar_arrive_expect_tx(q_full, kQTiles * Cfg::kQBytes);
 #pragma unroll
-            for (int bx = 0; bx < Cfg::kBoxes; ++bx) tma_load_4d(sQ + bx * kBox, &tmQ, q_full, bx * 64, m0, h, b);
-            for (int j = 0; j < nb; ++j) {
+            for (int i = 0; i < kQTiles; ++i)
+#pragma unroll
+                for (int bx = 0; bx < Cfg::kBoxes; ++bx)
+                    tma_load_4d(sQ + i * Cfg::kQBytes + bx * kBox, &tmQ, q_full, bx * 64, m0 + i * kBM, h, b);
+            for (int j = 0; j < n_max; ++j) {
                 const int stage = j % ST;
                 if (!mbar_wait(&kv_empty[stage], ((j / ST) & 1) ^ 1)) break;
                 mbar_arrive_expect_tx(&kv_full[stage], Cfg::kStageBytes);
@@ -137,81 +150,86 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             constexpr uint32_t idesc_s = idesc_bf16_f32(kBM, kBN, false);
             constexpr uint32_t idesc_o = idesc_bf16_f32(kBM, D, true);
-            const uint32_t q_addr = smem_u32(sQ);
-            const uint32_t p_addr = smem_u32(sP);
-            bool alive = mbar_wait(q_full, 0);
-            auto issue_s = [&](int j) -> bool {
-                const int stage = j % ST, sb = j & 1;
-                if (!mbar_wait(&kv_full[stage], (j / ST) & 1)) return false;
-                if (!mbar_wait(&s_free[sb], ((j >> 1) & 1) ^ 1)) return false;
-                tc_fence_after();
-                const uint32_t k_addr = smem_u32(sKV + stage * Cfg::kStageBytes);
+            auto issue_s = [&](int i, int j) {
+                const uint32_t q_addr = smem_u32(sQ + i * Cfg::kQBytes);
+                const uint32_t k_addr = smem_u32(sKV + (j % ST) * Cfg::kStageBytes);
 #pragma unroll
                 for (int ks = 0; ks < D / 16; ++ks) {
                     const uint32_t off = (ks >> 2) * kBox + (ks & 3) * 32;
-                    tc_mma_ss(tmem + sb * kBN, smem_desc_sw128(q_addr + off, 16, 1024),
+                    tc_mma_ss(tmem + col_s(i), smem_desc_sw128(q_addr + off, 16, 1024),
                               smem_desc_sw128(k_addr + off, 16, 1024), idesc_s, ks > 0 ? 1u : 0u);
                 }
-                tc_commit(&s_full[sb]);
-                return true;
+                tc_commit(&s_full[i]);
             };
-            if (alive) alive = issue_s(0);
-            for (int j = 0; j < nb && alive; ++j) {
-                if (j + 1 < nb && !issue_s(j + 1)) break;
-                if (!mbar_wait(p_full, j & 1)) break;
+            bool alive = mbar_wait(q_full, 0) && (n_max == 0 || mbar_wait(&kv_full[0], 0));
+            if (alive) {
                 tc_fence_after();
+                for (int i = 0; i < kQTiles; ++i)
+                    if (n_tiles[i] > 0) issue_s(i, 0);
+            }
+            for (int j = 0; j < n_max && alive; ++j) {
                 const int stage = j % ST;
                 const uint32_t v_addr = smem_u32(sKV + stage * Cfg::kStageBytes + Cfg::kKVBytes);
+                bool next_ready = false;
+                for (int i = 0; i < kQTiles && alive; ++i) {
+                    if (j >= n_tiles[i]) continue;
+                    if (!mbar_wait(&p_full[i], j & 1)) { alive = false; break; }
+                    tc_fence_after();
 #pragma unroll
-                for (int ks = 0; ks < kBN / 16; ++ks) {
-                    const uint32_t pa = p_addr + (ks >> 2) * kBox + (ks & 3) * 32;
-                    tc_mma_ss(tmem + 2 * kBN, smem_desc_sw128(pa, 16, 1024),
-                              smem_desc_sw128(v_addr + ks * 16 * 128, kBox, 1024), idesc_o,
-                              (j > 0 || ks > 0) ? 1u : 0u);
+                    for (int ks = 0; ks < kBN / 16; ++ks)
+                        tc_mma_ts(tmem + col_o(i), tmem + col_s(i) + ks * 8,
+                                  smem_desc_sw128(v_addr + ks * 16 * 128, kBox, 1024), idesc_o,
+                                  (j > 0 || ks > 0) ? 1u : 0u);
+                    if (j + 1 < n_tiles[i]) {
+                        if (!next_ready) {
+                            if (!mbar_wait(&kv_full[(j + 1) % ST], ((j + 1) / ST) & 1)) { alive = false; break; }
+                            tc_fence_after();
+                            next_ready = true;
+                        }
+                        issue_s(i, j + 1);   // overwrites P_i(j) only after the P.V above read it
+                    } else {
+                        tc_commit(&o_done[i]);
+                    }
                 }
-                tc_commit(pv_done);
                 // release the stage only if the producer will refill it (no arrival may land
                 // on this CTA's barriers after its last wait)
-                if (j + ST < nb) tc_commit(&kv_empty[stage]);
+                if (alive && j + ST < n_max) tc_commit(&kv_empty[stage]);
             }
         }
-    } else {
+    } else if (warp >= 4) {
         // --------------------------------- softmax ---------------------------------
-        const int quad = warp & 3;
+        const int qt = (warp - 4) >> 2;          // query tile of this warp group
+        const int quad = warp & 3;               // TMEM lane quadrant of this warp
         const int row = quad * 32 + lane;
+        const int n = n_tiles[qt];
         const uint32_t t_lane = tmem + ((uint32_t)(quad * 32) << 16);
-        const int p_row = pos_offset + m0 + row;  // last cache row this query may see
+        const uint32_t t_s = t_lane + col_s(qt);
+        const uint32_t t_o = t_lane + col_o(qt);
+        const int q_row = m0 + qt * kBM + row;
+        const int p_row = pos_offset + q_row;    // last cache row this query may see
+        const int p_tile_min = pos_offset + m0 + qt * kBM;
+        constexpr int kAcc = 8;
         float m_run = -INFINITY, l_run = 0.f;
         bool alive = true;
-        for (int j = 0; j < nb; ++j) {
-            const int sb = j & 1;
-            if (!mbar_wait(&s_full[sb], (j >> 1) & 1)) { alive = false; break; }
+        for (int j = 0; j < n; ++j) {
+            if (!mbar_wait(&s_full[qt], j & 1)) { alive = false; break; }
             tc_fence_after();
-            float s[kBN];
-#pragma unroll
-            for (int c = 0; c < kBN / 32; ++c)
-                tmem_ld32(t_lane + sb * kBN + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
-            tmem_wait_ld();
-            tc_fence_before();
-            mbar_arrive(&s_free[sb]);
-
-            // Causal bound: only tiles reaching past the CTA's first query position need it
-            // (warp-uniform test).  Reductions use 8 independent accumulators so the 128-long
-            // max / sum chains do not serialise on instruction latency.
-            constexpr int kAcc = 8;
+            const bool diag = (j + 1) * kBN - 1 > p_tile_min;   // warp-uniform
+            const int lim = p_row - j * kBN;                     // columns <= lim are visible
+            // pass 1: row max
             float mx[kAcc];
 #pragma unroll
             for (int i = 0; i < kAcc; ++i) mx[i] = -INFINITY;
-            if ((j + 1) * kBN - 1 > pos_offset + m0) {
-                const int lim = p_row - j * kBN;   // columns <= lim are visible
 #pragma unroll
-                for (int c = 0; c < kBN; ++c) {
-                    s[c] = (c <= lim) ? s[c] : -INFINITY;
-                    mx[c % kAcc] = fmaxf(mx[c % kAcc], s[c]);
+            for (int c = 0; c < kBN / 32; ++c) {
+                float sv[32];
+                tmem_ld32(t_s + c * 32, sv);
+                tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const float v = (diag && c * 32 + e > lim) ? -INFINITY : sv[e];
+                    mx[e % kAcc] = fmaxf(mx[e % kAcc], v);
                 }
-            } else {
-#pragma unroll
-                for (int c = 0; c < kBN; ++c) mx[c % kAcc] = fmaxf(mx[c % kAcc], s[c]);
             }
 #pragma unroll
             for (int w = kAcc / 2; w >= 1; w >>= 1)
@@ -223,63 +241,62 @@ __global__ void __launch_bounds__(kThreads, 1)
             float m_use = grow ? m_new : m_run;
             if (m_use == -INFINITY) m_use = 0.f;
             const float alpha = grow ? ex2_approx(m_run - m_use) : 1.f;
+            if (j > 0 && __any_sync(0xffffffffu, grow)) {
+                // P_i(j-1) V_{j-1} is complete (S_i(j) completed after it): rescale O in place.
+#pragma unroll
+                for (int c = 0; c < D / 32; ++c) {
+                    float o[32];
+                    tmem_ld32(t_o + c * 32, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) o[e] *= alpha;
+                    tmem_st32(t_o + c * 32, o);
+                }
+            }
+            // pass 2: P = exp2(S * scale - m) as bf16, written over the consumed S columns
             const float neg_m = -m_use;
             float sum[kAcc];
 #pragma unroll
             for (int i = 0; i < kAcc; ++i) sum[i] = 0.f;
 #pragma unroll
-            for (int c = 0; c < kBN; ++c) {
-                s[c] = ex2_approx(fmaf(s[c], a.scale_log2, neg_m));
-                sum[c % kAcc] += s[c];
+            for (int c = 0; c < kBN / 32; ++c) {
+                float sv[32];
+                tmem_ld32(t_s + c * 32, sv);
+                tmem_wait_ld();
+                uint32_t pk[16];
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    float p0 = ex2_approx(fmaf(sv[e], a.scale_log2, neg_m));
+                    float p1 = ex2_approx(fmaf(sv[e + 1], a.scale_log2, neg_m));
+                    if (diag) {
+                        if (c * 32 + e > lim) p0 = 0.f;
+                        if (c * 32 + e + 1 > lim) p1 = 0.f;
+                    }
+                    sum[e % kAcc] += p0;
+                    sum[(e + 1) % kAcc] += p1;
+                    pk[e >> 1] = pack_bf16x2(p0, p1);
+                }
+                tmem_st16(t_s + c * 16, pk);
             }
+            tmem_wait_st();
 #pragma unroll
             for (int w = kAcc / 2; w >= 1; w >>= 1)
 #pragma unroll
                 for (int i = 0; i < w; ++i) sum[i] += sum[i + w];
             l_run = l_run * alpha + sum[0];
             m_run = m_use;
-
-            if (j > 0) {
-                // P buffer and O are still in use by P_{j-1} V_{j-1} until it completes.
-                if (!mbar_wait(pv_done, (j - 1) & 1)) { alive = false; break; }
-                tc_fence_after();
-                if (__any_sync(0xffffffffu, grow)) {
-#pragma unroll
-                    for (int c = 0; c < D / 32; ++c) {
-                        float o[32];
-                        tmem_ld32(t_lane + 2 * kBN + c * 32, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                        tmem_st32(t_lane + 2 * kBN + c * 32, o);
-                    }
-                    tmem_wait_st();
-                }
-            }
-            // P row -> swizzled K-major tile (two 64-column boxes)
-#pragma unroll
-            for (int cc = 0; cc < kBN / 8; ++cc) {
-                uint4 v;
-                v.x = pack_bf16x2(s[cc * 8 + 0], s[cc * 8 + 1]);
-                v.y = pack_bf16x2(s[cc * 8 + 2], s[cc * 8 + 3]);
-                v.z = pack_bf16x2(s[cc * 8 + 4], s[cc * 8 + 5]);
-                v.w = pack_bf16x2(s[cc * 8 + 6], s[cc * 8 + 7]);
-                *reinterpret_cast<uint4*>(sP + (cc >> 3) * kBox + swz128(row, cc & 7)) = v;
-            }
-            fence_proxy_async_smem();
             tc_fence_before();
-            mbar_arrive(p_full);
+            mbar_arrive(&p_full[qt]);
         }
-        if (alive && mbar_wait(pv_done, (nb - 1) & 1)) {
+        if (n > 0 && alive && mbar_wait(&o_done[qt], 0)) {
             tc_fence_after();
             const float inv_l = 1.f / l_run;
-            const bool valid = (m0 + row) < a.q_len;
-            __nv_bfloat16* orow =
-                a.out + (((int64_t)b * a.q_len + (m0 + row)) * a.H + h) * (int64_t)D;
+            const bool valid = q_row < a.q_len;
+            __nv_bfloat16* orow = a.out + (((int64_t)b * a.q_len + q_row) * a.H + h) * (int64_t)D;
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
                 float o[32];
-                tmem_ld32(t_lane + 2 * kBN + c * 32, o);
+                tmem_ld32(t_o + c * 32, o);
                 tmem_wait_ld();
                 if (valid) {
 #pragma unroll
@@ -347,7 +364,7 @@ extern "C" int mllm_prefill_attention_bf16(const void* q, const void* k_cache, c
     a.n_rep = num_heads / num_kv_heads;
     a.q_len = q_len;
     a.kv_len = kv_len;
-    a.n_mblocks = (q_len + kBM - 1) / kBM;
+    a.n_mblocks = (q_len + kQTiles * kBM - 1) / (kQTiles * kBM);
     a.scale_log2 = (float)((double)softmax_scale * 1.4426950408889634);
     dim3 grid(a.n_mblocks, num_heads, batch);
     cudaStream_t s = (cudaStream_t)stream;
