@@ -2,9 +2,9 @@
 
     python -m mllm_b200.build [--force] [--verbose]
 
-Every .cu file under mllm_b200/csrc is compiled with nvcc for sm_100a (relocatable device
-code, so the device status word is shared across translation units) and linked into one
-shared library with the CUDA runtime linked statically.  The library exports only the
+Every .cu file under mllm_b200/csrc is compiled with nvcc for sm_100a (whole-program device
+code per file: no relocatable device code, which would make ptxas ignore setmaxnreg) and
+linked into one shared library with the CUDA runtime linked statically.  The library exports only the
 extern "C" entry points declared in include/mllm_attn.h.
 """
 from __future__ import annotations
@@ -23,7 +23,7 @@ LIB_DIR = os.path.join(PKG, "lib")
 OBJ_DIR = os.path.join(PKG, "_build")
 LIB_NAME = "libmllm_attn.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-rdc=true", "-Xcompiler", "-fPIC", "-Xcompiler",
+NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler",
               "-fvisibility=hidden", "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
 
 
@@ -73,7 +73,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
         subprocess.run(cmd, check=True)
         objs.append(obj)
     tmp = out + ".tmp"
-    cmd = [cc, *ARCH, "-shared", "-rdc=true", "-cudart", "static", *objs, "-o", tmp,
+    cmd = [cc, *ARCH, "-shared", "-cudart", "static", *objs, "-o", tmp,
            "-Xcompiler", "-fPIC", "-Xlinker", "--exclude-libs,ALL"]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)

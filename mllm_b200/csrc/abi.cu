@@ -11,8 +11,6 @@
 
 namespace mllm_b200 {
 
-__device__ unsigned g_device_status = 0u;
-
 namespace {
 thread_local std::string t_last_error;
 
@@ -125,16 +123,16 @@ extern "C" const char* mllm_attn_last_error(void) { return t_last_error.c_str();
 
 extern "C" int mllm_attn_device_status(mllm_stream_t stream) {
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    unsigned v = 0, zero = 0;
-    int st = check_cuda(cudaMemcpyFromSymbolAsync(&v, g_device_status, sizeof(v), 0, cudaMemcpyDeviceToHost, s),
-                        "read device status");
-    if (st) return st;
-    st = check_cuda(cudaMemcpyToSymbolAsync(g_device_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s),
-                    "clear device status");
-    if (st) return st;
-    st = check_cuda(cudaStreamSynchronize(s), "synchronize");
-    if (st) return st;
-    if (v & kErrTimeout) return fail(MLLM_ERR_DEVICE_TIMEOUT, "a kernel's bounded wait expired");
-    if (v & kErrBadLength) return fail(MLLM_ERR_DEVICE_LENGTH, "a device-side length exceeded its capacity");
+    unsigned v[3] = {0u, 0u, 0u};
+    int (*readers[3])(cudaStream_t, unsigned*) = {read_clear_status_decode, read_clear_status_prefill,
+                                                   read_clear_status_epilogue};
+    for (int i = 0; i < 3; ++i) {
+        const int e = readers[i](s, &v[i]);
+        if (e != 0) return check_cuda((cudaError_t)e, "read device status");
+    }
+    if (int st = check_cuda(cudaStreamSynchronize(s), "synchronize")) return st;
+    const unsigned all = v[0] | v[1] | v[2];
+    if (all & kErrTimeout) return fail(MLLM_ERR_DEVICE_TIMEOUT, "a kernel's bounded wait expired");
+    if (all & kErrBadLength) return fail(MLLM_ERR_DEVICE_LENGTH, "a device-side length exceeded its capacity");
     return ok();
 }

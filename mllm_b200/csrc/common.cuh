@@ -19,17 +19,31 @@
 namespace mllm_b200 {
 
 // ---------------------------------------------------------------------------------------
-// Device status word (one per device, lives in this library's module).  Kernels OR error
-// bits into it; the host reads and clears it through mllm_attn_device_status().
+// Device status words.  Every translation unit that includes this header owns one (internal
+// linkage, so the library needs no relocatable device code); kernels OR error bits into it and
+// the host reads and clears all of them through mllm_attn_device_status().
 // ---------------------------------------------------------------------------------------
 enum DeviceError : unsigned {
     kErrNone = 0u,
     kErrTimeout = 1u,       // a bounded wait ran out (pipeline logic error)
     kErrBadLength = 2u,     // a device-side length exceeded the capacity given by the host
 };
-extern __device__ unsigned g_device_status;
+static __device__ unsigned g_tu_status = 0u;
 
-__device__ __forceinline__ void record_error(unsigned bits) { atomicOr(&g_device_status, bits); }
+__device__ __forceinline__ void record_error(unsigned bits) { atomicOr(&g_tu_status, bits); }
+
+// Defines `int read_clear_status_<name>(cudaStream_t, unsigned*)`: copies this translation
+// unit's status word to the host and clears it, in stream order (the caller synchronises).
+#define MLLM_DEFINE_STATUS_READER(name)                                                             \
+    int read_clear_status_##name(cudaStream_t s, unsigned* out) {                                   \
+        static const unsigned zero = 0u;                                                            \
+        cudaError_t e = cudaMemcpyFromSymbolAsync(out, g_tu_status, sizeof(unsigned), 0,            \
+                                                  cudaMemcpyDeviceToHost, s);                       \
+        if (e == cudaSuccess)                                                                       \
+            e = cudaMemcpyToSymbolAsync(g_tu_status, &zero, sizeof(unsigned), 0,                    \
+                                        cudaMemcpyHostToDevice, s);                                 \
+        return e == cudaSuccess ? 0 : (int)e;                                                       \
+    }
 
 // ~1 s at B200 clocks with the nanosleep back-off below.
 constexpr uint32_t kSpinLimit = 1u << 22;

@@ -381,6 +381,9 @@ size_t workspace_bytes_for(int B, int H, int Hkv, int D, int max_len) {
 }
 
 }  // namespace
+
+MLLM_DEFINE_STATUS_READER(decode)
+
 }  // namespace mllm_b200
 
 using namespace mllm_b200;

@@ -25,6 +25,11 @@ int require_sm100(int* num_sms = nullptr);
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Per-translation-unit device status readers (see MLLM_DEFINE_STATUS_READER).
+int read_clear_status_decode(cudaStream_t s, unsigned* out);
+int read_clear_status_prefill(cudaStream_t s, unsigned* out);
+int read_clear_status_epilogue(cudaStream_t s, unsigned* out);
+
 // Encodes a 4-D bf16 tensor map {d (inner), rows, heads, batch} with 128-byte swizzle and a
 // {box_d, box_rows, 1, 1} box.  Strides are in elements.  Returns MLLM_OK or an error.
 int encode_kv_map(CUtensorMap* map, const void* base, int64_t d, int64_t rows, int64_t heads, int64_t batch,

@@ -14,12 +14,14 @@
 //                   O_i  += P_i V_j      A = P_i from TMEM (written over S_i), B = V (MN-major)
 //                 per tile j it issues PV_0(j), S_0(j+1), PV_1(j), S_1(j+1): while one softmax
 //                 group works on its tile, the tensor pipe runs the other tile's products
-//   warps 4-7     softmax of query tile 0, warps 8-11 of tile 1.  Thread r owns row r (TMEM
-//                 lane r).  Pass 1 reads its S row from TMEM for the row max (causal bound
-//                 applied per element on diagonal tiles); the O row is rescaled in TMEM only
-//                 when the max grows by more than 2^8 (the stale max stays exact because the
-//                 final 1/l uses it too); pass 2 re-reads S, forms P = exp2(S*scale - m) in
-//                 bf16 and writes it back over the consumed S columns for the next P.V.
+//   warps 4-7     softmax of query tile 0, warps 8-11 of tile 1 (warp w reaches TMEM lanes
+//                 32*(w%4)..+31); they run with 224 registers each (setmaxnreg).  Thread r
+//                 owns row r: it loads its 128 scores from TMEM with back-to-back loads and a
+//                 single wait, takes the row max (causal bound applied
+//                 per element on diagonal tiles), rescales the O row in TMEM only when the max
+//                 grows by more than 2^8 (the stale max stays exact because the final 1/l uses
+//                 it too), forms P = exp2(S*scale - m) in bf16 and writes it back over the
+//                 consumed S columns for the next P.V.
 //                 Seeing S_i(j+1) complete also proves P_i(j) V_j completed (one issuing
 //                 thread, in-order tensor pipe), so O_i may be rescaled without another wait.
 //                 At the end the group reads O from TMEM and writes bf16 O / l into [B,S,H*D].
@@ -38,7 +40,16 @@ namespace {
 constexpr int kBM = 128;            // query rows per tile
 constexpr int kQTiles = 2;          // query tiles per CTA
 constexpr int kBN = 128;            // cache rows per K/V tile
-constexpr int kThreads = 384;       // 12 warps: producer, MMA, 2 idle, 2 softmax groups of 4
+constexpr int kThreads = 384;       // 3 warpgroups: {producer, MMA, 2 idle}, softmax tile 0, tile 1
+// Register split (setmaxnreg): the kernel launches at 168 registers per thread (384 x 168 =
+// 64,512, three warps per SM sub-partition).  The producer/MMA warpgroup gives registers back
+// and the two softmax warpgroups take them: 128 x 56 + 256 x 224 = 64,512, and per sub-partition
+// 56 + 224 + 224 = 504 = 3 x 168, so the increase can always be satisfied.
+constexpr uint32_t kLaunchRegs = 168;
+constexpr uint32_t kLowRegs = 56;
+constexpr uint32_t kHighRegs = 224;
+static_assert(128 * kLowRegs + 256 * kHighRegs <= kThreads * kLaunchRegs, "register split exceeds the launch");
+static_assert(kLowRegs + 2 * kHighRegs <= 3 * kLaunchRegs, "register split exceeds a sub-partition");
 constexpr int kBox = kBN * 128;     // one 128-row x 64-column bf16 box (16 KB)
 constexpr uint32_t kTmemCols = 512; // S_0 [0,128) S_1 [128,256) O_0 [256,384) O_1 [384,512)
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows > 2^8
@@ -119,8 +130,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-
-    if (warp == 0) {
+    // Each role's code sits inside the branch that sets its register budget, so the compiler
+    // allocates every region with the budget it actually runs under.
+    if (warp < 4) {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kLowRegs));
+      if (warp == 0) {
         // ------------------------------- TMA producer -------------------------------
         if (lane == 0) {
             tma_prefetch_desc(&tmQ);
@@ -145,19 +159,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-    } else if (warp == 1) {
+      } else if (warp == 1) {
         // ------------------------------- MMA issuer -------------------------------
         if (lane == 0) {
             constexpr uint32_t idesc_s = idesc_bf16_f32(kBM, kBN, false);
             constexpr uint32_t idesc_o = idesc_bf16_f32(kBM, D, true);
+            // Descriptors differ only in their start-address field (bits 0..13, in 16-byte
+            // units), so each k-step adds the byte offset >> 4 to a base descriptor.
             auto issue_s = [&](int i, int j) {
-                const uint32_t q_addr = smem_u32(sQ + i * Cfg::kQBytes);
-                const uint32_t k_addr = smem_u32(sKV + (j % ST) * Cfg::kStageBytes);
-#pragma unroll
+                const uint64_t qd = smem_desc_sw128(smem_u32(sQ + i * Cfg::kQBytes), 16, 1024);
+                const uint64_t kd = smem_desc_sw128(smem_u32(sKV + (j % ST) * Cfg::kStageBytes), 16, 1024);
+#pragma unroll 1
                 for (int ks = 0; ks < D / 16; ++ks) {
-                    const uint32_t off = (ks >> 2) * kBox + (ks & 3) * 32;
-                    tc_mma_ss(tmem + col_s(i), smem_desc_sw128(q_addr + off, 16, 1024),
-                              smem_desc_sw128(k_addr + off, 16, 1024), idesc_s, ks > 0 ? 1u : 0u);
+                    const uint64_t off = (uint64_t)(((ks >> 2) * kBox + (ks & 3) * 32) >> 4);
+                    tc_mma_ss(tmem + col_s(i), qd + off, kd + off, idesc_s, ks > 0 ? 1u : 0u);
                 }
                 tc_commit(&s_full[i]);
             };
@@ -175,11 +190,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (j >= n_tiles[i]) continue;
                     if (!mbar_wait(&p_full[i], j & 1)) { alive = false; break; }
                     tc_fence_after();
-#pragma unroll
+                    const uint64_t vd = smem_desc_sw128(v_addr, kBox, 1024);
+#pragma unroll 1
                     for (int ks = 0; ks < kBN / 16; ++ks)
-                        tc_mma_ts(tmem + col_o(i), tmem + col_s(i) + ks * 8,
-                                  smem_desc_sw128(v_addr + ks * 16 * 128, kBox, 1024), idesc_o,
-                                  (j > 0 || ks > 0) ? 1u : 0u);
+                        tc_mma_ts(tmem + col_o(i), tmem + col_s(i) + ks * 8, vd + (uint64_t)((ks * 16 * 128) >> 4),
+                                  idesc_o, (j > 0 || ks > 0) ? 1u : 0u);
                     if (j + 1 < n_tiles[i]) {
                         if (!next_ready) {
                             if (!mbar_wait(&kv_full[(j + 1) % ST], ((j + 1) / ST) & 1)) { alive = false; break; }
@@ -196,7 +211,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (alive && j + ST < n_max) tc_commit(&kv_empty[stage]);
             }
         }
-    } else if (warp >= 4) {
+      }
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kHighRegs));
         // --------------------------------- softmax ---------------------------------
         const int qt = (warp - 4) >> 2;          // query tile of this warp group
         const int quad = warp & 3;               // TMEM lane quadrant of this warp
@@ -214,23 +231,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < n; ++j) {
             if (!mbar_wait(&s_full[qt], j & 1)) { alive = false; break; }
             tc_fence_after();
-            const bool diag = (j + 1) * kBN - 1 > p_tile_min;   // warp-uniform
-            const int lim = p_row - j * kBN;                     // columns <= lim are visible
-            // pass 1: row max
+            float sv[kBN];
+#pragma unroll
+            for (int c = 0; c < kBN / 32; ++c)
+                tmem_ld32(t_s + c * 32, *reinterpret_cast<float(*)[32]>(&sv[c * 32]));
+            tmem_wait_ld();
+            if ((j + 1) * kBN - 1 > p_tile_min) {   // diagonal tile (warp-uniform): causal bound
+                const int lim = p_row - j * kBN;     // columns <= lim are visible
+#pragma unroll
+                for (int c = 0; c < kBN; ++c) sv[c] = (c <= lim) ? sv[c] : -INFINITY;
+            }
             float mx[kAcc];
 #pragma unroll
-            for (int i = 0; i < kAcc; ++i) mx[i] = -INFINITY;
+            for (int i = 0; i < kAcc; ++i) mx[i] = sv[i];
 #pragma unroll
-            for (int c = 0; c < kBN / 32; ++c) {
-                float sv[32];
-                tmem_ld32(t_s + c * 32, sv);
-                tmem_wait_ld();
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const float v = (diag && c * 32 + e > lim) ? -INFINITY : sv[e];
-                    mx[e % kAcc] = fmaxf(mx[e % kAcc], v);
-                }
-            }
+            for (int c = kAcc; c < kBN; ++c) mx[c % kAcc] = fmaxf(mx[c % kAcc], sv[c]);
 #pragma unroll
             for (int w = kAcc / 2; w >= 1; w >>= 1)
 #pragma unroll
@@ -253,25 +268,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_st32(t_o + c * 32, o);
                 }
             }
-            // pass 2: P = exp2(S * scale - m) as bf16, written over the consumed S columns
+            // P = exp2(S * scale - m) in bf16, written over the consumed S columns
             const float neg_m = -m_use;
             float sum[kAcc];
 #pragma unroll
             for (int i = 0; i < kAcc; ++i) sum[i] = 0.f;
 #pragma unroll
             for (int c = 0; c < kBN / 32; ++c) {
-                float sv[32];
-                tmem_ld32(t_s + c * 32, sv);
-                tmem_wait_ld();
                 uint32_t pk[16];
 #pragma unroll
                 for (int e = 0; e < 32; e += 2) {
-                    float p0 = ex2_approx(fmaf(sv[e], a.scale_log2, neg_m));
-                    float p1 = ex2_approx(fmaf(sv[e + 1], a.scale_log2, neg_m));
-                    if (diag) {
-                        if (c * 32 + e > lim) p0 = 0.f;
-                        if (c * 32 + e + 1 > lim) p1 = 0.f;
-                    }
+                    const float p0 = ex2_approx(fmaf(sv[c * 32 + e], a.scale_log2, neg_m));
+                    const float p1 = ex2_approx(fmaf(sv[c * 32 + e + 1], a.scale_log2, neg_m));
                     sum[e % kAcc] += p0;
                     sum[(e + 1) % kAcc] += p1;
                     pk[e >> 1] = pack_bf16x2(p0, p1);
@@ -322,6 +330,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 }  // namespace
+
+MLLM_DEFINE_STATUS_READER(prefill)
+
 }  // namespace mllm_b200
 
 using namespace mllm_b200;
@@ -368,6 +379,24 @@ extern "C" int mllm_prefill_attention_bf16(const void* q, const void* k_cache, c
     a.scale_log2 = (float)((double)softmax_scale * 1.4426950408889634);
     dim3 grid(a.n_mblocks, num_heads, batch);
     cudaStream_t s = (cudaStream_t)stream;
+    // The kernel moves registers between warpgroups with setmaxnreg; that is only safe if the
+    // compiled kernel launches with the register count the split was sized for (otherwise the
+    // increase could never be satisfied).  Checked once per kernel.
+    auto check_regs = [](const void* fn) -> int {
+        cudaFuncAttributes attr;
+        if (int st = check_cuda(cudaFuncGetAttributes(&attr, fn), "prefill attributes")) return st;
+        if ((uint32_t)attr.numRegs < kLaunchRegs)
+            return fail(MLLM_ERR_UNSUPPORTED, "prefill_kernel compiled with fewer registers than its register split needs");
+        return MLLM_OK;
+    };
+    static int regs_ok_128 = -1, regs_ok_64 = -1;
+    if (head_dim == 128) {
+        if (regs_ok_128 < 0) regs_ok_128 = check_regs((const void*)prefill_kernel<128>);
+        if (regs_ok_128 != MLLM_OK) return fail(regs_ok_128, "prefill_kernel<128>: register split check failed");
+    } else {
+        if (regs_ok_64 < 0) regs_ok_64 = check_regs((const void*)prefill_kernel<64>);
+        if (regs_ok_64 != MLLM_OK) return fail(regs_ok_64, "prefill_kernel<64>: register split check failed");
+    }
     if (head_dim == 128) {
         const int smem = PrefillCfg<128>::kSmemBytes;
         if (int st = check_cuda(cudaFuncSetAttribute(prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,

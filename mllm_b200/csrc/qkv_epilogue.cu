@@ -194,6 +194,9 @@ __global__ void __launch_bounds__(kWarps * 32) qkv_epilogue_kernel(EpilogueArgs 
 }
 
 }  // namespace
+
+MLLM_DEFINE_STATUS_READER(epilogue)
+
 }  // namespace mllm_b200
 
 using namespace mllm_b200;
