@@ -98,12 +98,14 @@ __device__ __forceinline__ HeadRef locate_head(const EpilogueArgs& a, int head, 
 // for the RoPE angles, so several rows per warp are in flight at once (the kernel is
 // HBM-bound at prefill sizes and latency-bound at decode sizes).
 template <int D, int HPW>
-__global__ void __launch_bounds__(kWarps * 32) qkv_epilogue_kernel(EpilogueArgs a) {
+__global__ void __launch_bounds__(kWarps * 32, 6) qkv_epilogue_kernel(EpilogueArgs a) {
     constexpr int NI = D / 32;     // elements per lane
     constexpr int HALF = D / 2;
     constexpr int PAIR = NI / 2;   // slot i pairs with slot i + PAIR (distance D/2)
     __shared__ float s_cos[D];
     __shared__ float s_sin[D];
+    __shared__ float s_gamma[2][D];   // q / k per-head norm weights (fp32 copies of the bf16 values)
+    __shared__ int64_t s_slot;
 
     const int token = blockIdx.x;
     const int b = token / a.S;
@@ -123,6 +125,15 @@ __global__ void __launch_bounds__(kWarps * 32) qkv_epilogue_kernel(EpilogueArgs 
         }
     }
 
+    // Everything the per-head work needs besides its own row is staged once per block, while
+    // the row loads above are in flight: norm weights, the cache slot and the RoPE angles.
+    if (a.q_gamma != nullptr) {
+        for (int d = tid; d < D; d += blockDim.x) {
+            s_gamma[0][d] = __bfloat162float(a.q_gamma[d]);
+            s_gamma[1][d] = __bfloat162float(a.k_gamma[d]);
+        }
+    }
+    if (tid == 0) s_slot = (a.cache_start ? (int64_t)a.cache_start[b] : a.uniform_start) + s;
     // Angles for this token: from the caller's table, or computed (bit-identical to the
     // table that mllm_rope_build_cos_sin would produce for the same position).
     if (a.rope_cos != nullptr) {
@@ -144,7 +155,7 @@ __global__ void __launch_bounds__(kWarps * 32) qkv_epilogue_kernel(EpilogueArgs 
     }
     __syncthreads();
 
-    const int64_t slot = (a.cache_start ? (int64_t)a.cache_start[b] : a.uniform_start) + s;
+    const int64_t slot = s_slot;
 #pragma unroll
     for (int t = 0; t < HPW; ++t) {
         if (head0 + t >= total_heads) break;
@@ -161,9 +172,10 @@ __global__ void __launch_bounds__(kWarps * 32) qkv_epilogue_kernel(EpilogueArgs 
                 // RMSNorm.h:48-63: var = mean(x^2); x * rsqrt(var + eps) * w; cast to bf16.
                 const float var = __fdiv_rn(row_sum_squares<NI>(xv, lane), (float)D);
                 const float rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));
+                const float* gw = s_gamma[r.kind];
 #pragma unroll
                 for (int i = 0; i < NI; ++i) {
-                    const float w = __bfloat162float(r.gamma[lane + 32 * i]);
+                    const float w = gw[lane + 32 * i];
                     xv[i] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(xv[i], rr), w)));
                 }
             }
