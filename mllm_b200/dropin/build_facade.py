@@ -71,6 +71,67 @@ def check_runners(reference: str = REFERENCE, verbose: bool = False) -> list[str
     return outs
 
 
+RUNNER_SOURCES = ["models/qwen/QwenRunner.cpp", "models/llama/LlamaRunner.cpp", "core/runtime/Sampler.cpp",
+                  "tokenizer/BpeTokenizer.cpp", "tokenizer/LlamaTokenizer.cpp", "tokenizer/QwenTokenizer.cpp",
+                  "tokenizer/TokenizerJsonLoader.cpp"]
+
+
+def runner_module_path(flavor: str) -> str:
+    ext = sysconfig.get_config_var("EXT_SUFFIX")
+    if flavor == "reference":
+        return os.path.join(ROOT, "oracle", "_ref", "mllm_ref_runner" + ext)
+    return os.path.join(ROOT, "tests", "facade", "mllm_dropin_runner" + ext)
+
+
+def build_runner_module(flavor: str, reference: str = REFERENCE, verbose: bool = False, force: bool = False) -> str:
+    """Compile tests/facade/runner_binding.cpp with the reference's unchanged runners, either
+    against the reference's own runtime headers ("reference") or with the drop-in headers
+    first ("dropin").  Returns the module path."""
+    import concurrent.futures as cf
+    assert flavor in ("reference", "dropin")
+    if not os.path.isdir(os.path.join(reference, "src", "models")):
+        raise FileNotFoundError("reference tree not present")
+    out = runner_module_path(flavor)
+    binding = os.path.join(ROOT, "tests", "facade", "runner_binding.cpp")
+    deps = [binding] + ([os.path.join(HERE, "core", "runtime", f) for f in os.listdir(os.path.join(HERE, "core", "runtime"))]
+                        if flavor == "dropin" else [])
+    if not force and os.path.exists(out) and all(os.path.getmtime(d) <= os.path.getmtime(out) for d in deps):
+        return out
+    inc, libs, defs = _torch_flags()
+    if flavor == "dropin":
+        from mllm_b200 import build as libbuild
+        lib = libbuild.build()
+        incs = include_flags(reference)
+        extra = [f"-L{os.path.dirname(lib)}", "-Wl,-rpath,$ORIGIN/../../mllm_b200/lib", "-lmllm_attn"]
+    else:
+        incs = [f"-I{_shim(reference)}", f"-I{os.path.join(reference, 'src')}",
+                f"-I{os.path.join(reference, 'external')}"]
+        extra = []
+    obj_dir = os.path.join(BUILD, "runner_" + flavor)
+    os.makedirs(obj_dir, exist_ok=True)
+    os.makedirs(os.path.dirname(out), exist_ok=True)
+    srcs = [binding] + [os.path.join(reference, "src", s) for s in RUNNER_SOURCES]
+    cflags = ["g++", "-std=c++17", "-O2", "-fPIC", "-w", *defs, "-DTORCH_EXTENSION_NAME=" + os.path.basename(out).split(".")[0],
+              f"-I{sysconfig.get_paths()['include']}", *incs, *inc]
+
+    def compile_one(src):
+        obj = os.path.join(obj_dir, os.path.basename(src).replace(".cpp", ".o"))
+        cmd = cflags + ["-c", src, "-o", obj]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        subprocess.run(cmd, check=True)
+        return obj
+
+    with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
+        objs = list(ex.map(compile_one, srcs))
+    cmd = ["g++", "-shared", "-fPIC", *objs, "-o", out, *libs, *extra,
+           "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-lc10", "-lc10_cuda", "-ltorch_python"]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    subprocess.run(cmd, check=True)
+    return out
+
+
 def build_facade_module(reference: str = REFERENCE, verbose: bool = False) -> str:
     from mllm_b200 import build as libbuild
     lib = libbuild.build()
@@ -90,4 +151,5 @@ def build_facade_module(reference: str = REFERENCE, verbose: bool = False) -> st
 
 if __name__ == "__main__":
     print(check_runners(verbose=True))
-    print(build_facade_module(verbose=True))
+    for fl in ("reference", "dropin"):
+        print(build_runner_module(fl, verbose=True))

@@ -1,0 +1,83 @@
+"""Random-init Qwen3-architecture checkpoints in the HuggingFace layout the mLLM runners load
+(config.json + model.safetensors, tensor names of QwenRunner::LoadAllWeights).  Test helper:
+the tests and the end-to-end generation bench write one into a temporary directory on the GPU
+machine, then load it with both the reference runner and the drop-in runner."""
+from __future__ import annotations
+
+import json
+import os
+import struct
+from dataclasses import dataclass
+
+import numpy as np
+
+
+@dataclass(frozen=True)
+class QwenShape:
+    layers: int
+    hidden: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    intermediate: int
+    vocab: int
+    rope_theta: float = 1e6
+    eps: float = 1e-6
+
+
+QWEN3_8B = QwenShape(layers=36, hidden=4096, heads=32, kv_heads=8, head_dim=128, intermediate=12288, vocab=151936)
+
+
+def _tensor_names(s: QwenShape):
+    names = [("model.embed_tokens.weight", (s.vocab, s.hidden)), ("model.norm.weight", (s.hidden,)),
+             ("lm_head.weight", (s.vocab, s.hidden))]
+    for i in range(s.layers):
+        p = f"model.layers.{i}"
+        names += [
+            (f"{p}.input_layernorm.weight", (s.hidden,)),
+            (f"{p}.post_attention_layernorm.weight", (s.hidden,)),
+            (f"{p}.self_attn.q_proj.weight", (s.heads * s.head_dim, s.hidden)),
+            (f"{p}.self_attn.k_proj.weight", (s.kv_heads * s.head_dim, s.hidden)),
+            (f"{p}.self_attn.v_proj.weight", (s.kv_heads * s.head_dim, s.hidden)),
+            (f"{p}.self_attn.o_proj.weight", (s.hidden, s.heads * s.head_dim)),
+            (f"{p}.self_attn.q_norm.weight", (s.head_dim,)),
+            (f"{p}.self_attn.k_norm.weight", (s.head_dim,)),
+            (f"{p}.mlp.gate_proj.weight", (s.intermediate, s.hidden)),
+            (f"{p}.mlp.up_proj.weight", (s.intermediate, s.hidden)),
+            (f"{p}.mlp.down_proj.weight", (s.hidden, s.intermediate)),
+        ]
+    return names
+
+
+def write_random_qwen3(path: str, s: QwenShape, seed: int = 0, device: str = "cuda") -> None:
+    """Weights N(0, 0.02) (norm weights 1 + N(0, 0.1)), bf16, generated with torch on `device`
+    (a seeded torch generator) and streamed to model.safetensors tensor by tensor."""
+    import torch
+    os.makedirs(path, exist_ok=True)
+    cfg = {"model_type": "qwen3", "_name_or_path": "random-qwen3", "hidden_size": s.hidden,
+           "num_hidden_layers": s.layers, "num_attention_heads": s.heads, "num_key_value_heads": s.kv_heads,
+           "head_dim": s.head_dim, "intermediate_size": s.intermediate, "vocab_size": s.vocab,
+           "max_position_embeddings": 40960, "rms_norm_eps": s.eps, "rope_theta": s.rope_theta,
+           "tie_word_embeddings": False, "torch_dtype": "bfloat16"}
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(cfg, f)
+    names = _tensor_names(s)
+    header = {}
+    off = 0
+    for n, shape in names:
+        nbytes = int(np.prod(shape)) * 2
+        header[n] = {"dtype": "BF16", "shape": list(shape), "data_offsets": [off, off + nbytes]}
+        off += nbytes
+    header["__metadata__"] = {"format": "pt"}
+    hb = json.dumps(header).encode()
+    hb += b" " * ((8 - len(hb) % 8) % 8)
+    g = torch.Generator(device=device).manual_seed(seed)
+    with open(os.path.join(path, "model.safetensors"), "wb") as f:
+        f.write(struct.pack("<Q", len(hb)))
+        f.write(hb)
+        for n, shape in names:
+            if n.endswith("norm.weight"):
+                t = 1.0 + 0.1 * torch.randn(shape, generator=g, device=device)
+            else:
+                t = 0.02 * torch.randn(shape, generator=g, device=device)
+            f.write(t.to(torch.bfloat16).view(torch.int16).cpu().numpy().tobytes())
