@@ -372,6 +372,133 @@ def run_gpu(args, rank, world, device):
             "h2d": qkv.numel() * 2, "d2h": out.numel() * 2}
 
 
+def run_generate(args):
+    """Full random-init Qwen3-8B (36 layers) through the reference's UNCHANGED QwenRunner, twice:
+    built on the reference's own runtime headers and on the drop-in headers.  Batch 8 prompts
+    of 2048 uniform-random ids, then greedy decode steps through IModelRunner::Forward (the runner
+    picks prefill vs decode).  Reports tokens/s of both and greedy-token parity: per sequence the
+    first step where the tokens differ and the reference's top-1/top-2 logit margin there."""
+    import importlib.util
+    import tempfile
+
+    import numpy as np
+    import torch
+    from tests.qwen_model import QWEN3_8B, write_random_qwen3
+    from mllm_b200.dropin.build_facade import runner_module_path
+
+    def load(flavor):
+        path = runner_module_path(flavor)
+        spec = importlib.util.spec_from_file_location(os.path.basename(path).split(".")[0], path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        return mod
+
+    B, S, steps = 8, 2048, args.gen_steps
+    rng = np.random.default_rng(2048)
+    prompt = torch.from_numpy(rng.integers(0, QWEN3_8B.vocab, size=(B, S))).long()
+    results = {}
+    with tempfile.TemporaryDirectory(dir=args.model_dir) as d:
+        t0 = time.time()
+        write_random_qwen3(d, QWEN3_8B, seed=8)
+        t_write = time.time() - t0
+        ref_tokens = ref_margins = None
+        ref_logits = []       # reference last-position logits per step (bf16, host)
+        dropin_tf_logits = []  # drop-in logits under teacher forcing (bf16, host)
+        tf = {}
+        for flavor in ("reference", "dropin"):
+            mod = load(flavor)
+            runner = mod.Runner(d)
+            if flavor == "dropin":
+                # teacher forcing: the reference's own greedy tokens fed to the drop-in runner
+                last = runner.forward(prompt)[:, -1].float()
+                agree, diffs = [], []
+                dropin_tf_logits.clear()
+                for k in range(steps):
+                    dropin_tf_logits.append(last.to(torch.bfloat16).cpu())
+                    r = ref_logits[k].to(last.device).float()
+                    diffs.append((last - r).abs().max(-1).values.cpu())
+                    agree.append((last.argmax(-1).cpu() == ref_tokens[:, k]))
+                    last = runner.forward(ref_tokens[:, k:k + 1])[:, -1].float()
+                agree = torch.stack(agree, 1)
+                diffs = torch.stack(diffs, 1)
+                tf = {"argmax_agreement": float(agree.float().mean()),
+                      "max_abs_logit_diff": float(diffs.max()), "mean_max_abs_logit_diff": float(diffs.mean())}
+                for thr in (0.1, 0.25, 0.5):
+                    sel = ref_margins > thr
+                    tf[f"argmax_agreement_margin_gt_{thr}"] = (float(agree[sel].float().mean()) if sel.any() else None)
+                    tf[f"steps_margin_gt_{thr}"] = int(sel.sum())
+                runner.reset_cache()
+            toks, margins = [], []
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            logits = runner.forward(prompt)
+            last = logits[:, -1].float()
+            del logits
+            torch.cuda.synchronize()
+            t_pre = time.perf_counter() - t0
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                if flavor == "reference":
+                    ref_logits.append(last.to(torch.bfloat16).cpu())
+                top2 = torch.topk(last, 2, dim=-1).values
+                margins.append((top2[:, 0] - top2[:, 1]).cpu())
+                nxt = last.argmax(-1, keepdim=True)          # greedy: first max wins
+                toks.append(nxt.cpu())
+                last = runner.forward(nxt.cpu())[:, -1].float()
+            torch.cuda.synchronize()
+            t_dec = time.perf_counter() - t0
+            results[flavor] = {"prefill_s": t_pre, "decode_s": t_dec,
+                               "prefill_tok_s": B * S / t_pre, "decode_tok_s": B * steps / t_dec}
+            tokens = torch.cat(toks, 1)
+            if flavor == "reference":
+                ref_tokens, ref_margins = tokens, torch.stack(margins, 1)
+            else:
+                new_tokens = tokens
+            del runner
+            torch.cuda.empty_cache()
+    # fp32 floor: the same (bf16-valued) weights in fp32 through the reference runner, fed the
+    # same tokens -- how far each bf16 runner's logits are from a higher-precision run.
+    if args.fp32_floor:
+        with tempfile.TemporaryDirectory(dir=args.model_dir) as d32:
+            write_random_qwen3(d32, QWEN3_8B, seed=8, dtype="f32")
+            runner = load("reference").Runner(d32)
+            last = runner.forward(prompt)[:, -1].float()
+            e_ref, e_new = [], []
+            for k in range(steps):
+                e_ref.append((ref_logits[k].to(last.device).float() - last).abs().max(-1).values.cpu())
+                e_new.append((dropin_tf_logits[k].to(last.device).float() - last).abs().max(-1).values.cpu())
+                last = runner.forward(ref_tokens[:, k:k + 1])[:, -1].float()
+            del runner
+            torch.cuda.empty_cache()
+        e_ref = torch.stack(e_ref)
+        e_new = torch.stack(e_new)
+        tf["fp32_floor"] = {"reference_bf16_max_abs_vs_fp32": float(e_ref.max()),
+                            "reference_bf16_mean_max_abs_vs_fp32": float(e_ref.mean()),
+                            "dropin_bf16_max_abs_vs_fp32": float(e_new.max()),
+                            "dropin_bf16_mean_max_abs_vs_fp32": float(e_new.mean())}
+    same = (new_tokens == ref_tokens)
+    first_div = []
+    for b in range(B):
+        bad = (~same[b]).nonzero()
+        if len(bad) == 0:
+            first_div.append({"seq": b, "diverged": False})
+        else:
+            k = int(bad[0])
+            first_div.append({"seq": b, "diverged": True, "step": k,
+                              "ref_top2_margin": float(ref_margins[b, k])})
+    line = {"metric": "Qwen3-8B random-init greedy generation through the unchanged QwenRunner",
+            "workload": f"batch {B} x {S}-token prompts + {steps} greedy steps, 36 layers, bf16",
+            "reference_runner": results["reference"], "dropin_runner": results["dropin"],
+            "speedup_prefill": results["reference"]["prefill_s"] / results["dropin"]["prefill_s"],
+            "speedup_decode": results["reference"]["decode_s"] / results["dropin"]["decode_s"],
+            "tokens_identical_fraction": float(same.float().mean()),
+            "sequences_fully_identical": int(sum(1 for f in first_div if not f["diverged"])),
+            "first_divergence": first_div, "teacher_forced": tf,
+            "note": "reference decode steps include copying its per-step logits to the host (parity record)",
+            "checkpoint_write_s": t_write}
+    print(json.dumps(line))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -380,8 +507,17 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--skip-prefill", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg (profiling runs)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "qwen3-8b-generate"],
+                    help="decode: the headline line; qwen3-8b-generate: full-model runner parity + speed")
+    ap.add_argument("--gen-steps", type=int, default=128)
+    ap.add_argument("--fp32-floor", action="store_true",
+                    help="also run the reference runner on fp32 weights as the precision floor")
+    ap.add_argument("--model-dir", default=None, help="where to write the random checkpoint (default: tmp)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.workload == "qwen3-8b-generate":
+        run_generate(args)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

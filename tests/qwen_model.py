@@ -49,9 +49,11 @@ def _tensor_names(s: QwenShape):
     return names
 
 
-def write_random_qwen3(path: str, s: QwenShape, seed: int = 0, device: str = "cuda") -> None:
-    """Weights N(0, 0.02) (norm weights 1 + N(0, 0.1)), bf16, generated with torch on `device`
-    (a seeded torch generator) and streamed to model.safetensors tensor by tensor."""
+def write_random_qwen3(path: str, s: QwenShape, seed: int = 0, device: str = "cuda", dtype: str = "bf16") -> None:
+    """Weights N(0, 0.02) (norm weights 1 + N(0, 0.1)), rounded to bf16, generated with torch on
+    `device` (a seeded torch generator) and streamed to model.safetensors tensor by tensor.
+    dtype="f32" stores the same bf16 values widened exactly to fp32 (a higher-precision run of
+    the same model)."""
     import torch
     os.makedirs(path, exist_ok=True)
     cfg = {"model_type": "qwen3", "_name_or_path": "random-qwen3", "hidden_size": s.hidden,
@@ -64,9 +66,10 @@ def write_random_qwen3(path: str, s: QwenShape, seed: int = 0, device: str = "cu
     names = _tensor_names(s)
     header = {}
     off = 0
+    es, st_name = (2, "BF16") if dtype == "bf16" else (4, "F32")
     for n, shape in names:
-        nbytes = int(np.prod(shape)) * 2
-        header[n] = {"dtype": "BF16", "shape": list(shape), "data_offsets": [off, off + nbytes]}
+        nbytes = int(np.prod(shape)) * es
+        header[n] = {"dtype": st_name, "shape": list(shape), "data_offsets": [off, off + nbytes]}
         off += nbytes
     header["__metadata__"] = {"format": "pt"}
     hb = json.dumps(header).encode()
@@ -80,4 +83,8 @@ def write_random_qwen3(path: str, s: QwenShape, seed: int = 0, device: str = "cu
                 t = 1.0 + 0.1 * torch.randn(shape, generator=g, device=device)
             else:
                 t = 0.02 * torch.randn(shape, generator=g, device=device)
-            f.write(t.to(torch.bfloat16).view(torch.int16).cpu().numpy().tobytes())
+            t = t.to(torch.bfloat16)
+            if dtype == "bf16":
+                f.write(t.view(torch.int16).cpu().numpy().tobytes())
+            else:
+                f.write(t.float().cpu().numpy().tobytes())
