@@ -343,10 +343,25 @@ def run_gpu(args, rank, world, device):
                                                  Bp, Hr, Hkvr, D, S, S, scale, op.data_ptr(), sh)
             assert st == 0, lib.mllm_attn_last_error()
 
+        # tensor-parallel exchange: this rank's column slice of o_proj, then the all-reduce of the
+        # partial [B*S, hidden] outputs (NCCL over NVLink), as mllm_b200.tp.tp_attention_block does
+        w_o = (0.02 * torch.randn(HIDDEN, Hr * D, device=device, generator=gen)).bfloat16()
+        o_part = torch.empty(Bp * S, HIDDEN, dtype=torch.bfloat16, device=device)
+
+        def oproj_p():
+            torch.matmul(op.view(Bp * S, Hr * D), w_o.t(), out=o_part)
+
+        def allreduce_p():
+            if world > 1:
+                import torch.distributed as dist
+                dist.all_reduce(o_part)
+
         ksteps = max(3, min(args.steps, 20))
         for _ in range(args.warmup):
             epi_p()
             attn_p()
+            oproj_p()
+            allreduce_p()
         evp = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(ksteps)]
         p0 = torch.cuda.Event(enable_timing=True)
         p1 = torch.cuda.Event(enable_timing=True)
@@ -363,8 +378,26 @@ def run_gpu(args, rank, world, device):
         barrier()
         pre_ms = max_over_ranks(p0.elapsed_time(p1)) / ksteps
         attn_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in evp))
-        pre = {"pre_ms": pre_ms, "attn_ms": attn_ms, "steps": ksteps}
-        del qkv_p, kp, vp, qp, op
+        # the layer's exchange step, timed separately (o_proj GEMM, then the all-reduce)
+        evo = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(ksteps)]
+        barrier()
+        torch.cuda.synchronize()
+        for i in range(ksteps):
+            evo[i][0].record(stream)
+            oproj_p()
+            evo[i][1].record(stream)
+            allreduce_p()
+            evo[i][2].record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        oproj_ms = max_over_ranks(statistics.mean(e[0].elapsed_time(e[1]) for e in evo))
+        ar_ms = max_over_ranks(statistics.mean(e[1].elapsed_time(e[2]) for e in evo))
+        ar_bytes = o_part.numel() * 2
+        pre = {"pre_ms": pre_ms, "attn_ms": attn_ms, "steps": ksteps, "oproj_ms": oproj_ms,
+               "allreduce_ms": ar_ms if world > 1 else 0.0, "allreduce_bytes": ar_bytes if world > 1 else 0,
+               "allreduce_busbw_gbs": (2 * (world - 1) / world * ar_bytes / (ar_ms * 1e-3) / 1e9)
+               if world > 1 and ar_ms > 0 else None}
+        del qkv_p, kp, vp, qp, op, o_part, w_o
 
     clocks = sampler.stop() if rank == 0 else None
     return {"elapsed_ms": elapsed_ms, "dec_ms": dec_ms, "e2e_ms": e2e_ms, "pre": pre, "clocks": clocks,
@@ -586,6 +619,9 @@ def main():
             "workload": f"Qwen3-8B causal prefill attention, batch {PRE_B} x {PRE_S}, heads split over {n} GPU(s)",
             "value": fl / (p["pre_ms"] * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": p["pre_ms"],
             "steps": p["steps"],
+            "tp_exchange": {"o_proj_ms": p["oproj_ms"], "allreduce_ms": p["allreduce_ms"],
+                            "allreduce_bytes": p["allreduce_bytes"], "allreduce_busbw_gbs": p["allreduce_busbw_gbs"],
+                            "note": "column-sharded o_proj GEMM + NCCL all-reduce of the [B*S, hidden] partials"},
             "roofline": {"bound": "tensor", "kernel": "prefill_kernel<128>",
                          "achieved": fl / n / (p["attn_ms"] * 1e-3) / 1e12, "peak": tf_peak, "unit": "TFLOP/s",
                          "frac": fl / n / (p["attn_ms"] * 1e-3) / 1e12 / tf_peak, "peak_source": peak_src,

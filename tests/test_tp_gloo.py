@@ -1,0 +1,105 @@
+"""Tensor-parallel host logic on CPU: 2 gloo ranks, each computing its KV-head group's attention
+with the numpy oracle (as a stand-in compute backend for the test) plus its partial o_proj,
+summed by the all-reduce, must equal the unsharded oracle layer (prefill then decode steps)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from mllm_b200 import tp
+from oracle import attention_oracle as O
+from tests.golden.cases import case_by_name, make_inputs
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _oracle_attention_fn(caches):
+    """attention_fn backed by the oracle (test only): same signature as runtime.attention_block."""
+    def fn(h, w_q, w_k, w_v, w_o, H, Hkv, D, theta, pos, cache_key, gq, gk, eps):
+        x = h.numpy()
+        q, k, v = O.qwen_qkv_prologue(x, w_q.numpy(), w_k.numpy(), w_v.numpy(), gq.numpy(), gk.numpy(), H, Hkv, D, eps)
+        out = O.attention_forward_projected(q, k, v, w_o.numpy(), H, Hkv, D, theta, pos.numpy(), caches[cache_key])
+        return torch.from_numpy(np.ascontiguousarray(out))
+    return fn
+
+
+def _worker(rank, world, port, case_name, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        c = case_by_name(case_name)
+        inp = make_inputs(c)
+        shard = tp.shard_heads(c.num_heads, c.num_kv_heads, world, rank)
+        T = {k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in inp.items()}
+        wq, wk, wv, wo = tp.shard_weights(shard, c.head_dim, T["w_q"], T["w_k"], T["w_v"], T["w_o"])
+        caches = {"layer0": O.KVCache()}
+        fn = _oracle_attention_fn(caches)
+        outs = []
+        steps = [inp["hidden"]] + [inp["decode_hidden"][i] for i in range(c.decode_steps)]
+        for i, x in enumerate(steps):
+            S = x.shape[1]
+            pos = np.array([caches["layer0"].key.shape[2]]) if i > 0 else np.arange(S)
+            out = tp.tp_attention_block(torch.from_numpy(x), shard, c.head_dim, c.rope_theta, torch.from_numpy(pos),
+                                        "layer0", wq, wk, wv, wo, T["w_q_norm"], T["w_k_norm"], c.eps,
+                                        attention_fn=fn)
+            outs.append(out.numpy())
+        q.put((rank, outs, caches["layer0"].key.shape))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case_name", ["qwen_d128_gqa4"])
+def test_two_rank_head_sharding_matches_unsharded(case_name):
+    c = case_by_name(case_name)
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, case_name, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        rank, outs, kshape = q.get(timeout=120)
+        res[rank] = (outs, kshape)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    # unsharded oracle layer
+    inp = make_inputs(c)
+    cache = O.KVCache()
+    steps = [inp["hidden"]] + [inp["decode_hidden"][i] for i in range(c.decode_steps)]
+    for i, x in enumerate(steps):
+        S = x.shape[1]
+        pos = np.array([cache.key.shape[2]]) if i > 0 else np.arange(S)
+        qq, kk, vv = O.qwen_qkv_prologue(x, inp["w_q"], inp["w_k"], inp["w_v"], inp["w_q_norm"], inp["w_k_norm"],
+                                         c.num_heads, c.num_kv_heads, c.head_dim, c.eps)
+        ref = O.attention_forward_projected(qq, kk, vv, inp["w_o"], c.num_heads, c.num_kv_heads, c.head_dim,
+                                            c.rope_theta, pos, cache)
+        for r in range(world):
+            np.testing.assert_allclose(res[r][0][i], ref, rtol=1e-4, atol=1e-5, err_msg=f"rank {r} step {i}")
+    # each rank's cache holds only its kv heads
+    for r in range(world):
+        assert res[r][1][1] == c.num_kv_heads // world
+
+
+def test_shard_heads_layout():
+    s = [tp.shard_heads(32, 8, 4, r) for r in range(4)]
+    assert [x.kv_heads for x in s] == [(0, 2), (2, 4), (4, 6), (6, 8)]
+    assert [x.q_heads for x in s] == [(0, 8), (8, 16), (16, 24), (24, 32)]
+    assert tp.shard_heads(40, 8, 8, 7).q_heads == (35, 40)   # Qwen3-14B: one kv head (5 q heads) per GPU
+    with pytest.raises(RuntimeError, match="do not split"):
+        tp.shard_heads(32, 8, 3, 0)
+    with pytest.raises(RuntimeError, match="divisible"):
+        tp.shard_heads(30, 8, 2, 0)
