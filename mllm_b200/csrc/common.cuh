@@ -96,6 +96,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // ---------------------------------------------------------------------------------------
+// Programmatic dependent launch: a kernel launched with programmatic stream serialisation may
+// start while the previous kernel in the stream still runs; pdl_wait() blocks until that
+// kernel has completed and its memory is visible (a no-op for an ordinary launch).
+// pdl_trigger() lets the next kernel in the stream start launching early.
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor), unicast only.  Coordinates are innermost-first; the innermost
 // coordinate of every call site is a multiple of 64 bf16 elements (128 B), which satisfies
 // the 16-byte rule for tiled copies.

@@ -83,6 +83,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         mbar_fence_init();
     }
     __syncthreads();
+    pdl_wait();      // q and the cache rows may come from the kernel launched just before
+    pdl_trigger();   // the combine kernel may start launching (it waits for this grid)
 
     auto item_range = [&](int item, int& b, int& g, int& c, int& t0, int& t1, int& L) {
         c = item % a.nch;
@@ -330,30 +332,55 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 // Merges the per-chunk partials of every (sequence, query head) whose cache spans more
-// than one chunk.  One CTA per (kv head, sequence); thread d owns column d.
+// than one chunk.  One CTA per (kv head, sequence).  The (m, l) pairs of all its chunks are
+// staged in shared memory with one parallel load; thread r < n_rep turns its head's pairs into
+// per-chunk weights exp2(m_c - M) and 1/L; then thread d sums the partial column d over the
+// chunks with independent loads.
+constexpr int kMaxChunks = 128;
+
 template <int D>
 __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeArgs a) {
+    __shared__ float s_m[kMaxGroup * kMaxChunks];   // m, then the chunk weight
+    __shared__ float s_l[kMaxGroup * kMaxChunks];
+    __shared__ float s_inv[kMaxGroup];
+    pdl_wait();      // partials come from the split kernel launched just before
     const int g = blockIdx.x, b = blockIdx.y;
     int L = a.kv_lens ? a.kv_lens[b] : a.max_len;
     L = L < 0 ? 0 : (L > a.max_len ? a.max_len : L);
     const int nch_b = (L + a.chunk - 1) / a.chunk;
     if (nch_b <= 1) return;  // written directly by the split kernel
+    const int64_t item0 = ((int64_t)b * a.Hkv + g) * a.nch;
+    const int n = a.n_rep * nch_b;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int r = i / nch_b, c = i - r * nch_b;
+        const float2 ml = *reinterpret_cast<const float2*>(a.part_ml + ((item0 + c) * a.n_rep + r) * 2);
+        s_m[i] = ml.x;
+        s_l[i] = ml.y;
+    }
+    __syncthreads();
+    if (threadIdx.x < a.n_rep) {
+        const int r = threadIdx.x;
+        float M = -INFINITY;
+        for (int c = 0; c < nch_b; ++c) M = fmaxf(M, s_m[r * nch_b + c]);
+        const float Mu = (M == -INFINITY) ? 0.f : M;
+        float Lt = 0.f;
+        for (int c = 0; c < nch_b; ++c) {
+            const float w = ex2_approx(s_m[r * nch_b + c] - Mu);
+            s_m[r * nch_b + c] = w;
+            Lt += s_l[r * nch_b + c] * w;
+        }
+        s_inv[r] = (Lt > 0.f) ? 1.f / Lt : 0.f;
+    }
+    __syncthreads();
     const int d = threadIdx.x;
     if (d >= D) return;
-    const int64_t item0 = ((int64_t)b * a.Hkv + g) * a.nch;
     for (int r = 0; r < a.n_rep; ++r) {
-        float M = -INFINITY;
-        for (int c = 0; c < nch_b; ++c) M = fmaxf(M, a.part_ml[((item0 + c) * a.n_rep + r) * 2]);
-        const float Mu = (M == -INFINITY) ? 0.f : M;
-        float Lt = 0.f, acc = 0.f;
-        for (int c = 0; c < nch_b; ++c) {
-            const int64_t pidx = (item0 + c) * a.n_rep + r;
-            const float sc = ex2_approx(a.part_ml[pidx * 2] - Mu);
-            Lt += a.part_ml[pidx * 2 + 1] * sc;
-            acc += a.part_o[pidx * D + d] * sc;
-        }
-        const float res = (Lt > 0.f) ? acc / Lt : 0.f;
-        a.out[((int64_t)b * a.H + (int64_t)g * a.n_rep + r) * D + d] = __float2bfloat16_rn(res);
+        const float* col = a.part_o + ((item0 * a.n_rep) + r) * D + d;
+        const int64_t step = (int64_t)a.n_rep * D;   // next chunk, same head
+        float acc = 0.f;
+#pragma unroll 8
+        for (int c = 0; c < nch_b; ++c) acc += col[c * step] * s_m[r * nch_b + c];
+        a.out[((int64_t)b * a.H + (int64_t)g * a.n_rep + r) * D + d] = __float2bfloat16_rn(acc * s_inv[r]);
     }
 }
 
@@ -361,15 +388,31 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeArgs a) {
 // grid stays balanced, with chunks of at least 256 rows (amortises the per-item merge).
 constexpr int kMinChunk = 256;
 
-int max_chunks(int max_len) { return std::max(1, (max_len + kMinChunk - 1) / kMinChunk); }
+int max_chunks(int max_len) { return std::min(kMaxChunks, std::max(1, (max_len + kMinChunk - 1) / kMinChunk)); }
 
-void plan_chunks(int B, int Hkv, int max_len, int num_sms, int& chunk, int& nch) {
+// Picks the chunk count per sequence for the static, strided item list of a grid of
+// `grid` persistent CTAs: the slowest CTA processes ceil(items / grid) items of
+// ceil(tiles / nch) tiles each, plus a merge cost of about half a tile per item.  Equal-sized
+// chunks that divide the work evenly over the CTAs win.
+void plan_chunks(int B, int Hkv, int max_len, int grid, int& chunk, int& nch) {
     const int64_t pairs = (int64_t)B * Hkv;
-    int64_t want = (16LL * num_sms + pairs - 1) / pairs;
-    want = std::max<int64_t>(1, std::min<int64_t>(want, max_chunks(max_len)));
-    int64_t ch = (max_len + want - 1) / want;
-    ch = ((ch + kTile - 1) / kTile) * kTile;
-    chunk = (int)std::max<int64_t>(ch, kTile);
+    const int64_t tiles = (max_len + kTile - 1) / kTile;
+    double best = 1e30;
+    int best_n = 1;
+    const int n_max = (int)std::min<int64_t>(max_chunks(max_len), tiles);
+    for (int n = 1; n <= n_max; ++n) {
+        const int64_t chunk_tiles = (tiles + n - 1) / n;
+        const int64_t n_eff = (tiles + chunk_tiles - 1) / chunk_tiles;   // chunks actually used
+        const int64_t items = pairs * n_eff;
+        const int64_t per_cta = (items + grid - 1) / grid;
+        const double cost = (double)per_cta * ((double)chunk_tiles + 0.5);
+        if (cost < best - 1e-9) {
+            best = cost;
+            best_n = (int)n_eff;
+        }
+    }
+    const int64_t chunk_tiles = (tiles + best_n - 1) / best_n;
+    chunk = (int)(chunk_tiles * kTile);
     nch = (max_len + chunk - 1) / chunk;
 }
 
@@ -439,7 +482,7 @@ extern "C" int mllm_decode_attention_bf16(const void* q, const void* k_cache, co
     a.Hkv = num_kv_heads;
     a.n_rep = n_rep;
     a.max_len = max_kv_len;
-    plan_chunks(batch, num_kv_heads, max_kv_len, num_sms, a.chunk, a.nch);
+    plan_chunks(batch, num_kv_heads, max_kv_len, 2 * num_sms, a.chunk, a.nch);
     const size_t parts = (size_t)batch * num_kv_heads * a.nch * n_rep;
     a.part_o = reinterpret_cast<float*>(workspace);
     a.part_ml = a.part_o + parts * head_dim;
@@ -454,18 +497,26 @@ extern "C" int mllm_decode_attention_bf16(const void* q, const void* k_cache, co
         if (int st = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                                 "decode smem attribute"))
             return st;
-        kern<<<grid, kThreads, smem, s>>>(tmK, tmV, a);
-        if (int st = check_cuda(cudaGetLastError(), "decode_split_kernel launch")) return st;
-        if (a.nch > 1) decode_combine_kernel<128><<<dim3(num_kv_heads, batch), 128, 0, s>>>(a);
+        if (int st = check_cuda(launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, tmK, tmV, a),
+                                "decode_split_kernel launch"))
+            return st;
+        if (a.nch > 1 &&
+            check_cuda(launch_pdl(decode_combine_kernel<128>, dim3(num_kv_heads, batch), dim3(128), 0, s, a),
+                       "decode_combine_kernel launch"))
+            return MLLM_ERR_CUDA;
     } else {
         auto kern = decode_split_kernel<64>;
         const int smem = DecodeCfg<64>::kSmemBytes;
         if (int st = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                                 "decode smem attribute"))
             return st;
-        kern<<<grid, kThreads, smem, s>>>(tmK, tmV, a);
-        if (int st = check_cuda(cudaGetLastError(), "decode_split_kernel launch")) return st;
-        if (a.nch > 1) decode_combine_kernel<64><<<dim3(num_kv_heads, batch), 128, 0, s>>>(a);
+        if (int st = check_cuda(launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, tmK, tmV, a),
+                                "decode_split_kernel launch"))
+            return st;
+        if (a.nch > 1 &&
+            check_cuda(launch_pdl(decode_combine_kernel<64>, dim3(num_kv_heads, batch), dim3(128), 0, s, a),
+                       "decode_combine_kernel launch"))
+            return MLLM_ERR_CUDA;
     }
     if (int st = check_cuda(cudaGetLastError(), "decode_combine_kernel launch")) return st;
     return ok();
@@ -570,7 +621,7 @@ extern "C" int mllm_decode_attention_noalloc_bf16(const void* q, const void* k_c
     a.Hkv = num_kv_heads;
     a.n_rep = n_rep;
     a.max_len = max_kv_len;
-    plan_chunks(batch, num_kv_heads, max_kv_len, num_sms, a.chunk, a.nch);
+    plan_chunks(batch, num_kv_heads, max_kv_len, 2 * num_sms, a.chunk, a.nch);
     const size_t parts = (size_t)batch * num_kv_heads * a.nch * n_rep;
     a.part_o = reinterpret_cast<float*>(scratch);
     a.part_ml = a.part_o + parts * head_dim;
@@ -585,18 +636,26 @@ extern "C" int mllm_decode_attention_noalloc_bf16(const void* q, const void* k_c
                                                      cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                                 "decode smem attribute"))
             return st;
-        decode_split_kernel<128><<<grid, kThreads, smem, s>>>(tmK, tmV, a);
-        if (int st = check_cuda(cudaGetLastError(), "decode_split_kernel launch")) return st;
-        if (a.nch > 1) decode_combine_kernel<128><<<dim3(num_kv_heads, batch), 128, 0, s>>>(a);
+        if (int st = check_cuda(launch_pdl(decode_split_kernel<128>, dim3(grid), dim3(kThreads), smem, s, tmK, tmV, a),
+                                "decode_split_kernel launch"))
+            return st;
+        if (a.nch > 1 &&
+            check_cuda(launch_pdl(decode_combine_kernel<128>, dim3(num_kv_heads, batch), dim3(128), 0, s, a),
+                       "decode_combine_kernel launch"))
+            return MLLM_ERR_CUDA;
     } else {
         const int smem = DecodeCfg<64>::kSmemBytes;
         if (int st = check_cuda(cudaFuncSetAttribute(decode_split_kernel<64>,
                                                      cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                                 "decode smem attribute"))
             return st;
-        decode_split_kernel<64><<<grid, kThreads, smem, s>>>(tmK, tmV, a);
-        if (int st = check_cuda(cudaGetLastError(), "decode_split_kernel launch")) return st;
-        if (a.nch > 1) decode_combine_kernel<64><<<dim3(num_kv_heads, batch), 128, 0, s>>>(a);
+        if (int st = check_cuda(launch_pdl(decode_split_kernel<64>, dim3(grid), dim3(kThreads), smem, s, tmK, tmV, a),
+                                "decode_split_kernel launch"))
+            return st;
+        if (a.nch > 1 &&
+            check_cuda(launch_pdl(decode_combine_kernel<64>, dim3(num_kv_heads, batch), dim3(128), 0, s, a),
+                       "decode_combine_kernel launch"))
+            return MLLM_ERR_CUDA;
     }
     if (int st = check_cuda(cudaGetLastError(), "decode_combine_kernel launch")) return st;
     return ok();

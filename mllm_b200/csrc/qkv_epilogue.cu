@@ -107,6 +107,7 @@ __global__ void __launch_bounds__(kWarps * 32, 6) qkv_epilogue_kernel(EpilogueAr
     __shared__ float s_gamma[2][D];   // q / k per-head norm weights (fp32 copies of the bf16 values)
     __shared__ int64_t s_slot;
 
+    pdl_trigger();   // a decode launched next may start its set-up (it waits for this grid)
     const int token = blockIdx.x;
     const int b = token / a.S;
     const int s = token - b * a.S;
