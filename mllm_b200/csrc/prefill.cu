@@ -241,15 +241,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int c = 0; c < kBN; ++c) sv[c] = (c <= lim) ? sv[c] : -INFINITY;
             }
-            float mx[kAcc];
+            // row max: 4 independent chains of three-input max (two new scores per step)
+            float mx[4];
 #pragma unroll
-            for (int i = 0; i < kAcc; ++i) mx[i] = sv[i];
+            for (int i = 0; i < 4; ++i) mx[i] = fmaxf(sv[2 * i], sv[2 * i + 1]);
 #pragma unroll
-            for (int c = kAcc; c < kBN; ++c) mx[c % kAcc] = fmaxf(mx[c % kAcc], sv[c]);
+            for (int c = 8; c < kBN; c += 8)
 #pragma unroll
-            for (int w = kAcc / 2; w >= 1; w >>= 1)
-#pragma unroll
-                for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
+                for (int i = 0; i < 4; ++i) mx[i] = fmax3(mx[i], sv[c + 2 * i], sv[c + 2 * i + 1]);
+            mx[0] = fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3]));
             const float mt = mx[0] * a.scale_log2;   // scale > 0: max of scaled = scaled max
             const float m_new = fmaxf(m_run, mt);
             const bool grow = (m_new - m_run) > kRescaleThreshold;   // true on the first tile
@@ -269,6 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             // P = exp2(S * scale - m) in bf16, written over the consumed S columns
+            // P = exp2(S * scale - m): packed fp32 pairs for the scale/subtract and the row sum
             const float neg_m = -m_use;
             float sum[kAcc];
 #pragma unroll
@@ -278,20 +279,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t pk[16];
 #pragma unroll
                 for (int e = 0; e < 32; e += 2) {
-                    const float p0 = ex2_approx(fmaf(sv[c * 32 + e], a.scale_log2, neg_m));
-                    const float p1 = ex2_approx(fmaf(sv[c * 32 + e + 1], a.scale_log2, neg_m));
-                    sum[e % kAcc] += p0;
-                    sum[(e + 1) % kAcc] += p1;
+                    float x0, x1;
+                    fma2(x0, x1, sv[c * 32 + e], sv[c * 32 + e + 1], a.scale_log2, a.scale_log2, neg_m, neg_m);
+                    const float p0 = ex2_approx(x0);
+                    const float p1 = ex2_approx(x1);
+                    add2(sum[(e >> 1) % 4 * 2], sum[(e >> 1) % 4 * 2 + 1], p0, p1);
                     pk[e >> 1] = pack_bf16x2(p0, p1);
                 }
                 tmem_st16(t_s + c * 16, pk);
             }
             tmem_wait_st();
-#pragma unroll
-            for (int w = kAcc / 2; w >= 1; w >>= 1)
-#pragma unroll
-                for (int i = 0; i < w; ++i) sum[i] += sum[i + w];
-            l_run = l_run * alpha + sum[0];
+            add2(sum[0], sum[1], sum[2], sum[3]);
+            add2(sum[4], sum[5], sum[6], sum[7]);
+            add2(sum[0], sum[1], sum[4], sum[5]);
+            l_run = l_run * alpha + (sum[0] + sum[1]);
             m_run = m_use;
             tc_fence_before();
             mbar_arrive(&p_full[qt]);
