@@ -8,14 +8,20 @@
 // One CTA computes TWO 128-row query tiles (256 consecutive rows) of one (sequence, q head);
 // both tiles share every K/V tile the CTA loads.
 //   warp 0        TMA producer: both Q tiles once, then K/V tiles of 128 cache rows into a
-//                 shared-memory ring (128-byte swizzle; innermost coordinates multiples of 64)
+//                 shared-memory ring (128-byte swizzle; innermost coordinates multiples of 64).
+//                 K and V of a stage have their own full/empty barriers: K(j) is free once the
+//                 S products of tile j are done, a whole iteration before V(j) is, so the next
+//                 K tile is loaded early instead of waiting for the previous P.V
 //   warp 1        TMEM allocator + single-thread MMA issuer (tcgen05.mma kind::f16, M=128):
 //                   S_i   = Q_i K_j^T    A, B from shared memory, fp32 into TMEM columns S_i
 //                   O_i  += P_i V_j      A = P_i from TMEM (written over S_i), B = V (MN-major)
 //                 per tile j it issues PV_0(j), S_0(j+1), PV_1(j), S_1(j+1): while one softmax
-//                 group works on its tile, the tensor pipe runs the other tile's products
+//                 group works on its tile, the tensor pipe runs the other tile's products.
+//                 Each product's k-steps are fully unrolled with constant descriptor offsets:
+//                 one thread feeds the tensor pipe, and a rolled loop could not keep a 64-cycle
+//                 128 x 128 x 16 instruction queued back to back
 //   warps 4-7     softmax of query tile 0, warps 8-11 of tile 1 (warp w reaches TMEM lanes
-//                 32*(w%4)..+31); they run with 224 registers each (setmaxnreg).  Thread r
+//                 32*(w%4)..+31); they run with 216 registers each (setmaxnreg).  Thread r
 //                 owns row r: it loads its 128 scores from TMEM with back-to-back loads and a
 //                 single wait, takes the row max (causal bound applied
 //                 per element on diagonal tiles), rescales the O row in TMEM only when the max
@@ -43,11 +49,12 @@ constexpr int kBN = 128;            // cache rows per K/V tile
 constexpr int kThreads = 384;       // 3 warpgroups: {producer, MMA, 2 idle}, softmax tile 0, tile 1
 // Register split (setmaxnreg): the kernel launches at 168 registers per thread (384 x 168 =
 // 64,512, three warps per SM sub-partition).  The producer/MMA warpgroup gives registers back
-// and the two softmax warpgroups take them: 128 x 56 + 256 x 224 = 64,512, and per sub-partition
-// 56 + 224 + 224 = 504 = 3 x 168, so the increase can always be satisfied.
+// and the two softmax warpgroups take them: 128 x 72 + 256 x 216 = 64,512, and per sub-partition
+// 72 + 216 + 216 = 504 = 3 x 168, so the increase can always be satisfied.  72 keeps the fully
+// unrolled MMA issue loops free of spills, 216 the softmax.
 constexpr uint32_t kLaunchRegs = 168;
-constexpr uint32_t kLowRegs = 56;
-constexpr uint32_t kHighRegs = 224;
+constexpr uint32_t kLowRegs = 72;
+constexpr uint32_t kHighRegs = 216;
 static_assert(128 * kLowRegs + 256 * kHighRegs <= kThreads * kLaunchRegs, "register split exceeds the launch");
 static_assert(kLowRegs + 2 * kHighRegs <= 3 * kLaunchRegs, "register split exceeds a sub-partition");
 constexpr int kBox = kBN * 128;     // one 128-row x 64-column bf16 box (16 KB)
@@ -63,6 +70,8 @@ struct PrefillCfg {
     static constexpr int kStageBytes = 2 * kKVBytes;
     static constexpr int kBarBytes = 256;
     static constexpr int kSmemBytes = kQTiles * kQBytes + kStages * kStageBytes + kBarBytes + 1024;
+    // q_full, k/v full/empty per stage, s_full/p_full/o_done per query tile, the TMEM slot
+    static_assert((1 + 4 * kStages + 3 * kQTiles) * 8 + 4 <= kBarBytes, "barrier area too small");
 };
 
 struct PrefillArgs {
@@ -86,9 +95,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* sKV = sQ + kQTiles * Cfg::kQBytes;          // [ST][K | V]
     uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + ST * Cfg::kStageBytes);
     uint64_t* q_full = bars;
-    uint64_t* kv_full = bars + 1;
-    uint64_t* kv_empty = kv_full + ST;
-    uint64_t* s_full = kv_empty + ST;   // [2]  S_i(j) complete
+    uint64_t* k_full = bars + 1;        // [ST] K tile landed
+    uint64_t* k_empty = k_full + ST;    // [ST] S products that read the K tile are complete
+    uint64_t* v_full = k_empty + ST;    // [ST] V tile landed
+    uint64_t* v_empty = v_full + ST;    // [ST] P.V products that read the V tile are complete
+    uint64_t* s_full = v_empty + ST;    // [2]  S_i(j) complete
     uint64_t* p_full = s_full + 2;      // [2]  P_i(j) written (128 arrivals)
     uint64_t* o_done = p_full + 2;      // [2]  last P_i V complete
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
@@ -112,8 +123,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
         for (int s = 0; s < ST; ++s) {
-            mbar_init(&kv_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+            mbar_init(&k_full[s], 1);
+            mbar_init(&k_empty[s], 1);
+            mbar_init(&v_full[s], 1);
+            mbar_init(&v_empty[s], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
@@ -148,15 +161,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tma_load_4d(sQ + i * Cfg::kQBytes + bx * kBox, &tmQ, q_full, bx * 64, m0 + i * kBM, h, b);
             for (int j = 0; j < n_max; ++j) {
                 const int stage = j % ST;
-                if (!mbar_wait(&kv_empty[stage], ((j / ST) & 1) ^ 1)) break;
-                mbar_arrive_expect_tx(&kv_full[stage], Cfg::kStageBytes);
+                const uint32_t phase = ((j / ST) & 1) ^ 1;
                 uint8_t* sk = sKV + stage * Cfg::kStageBytes;
                 uint8_t* sv = sk + Cfg::kKVBytes;
+                if (!mbar_wait(&k_empty[stage], phase)) break;
+                mbar_arrive_expect_tx(&k_full[stage], Cfg::kKVBytes);
 #pragma unroll
-                for (int bx = 0; bx < Cfg::kBoxes; ++bx) {
-                    tma_load_4d(sk + bx * kBox, &tmK, &kv_full[stage], bx * 64, j * kBN, g, b);
-                    tma_load_4d(sv + bx * kBox, &tmV, &kv_full[stage], bx * 64, j * kBN, g, b);
-                }
+                for (int bx = 0; bx < Cfg::kBoxes; ++bx)
+                    tma_load_4d(sk + bx * kBox, &tmK, &k_full[stage], bx * 64, j * kBN, g, b);
+                if (!mbar_wait(&v_empty[stage], phase)) break;
+                mbar_arrive_expect_tx(&v_full[stage], Cfg::kKVBytes);
+#pragma unroll
+                for (int bx = 0; bx < Cfg::kBoxes; ++bx)
+                    tma_load_4d(sv + bx * kBox, &tmV, &v_full[stage], bx * 64, j * kBN, g, b);
             }
         }
       } else if (warp == 1) {
@@ -166,49 +183,57 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t idesc_o = idesc_bf16_f32(kBM, D, true);
             // Descriptors differ only in their start-address field (bits 0..13, in 16-byte
             // units), so each k-step adds the byte offset >> 4 to a base descriptor.
+            constexpr uint32_t desc_hi = smem_desc_hi_sw128(1024);   // every operand: 8-row groups 1 KB apart
             auto issue_s = [&](int i, int j) {
-                const uint64_t qd = smem_desc_sw128(smem_u32(sQ + i * Cfg::kQBytes), 16, 1024);
-                const uint64_t kd = smem_desc_sw128(smem_u32(sKV + (j % ST) * Cfg::kStageBytes), 16, 1024);
-#pragma unroll 1
+                const uint32_t qd = smem_desc_lo(smem_u32(sQ + i * Cfg::kQBytes), 16);
+                const uint32_t kd = smem_desc_lo(smem_u32(sKV + (j % ST) * Cfg::kStageBytes), 16);
+#pragma unroll
                 for (int ks = 0; ks < D / 16; ++ks) {
-                    const uint64_t off = (uint64_t)(((ks >> 2) * kBox + (ks & 3) * 32) >> 4);
-                    tc_mma_ss(tmem + col_s(i), qd + off, kd + off, idesc_s, ks > 0 ? 1u : 0u);
+                    const uint32_t off = (uint32_t)(((ks >> 2) * kBox + (ks & 3) * 32) >> 4);
+                    tc_mma_ss_w(tmem + col_s(i), qd + off, kd + off, desc_hi, idesc_s, ks > 0 ? 1u : 0u);
                 }
                 tc_commit(&s_full[i]);
             };
-            bool alive = mbar_wait(q_full, 0) && (n_max == 0 || mbar_wait(&kv_full[0], 0));
+            // A stage's K or V is released only if the producer will refill it (no arrival may
+            // land on this CTA's barriers after its last wait).
+            bool alive = mbar_wait(q_full, 0) && (n_max == 0 || mbar_wait(&k_full[0], 0));
             if (alive) {
                 tc_fence_after();
                 for (int i = 0; i < kQTiles; ++i)
                     if (n_tiles[i] > 0) issue_s(i, 0);
+                if (ST < n_max) tc_commit(&k_empty[0]);
             }
             for (int j = 0; j < n_max && alive; ++j) {
                 const int stage = j % ST;
                 const uint32_t v_addr = smem_u32(sKV + stage * Cfg::kStageBytes + Cfg::kKVBytes);
-                bool next_ready = false;
+                bool v_ready = false, k_next_ready = false;
                 for (int i = 0; i < kQTiles && alive; ++i) {
                     if (j >= n_tiles[i]) continue;
                     if (!mbar_wait(&p_full[i], j & 1)) { alive = false; break; }
+                    if (!v_ready) {
+                        if (!mbar_wait(&v_full[stage], (j / ST) & 1)) { alive = false; break; }
+                        v_ready = true;
+                    }
                     tc_fence_after();
-                    const uint64_t vd = smem_desc_sw128(v_addr, kBox, 1024);
-#pragma unroll 1
+                    const uint32_t vd = smem_desc_lo(v_addr, kBox);
+#pragma unroll
                     for (int ks = 0; ks < kBN / 16; ++ks)
-                        tc_mma_ts(tmem + col_o(i), tmem + col_s(i) + ks * 8, vd + (uint64_t)((ks * 16 * 128) >> 4),
-                                  idesc_o, (j > 0 || ks > 0) ? 1u : 0u);
+                        tc_mma_ts_w(tmem + col_o(i), tmem + col_s(i) + ks * 8, vd + (uint32_t)((ks * 16 * 128) >> 4),
+                                    desc_hi, idesc_o, (j > 0 || ks > 0) ? 1u : 0u);
                     if (j + 1 < n_tiles[i]) {
-                        if (!next_ready) {
-                            if (!mbar_wait(&kv_full[(j + 1) % ST], ((j + 1) / ST) & 1)) { alive = false; break; }
+                        if (!k_next_ready) {
+                            if (!mbar_wait(&k_full[(j + 1) % ST], ((j + 1) / ST) & 1)) { alive = false; break; }
                             tc_fence_after();
-                            next_ready = true;
+                            k_next_ready = true;
                         }
                         issue_s(i, j + 1);   // overwrites P_i(j) only after the P.V above read it
                     } else {
                         tc_commit(&o_done[i]);
                     }
                 }
-                // release the stage only if the producer will refill it (no arrival may land
-                // on this CTA's barriers after its last wait)
-                if (alive && j + ST < n_max) tc_commit(&kv_empty[stage]);
+                if (!alive) break;
+                if (j + ST < n_max) tc_commit(&v_empty[stage]);
+                if (k_next_ready && j + 1 + ST < n_max) tc_commit(&k_empty[(j + 1) % ST]);
             }
         }
       }
