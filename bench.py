@@ -14,6 +14,11 @@ than L2 (126 MB), so every step streams it from HBM.
 Secondary (`prefill`): Qwen3-8B causal prefill attention, batch 4 x 8192 rows, same head
 geometry; FLOPs = 4 * B * H * D * S(S+1)/2 = 2.199e12 per step.
 
+Secondary (`ragged_decode`): Qwen3-14B-shaped decode over a ragged batch -- 64 requests whose
+cache lengths are drawn from U[256, 32768] with a fixed seed, 40 q heads / 8 kv heads,
+head_dim 128; one layer's decode call timed back to back (a 40-layer step is 40 such calls).
+Metric = algorithmic KV bytes (sum_b L_b * 2 * Hkv * D * 2 B) / call time.
+
 Multi-GPU (torchrun, one rank per GPU): decode is split by request batches -- every rank owns
 its own 32 sequences (weak scaling, no collective on the data path); prefill is split by
 KV-head groups (H/N query heads and Hkv/N kv heads per rank).  Timing is max over ranks.
@@ -42,6 +47,14 @@ HIDDEN, H, HKV, D = 4096, 32, 8, 128
 THETA, EPS = 1e6, 1e-6
 DEC_B, DEC_L = 32, 4096
 PRE_B, PRE_S = 4, 8192
+# Qwen3-14B ragged decode: 64 requests, lengths U[256, 32768] (seeded), 40 layers
+RAG_B, RAG_H, RAG_HKV, RAG_LAYERS = 64, 40, 8, 40
+RAG_LMIN, RAG_LMAX, RAG_SEED = 256, 32768, 14
+
+
+def ragged_lengths():
+    import numpy as np
+    return np.random.default_rng(RAG_SEED).integers(RAG_LMIN, RAG_LMAX + 1, size=RAG_B)
 
 
 def decode_kv_bytes(b, hkv, L, d):
@@ -442,8 +455,50 @@ def run_gpu(args, rank, world, device):
                if world > 1 and ar_ms > 0 else None}
         del qkv_p, kp, vp, qp, op, o_part, w_o
 
+    # ---------------- ragged decode: Qwen3-14B geometry, 64 requests of mixed length ----------------
+    rag = None
+    if not args.skip_ragged and RAG_HKV % world == 0:
+        torch.cuda.empty_cache()
+        Hr, Hkvr = RAG_H // world, RAG_HKV // world   # kv-head groups per rank
+        lens_np = ragged_lengths()
+        Lmax = int(lens_np.max())
+        kr = torch.empty(RAG_B, Hkvr, Lmax, D, dtype=torch.bfloat16, device=device)
+        vr = torch.empty_like(kr)
+        kr.normal_(generator=gen)
+        vr.normal_(generator=gen)
+        qr = torch.randn(RAG_B, Hr, D, device=device, generator=gen).bfloat16()
+        orr = torch.empty(RAG_B, Hr * D, dtype=torch.bfloat16, device=device)
+        lens_r = torch.from_numpy(lens_np.astype("int32")).to(device)
+        ws_r_bytes = lib.mllm_decode_attention_workspace_size(RAG_B, Hr, Hkvr, D, Lmax)
+        ws_r = torch.empty(ws_r_bytes, dtype=torch.uint8, device=device)
+        rsb, rsh, rst = kr.stride()[:3]
+
+        def decode_r():
+            st = lib.mllm_decode_attention_bf16(qr.data_ptr(), kr.data_ptr(), vr.data_ptr(), rsb, rsh, rst,
+                                                lens_r.data_ptr(), RAG_B, Hr, Hkvr, D, Lmax, scale, orr.data_ptr(),
+                                                ws_r.data_ptr(), ws_r_bytes, sh)
+            assert st == 0, lib.mllm_attn_last_error()
+
+        rsteps = max(3, min(args.steps, 50))
+        for _ in range(args.warmup):
+            decode_r()
+        r0 = torch.cuda.Event(enable_timing=True)
+        r1 = torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        r0.record(stream)
+        for i in range(rsteps):
+            decode_r()
+        r1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        rag = {"ms": max_over_ranks(r0.elapsed_time(r1) / rsteps), "steps": rsteps,
+               "bytes_per_rank": int(lens_np.sum()) * 2 * Hkvr * D * 2, "sum_len": int(lens_np.sum()),
+               "max_len": Lmax}
+        del kr, vr, qr, orr, ws_r
+
     clocks = sampler.stop() if rank == 0 else None
-    return {"elapsed_ms": elapsed_ms, "dec_ms": dec_ms, "e2e_ms": e2e_ms, "pre": pre, "clocks": clocks,
+    return {"elapsed_ms": elapsed_ms, "dec_ms": dec_ms, "e2e_ms": e2e_ms, "pre": pre, "rag": rag, "clocks": clocks,
             "launches_per_step": launches_per_step,
             "h2d": qkv.numel() * 2, "d2h": out.numel() * 2}
 
@@ -582,6 +637,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--skip-prefill", action="store_true")
+    ap.add_argument("--skip-ragged", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg (profiling runs)")
     ap.add_argument("--workload", default="decode", choices=["decode", "qwen3-8b-generate"],
                     help="decode: the headline line; qwen3-8b-generate: full-model runner parity + speed")
@@ -670,6 +726,19 @@ def main():
                          "achieved": fl / n / (p["attn_ms"] * 1e-3) / 1e12, "peak": tf_peak, "unit": "TFLOP/s",
                          "frac": fl / n / (p["attn_ms"] * 1e-3) / 1e12 / tf_peak, "peak_source": peak_src,
                          "traffic": profile_traffic("prefill_qwen3_8b_b4_s8192")}}
+    if res["rag"] is not None:
+        r = res["rag"]
+        ach = r["bytes_per_rank"] / (r["ms"] * 1e-3) / 1e9
+        line["ragged_decode"] = {
+            "workload": f"Qwen3-14B decode over a ragged batch: {RAG_B} requests, cache lengths U[{RAG_LMIN}, "
+                        f"{RAG_LMAX}] (seed {RAG_SEED}, sum {r['sum_len']}, max {r['max_len']}), H={RAG_H} "
+                        f"Hkv={RAG_HKV} D={D}; one layer per call, kv-head groups /{n}",
+            "value": ach * n, "unit": "GB/s", "ms_per_layer": r["ms"],
+            "ms_per_step_all_layers": r["ms"] * RAG_LAYERS, "layers": RAG_LAYERS, "steps": r["steps"],
+            "scaling": "strong", "higher_is_better": True,
+            "roofline": {"bound": "hbm", "kernel": "decode_split_kernel<128> + decode_combine_kernel",
+                         "achieved": ach, "peak": hbm_peak, "unit": "GB/s", "frac": ach / hbm_peak,
+                         "peak_source": peak_src}}
     print(json.dumps(line))
 
 
