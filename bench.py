@@ -5,11 +5,13 @@
 
 Headline (`value`): Qwen3-8B-shaped decode attention -- 32 sequences, one new token each,
 against a bf16 KV cache of 4096 rows per sequence (hidden 4096, 32 q heads, 8 kv heads,
-head_dim 128, per-head QK-RMSNorm eps 1e-6, RoPE theta 1e6).  One step = the fused QKV epilogue
-(QK-norm + RoPE + KV append of the new token) + split-K flash-decode over 4096 rows, i.e. the
-attention step between the q/k/v projections and o_proj.  Metric = algorithmic KV bytes read
-(2 * B * Hkv * L * D * 2 B = 536,870,912 B per step) / step time.  The cache (537 MB) is larger
-than L2 (126 MB), so every step streams it from HBM.
+head_dim 128, per-head QK-RMSNorm eps 1e-6, RoPE theta 1e6).  One step = the QKV epilogue of
+the new token (QK-norm + RoPE + KV append) + split-K flash-decode over 4096 rows, i.e. the
+attention step between the q/k/v projections and o_proj, run as the fused decode step
+(mllm_decode_step_bf16: one split-kernel launch plus the chunk combine).  Metric = algorithmic
+KV bytes read (2 * B * Hkv * L * D * 2 B = 536,870,912 B per step) / step time.  The cache
+(537 MB) is larger than L2 (126 MB), so every step streams it from HBM.  `unfused` reports the
+same step as two calls (mllm_qkv_epilogue_bf16, then mllm_decode_attention_bf16).
 
 Secondary (`prefill`): Qwen3-8B causal prefill attention, batch 4 x 8192 rows, same head
 geometry; FLOPs = 4 * B * H * D * S(S+1)/2 = 2.199e12 per step.
@@ -256,8 +258,17 @@ def run_gpu(args, rank, world, device):
                                             ws.data_ptr(), ws_bytes, sh)
         assert st == 0, lib.mllm_attn_last_error()
 
-    nch = None
-    launches_per_step = 3  # epilogue + split + combine (the cache is split into several chunks here)
+    def step(src, dst):
+        # the fused step: the new token (row L-1 of every sequence, position L-1) and the decode
+        # over all L rows in one split-kernel launch (+ the chunk combine)
+        st = lib.mllm_decode_step_bf16(
+            src.data_ptr(), row, D, src.data_ptr() + H * D * 2, row, D, src.data_ptr() + (H + HKV) * D * 2, row, D,
+            pos.data_ptr(), 1, THETA, None, None, 0, gq.data_ptr(), gk.data_ptr(), EPS,
+            kbuf.data_ptr(), vbuf.data_ptr(), csb, csh, cst, lens.data_ptr(), B, H, HKV, D, L, scale,
+            dst.data_ptr(), ws.data_ptr(), ws_bytes, sh)
+        assert st == 0, lib.mllm_attn_last_error()
+
+    launches_per_step = 2  # split + combine (the cache is split into several chunks here)
 
     def barrier():
         if world > 1:
@@ -273,6 +284,7 @@ def run_gpu(args, rank, world, device):
         return float(t.item())
 
     for _ in range(args.warmup):
+        step(qkv, out)
         epilogue(qkv)
         decode(out)
     torch.cuda.synchronize()
@@ -282,32 +294,42 @@ def run_gpu(args, rank, world, device):
     if rank == 0:
         sampler.start()
         time.sleep(0.3)
-    # timed region: K steps (epilogue + decode), no events inside the loop
+    # timed region: K fused steps back to back between two events, nothing else in the loop;
+    # the step's kernels are the whole step, so this is also the roofline timing
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     t0.record(stream)
     for i in range(args.steps):
-        epilogue(qkv)
-        decode(out)
+        step(qkv, out)
     t1.record(stream)
     torch.cuda.synchronize()
     barrier()
     elapsed_ms = max_over_ranks(t0.elapsed_time(t1))
-    # the decode kernels alone (split + combine), K back-to-back calls between two events, for the
-    # roofline: algorithmic KV bytes / average duration of one decode call
-    d0 = torch.cuda.Event(enable_timing=True)
-    d1 = torch.cuda.Event(enable_timing=True)
+    # the same step as two calls (epilogue kernel, then the decode kernels), and the decode
+    # kernels alone, for comparison
+    u0 = torch.cuda.Event(enable_timing=True)
+    u1 = torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
-    d0.record(stream)
+    u0.record(stream)
+    for i in range(args.steps):
+        epilogue(qkv)
+        decode(out)
+    u1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    unfused_ms = max_over_ranks(u0.elapsed_time(u1) / args.steps)
+    barrier()
+    torch.cuda.synchronize()
+    u0.record(stream)
     for i in range(args.steps):
         decode(out)
-    d1.record(stream)
+    u1.record(stream)
     torch.cuda.synchronize()
     barrier()
-    dec_ms = max_over_ranks(d0.elapsed_time(d1) / args.steps)
+    dec_ms = max_over_ranks(u0.elapsed_time(u1) / args.steps)
 
     # ---- e2e through the C ABI with host buffers: every step copies its q/k/v in from pinned
     # host memory and its output back out.  Copies run on a second stream, double-buffered, so
@@ -323,7 +345,7 @@ def run_gpu(args, rank, world, device):
 
     def e2e_run(n):
         ev_in = [ev(), ev()]      # input copy into buffer j done
-        ev_used = [ev(), ev()]    # epilogue finished reading input buffer j
+        ev_used = [ev(), ev()]    # the step finished reading input buffer j
         ev_done = [ev(), ev()]    # output buffer j written
         ev_out = [ev(), ev()]     # output buffer j copied back to the host
         with torch.cuda.stream(cs):
@@ -338,11 +360,10 @@ def run_gpu(args, rank, world, device):
                     d_in[(i + 1) % 2].copy_(h_in, non_blocking=True)
                     ev_in[(i + 1) % 2].record(cs)
             stream.wait_event(ev_in[j])
-            epilogue(d_in[j])
-            ev_used[j].record(stream)
             if i >= 2:
                 stream.wait_event(ev_out[j])
-            decode(d_out[j])
+            step(d_in[j], d_out[j])
+            ev_used[j].record(stream)
             ev_done[j].record(stream)
             with torch.cuda.stream(cs):
                 cs.wait_event(ev_done[j])
@@ -498,7 +519,8 @@ def run_gpu(args, rank, world, device):
         del kr, vr, qr, orr, ws_r
 
     clocks = sampler.stop() if rank == 0 else None
-    return {"elapsed_ms": elapsed_ms, "dec_ms": dec_ms, "e2e_ms": e2e_ms, "pre": pre, "rag": rag, "clocks": clocks,
+    return {"elapsed_ms": elapsed_ms, "dec_ms": dec_ms, "unfused_ms": unfused_ms, "e2e_ms": e2e_ms, "pre": pre,
+            "rag": rag, "clocks": clocks,
             "launches_per_step": launches_per_step,
             "h2d": qkv.numel() * 2, "d2h": out.numel() * 2}
 
@@ -694,7 +716,7 @@ def main():
     kv_bytes = decode_kv_bytes(DEC_B, HKV, DEC_L, D)
     ms = res["elapsed_ms"] / args.steps
     value = kv_bytes * n / (ms * 1e-3) / 1e9
-    achieved = kv_bytes / (res["dec_ms"] * 1e-3) / 1e9
+    achieved = kv_bytes / (ms * 1e-3) / 1e9
     e2e_ms = res["e2e_ms"] / args.steps
     cpu = None
     if n == 1 and not args.skip_cpu:
@@ -707,8 +729,11 @@ def main():
                     "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"],
                     "ms_per_step": e2e_ms},
             "gpu_launches": res["launches_per_step"] * args.steps,
-            "roofline": {"bound": "hbm", "kernel": "decode_split_kernel<128> + decode_combine_kernel",
-                         "timing": "K back-to-back decode calls between two CUDA events",
+            "unfused": {"ms_per_step": res["unfused_ms"], "decode_only_ms": res["dec_ms"],
+                        "value": kv_bytes * n / (res["unfused_ms"] * 1e-3) / 1e9, "unit": "GB/s",
+                        "note": "the same step as mllm_qkv_epilogue_bf16 + mllm_decode_attention_bf16"},
+            "roofline": {"bound": "hbm", "kernel": "decode_split_kernel<128, fused> + decode_combine_kernel",
+                         "timing": "K back-to-back fused decode steps between two CUDA events",
                          "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                          "peak_source": peak_src, "traffic": profile_traffic("decode_qwen3_8b_b32_l4096")},
             "cpu_baseline": cpu, "clocks": res["clocks"]}

@@ -8,6 +8,7 @@
  *   mllm_qkv_epilogue_bf16      per-head QK-RMSNorm + RoPE + KV-cache append, one kernel
  *   mllm_prefill_attention_bf16 causal GQA attention over the cache (tcgen05 / TMEM / TMA)
  *   mllm_decode_attention_bf16  split-K flash-decode over the cache (HBM-bound)
+ *   mllm_decode_step_bf16       the epilogue of one new token per sequence fused into decode
  *
  * plus the RoPE table builder and RoPE apply that back the `mllm::RoPE` facade.
  *
@@ -180,6 +181,36 @@ MLLM_API int mllm_decode_attention_noalloc_bf16(const void* q, const void* k_cac
                                                 const int32_t* kv_lens, int batch, int num_heads,
                                                 int num_kv_heads, int head_dim, int max_kv_len,
                                                 float softmax_scale, void* out, mllm_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------
+ * Fused decode step.  Replaces, for one new token per sequence, the whole attention step
+ * between the projections and o_proj: TransformerBlock.h:103-107,130-134 (per-head QK-norm),
+ * Attention.h:157-208 (RoPE + KV append) and Attention.h:183-316 at S == 1 -- i.e.
+ * mllm_qkv_epilogue_bf16 with seq_len 1 followed by mllm_decode_attention_bf16, as one
+ * launch of the split kernel (plus its combine kernel when a sequence spans several chunks).
+ * The cache rows it writes are bit-identical to mllm_qkv_epilogue_bf16's; the attention
+ * output equals mllm_decode_attention_bf16's up to fp32 summation order.
+ *   q: bf16 head h of sequence b at q + b*q_sb + h*q_sh (head_dim contiguous); k, v likewise
+ *      for the kv heads (strided views of the q/k/v projections)
+ *   positions: int64 device, RoPE position of sequence b at positions[b*pos_sb] (pos_sb = 0:
+ *      one position for the batch), used when rope_cos/rope_sin are NULL; otherwise fp32
+ *      tables with sequence b's row at rope_row_sb*b ([rows, head_dim], halves duplicated)
+ *   q_norm_weight / k_norm_weight: bf16 [head_dim] (both, or both NULL for Llama)
+ *   kv_lens: int32 device [batch]: rows of each sequence INCLUDING the new token, which is
+ *      written to row kv_lens[b] - 1; every value must lie in [1, max_kv_len] (a value outside
+ *      records MLLM_ERR_DEVICE_LENGTH; a zero length yields a zero output row).  NULL: every
+ *      sequence has max_kv_len rows.
+ *   caches, max_kv_len, out, workspace: as for mllm_decode_attention_bf16 (same
+ *      workspace size). */
+MLLM_API int mllm_decode_step_bf16(const void* q, int64_t q_sb, int64_t q_sh, const void* k, int64_t k_sb,
+                                   int64_t k_sh, const void* v, int64_t v_sb, int64_t v_sh,
+                                   const int64_t* positions, int64_t pos_sb, double rope_theta,
+                                   const float* rope_cos, const float* rope_sin, int64_t rope_row_sb,
+                                   const void* q_norm_weight, const void* k_norm_weight, double rms_norm_eps,
+                                   void* k_cache, void* v_cache, int64_t cache_sb, int64_t cache_sh,
+                                   int64_t cache_st, const int32_t* kv_lens, int batch, int num_heads,
+                                   int num_kv_heads, int head_dim, int max_kv_len, float softmax_scale, void* out,
+                                   void* workspace, size_t workspace_bytes, mllm_stream_t stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

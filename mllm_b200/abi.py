@@ -48,6 +48,9 @@ SIGNATURES = {
                                         _p, _sz, _p]),
     "mllm_decode_attention_noalloc_bf16": (_i, [_p, _p, _p, _i64, _i64, _i64, _p, _i, _i, _i, _i, _i, _f,
                                                 _p, _p]),
+    "mllm_decode_step_bf16": (_i, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _d, _p, _p, _i64,
+                                   _p, _p, _d, _p, _p, _i64, _i64, _i64, _p, _i, _i, _i, _i, _i, _f, _p, _p,
+                                   _sz, _p]),
 }
 
 

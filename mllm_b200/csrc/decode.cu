@@ -22,18 +22,34 @@
 //
 // Rows past a sequence's length inside its last tile are masked to -inf in S and zeroed in
 // the V tile (the cache beyond the length may hold any bit pattern).
+//
+// Fused decode step (kFused, mllm_decode_step_bf16): the QKV epilogue of the new token runs
+// inside the split kernel instead of as a launch of its own.  A sixth warp does it: for each
+// work item it computes QK-RMSNorm + RoPE of the group's query rows (angles and norm weights in
+// registers, each lane evaluating only the columns it holds) into a shared-memory slot that
+// the consumers pick up when they reach the item; it can run a whole item ahead.  Doing this
+// in the consumers put it on the critical path of every item boundary, and doing it in the
+// TMA producer let the stage ring drain -- with equal items every CTA reaches its boundaries
+// at the same moments, so either idled HBM.  The item that owns a sequence's
+// last chunk also computes the new token's K (norm + RoPE) and V rows, writes them to cache
+// row L-1, and leaves the V row and the row's scores for the consumers' merge, which folds the
+// row into the softmax; every item's TMA range stops before row L-1, so no CTA of the launch
+// reads a row the launch is writing.  The row arithmetic is qkv_math.cuh's, so the cache rows
+// are bit-identical to the epilogue kernel's.
 #include <algorithm>
 #include <cmath>
 
 #include "common.cuh"
 #include "host_util.h"
+#include "qkv_math.cuh"
 
 namespace mllm_b200 {
 namespace {
 
 constexpr int kTile = 64;         // cache rows per pipeline stage
 constexpr int kConsumerWarps = 4;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;   // consumers + TMA producer
+constexpr int kThreadsFused = kThreads + 32;          // + the fused step's epilogue warp
 constexpr int kMaxGroup = 8;      // query heads per kv head handled as MMA rows
 constexpr int kBoxBytes = kTile * 128;  // one 64-row x 64-column bf16 TMA box
 
@@ -46,6 +62,11 @@ struct DecodeCfg {
     static constexpr int kRedFloats = (kConsumerWarps - 1) * kMaxGroup * D;
     static constexpr int kSmemBytes =
         kStages * kStageBytes + kRedFloats * 4 + 2 * kConsumerWarps * kMaxGroup * 4 + 2 * kStages * 8 + 1024;
+    // fused step: the transformed q rows of the next item (one slot), the new V row and the new
+    // row's scores (two slots, by active-item parity) and four barriers
+    static constexpr int kFusedBytes = kMaxGroup * D * 2 + 2 * D * 2 + 2 * kMaxGroup * 4 + 4 * 8;
+    static constexpr int kSmemBytesFused = kSmemBytes + kFusedBytes;
+    static_assert(2 * (kSmemBytesFused + 1024) <= 233472, "two CTAs per SM no longer fit");
 };
 
 struct DecodeArgs {
@@ -56,10 +77,27 @@ struct DecodeArgs {
     float* part_ml;             // [B*Hkv*nch, n_rep, 2]
     int B, H, Hkv, n_rep, max_len, chunk, nch, items;
     float scale_log2;
+    // fused step only: the new token's projections, RoPE, norm weights and the cache to append to
+    const __nv_bfloat16* q_in;   // q head h of sequence b at q_in + b*q_sb + h*q_sh
+    const __nv_bfloat16* k_in;
+    const __nv_bfloat16* v_in;
+    int64_t q_sb, q_sh, k_sb, k_sh, v_sb, v_sh;
+    const int64_t* positions;    // positions[b * pos_sb] (when no table is given)
+    int64_t pos_sb;
+    float log_theta;
+    const float* rope_cos;       // optional [rows, D] tables, row b * rope_row_sb
+    const float* rope_sin;
+    int64_t rope_row_sb;
+    const __nv_bfloat16* q_gamma;   // optional per-head QK-RMSNorm weights [D]
+    const __nv_bfloat16* k_gamma;
+    float eps;
+    __nv_bfloat16* k_cache;
+    __nv_bfloat16* v_cache;
+    int64_t c_sb, c_sh, c_st;
 };
 
-template <int D>
-__global__ void __launch_bounds__(kThreads, 2)
+template <int D, bool kFused>
+__global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 2)
     decode_split_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                         DecodeArgs a) {
     using Cfg = DecodeCfg<D>;
@@ -71,6 +109,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     float* red_l = red_m + kConsumerWarps * kMaxGroup;
     uint64_t* full = reinterpret_cast<uint64_t*>(red_l + kConsumerWarps * kMaxGroup);
     uint64_t* empty = full + NS;
+    // fused step only
+    uint64_t* f_qfull = empty + NS;      // the next item's q rows (and new-row data) are ready
+    uint64_t* f_qfree = f_qfull + 1;     // every consumer warp has loaded its q fragments
+    uint64_t* f_vsfree = f_qfree + 1;    // [2] the merge has used slot p's new-row data
+    float* f_snew = reinterpret_cast<float*>(f_vsfree + 2);                        // [2][kMaxGroup]
+    __nv_bfloat16* f_q = reinterpret_cast<__nv_bfloat16*>(f_snew + 2 * kMaxGroup);  // [kMaxGroup][D]
+    __nv_bfloat16* f_vnew = f_q + kMaxGroup * D;                                     // [2][D]
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -79,6 +124,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
+        }
+        if constexpr (kFused) {
+            mbar_init(f_qfull, 1);
+            mbar_init(f_qfree, kConsumerWarps);
+            mbar_init(&f_vsfree[0], 1);
+            mbar_init(&f_vsfree[1], 1);
         }
         mbar_fence_init();
     }
@@ -92,15 +143,105 @@ __global__ void __launch_bounds__(kThreads, 2)
         g = bg % a.Hkv;
         b = bg / a.Hkv;
         int len = a.kv_lens ? a.kv_lens[b] : a.max_len;
-        if (len < 0 || len > a.max_len) {
+        if (len < (kFused ? 1 : 0) || len > a.max_len) {
             if (threadIdx.x == 0 && c == 0 && g == 0) record_error(kErrBadLength);
-            len = len < 0 ? 0 : a.max_len;
+            len = len < 1 ? 0 : a.max_len;
         }
         L = len;
         t0 = c * a.chunk;
-        t1 = min(t0 + a.chunk, L);
+        // the fused step's new row L-1 is not loaded: its item takes it from shared memory
+        t1 = min(t0 + a.chunk, kFused ? L - 1 : L);
     };
 
+    if (kFused && warp == kConsumerWarps + 1) {
+        // --------------------- the new token's epilogue (whole warp) ---------------------
+        constexpr int NI = D / 32;
+        const bool norm = a.q_gamma != nullptr;
+        float gq[NI], gk[NI];   // norm weights at this lane's columns d = lane + 32 i
+#pragma unroll
+        for (int i = 0; i < NI; ++i) {
+            gq[i] = norm ? __bfloat162float(a.q_gamma[lane + 32 * i]) : 0.f;
+            gk[i] = norm ? __bfloat162float(a.k_gamma[lane + 32 * i]) : 0.f;
+        }
+        int n_act = 0;   // active items so far (items with tiles or with the new row)
+        for (int item = blockIdx.x; item < a.items; item += gridDim.x) {
+            int b, g, c, t0, t1, L;
+            item_range(item, b, g, c, t0, t1, L);
+            const int nch_b = (L + a.chunk - 1) / a.chunk;
+            const bool last = c == nch_b - 1;
+            if (t1 <= t0 && !last) continue;   // nothing to load, no new row: the consumers skip it too
+            const int p = n_act & 1;
+            if (n_act >= 1 && !mbar_wait(f_qfree, (n_act - 1) & 1)) break;
+            if (n_act >= 2 && !mbar_wait(&f_vsfree[p], ((n_act - 2) >> 1) & 1)) break;
+            // every row's loads go out first (q rows, and the new K/V rows for the last chunk),
+            // so the item costs one memory round trip; the angles are computed meanwhile
+            __nv_bfloat16 rq[kMaxGroup][NI], rk[NI], rv[NI];   // indices fixed after unrolling
+#pragma unroll
+            for (int r = 0; r < kMaxGroup; ++r) {
+                if (r < a.n_rep) {
+                    const __nv_bfloat16* src = a.q_in + (int64_t)b * a.q_sb + (int64_t)(g * a.n_rep + r) * a.q_sh;
+#pragma unroll
+                    for (int i = 0; i < NI; ++i) rq[r][i] = src[lane + 32 * i];
+                }
+            }
+            if (last) {
+                const __nv_bfloat16* ksrc = a.k_in + (int64_t)b * a.k_sb + (int64_t)g * a.k_sh;
+                const __nv_bfloat16* vsrc = a.v_in + (int64_t)b * a.v_sb + (int64_t)g * a.v_sh;
+#pragma unroll
+                for (int i = 0; i < NI; ++i) {
+                    rk[i] = ksrc[lane + 32 * i];
+                    rv[i] = vsrc[lane + 32 * i];
+                }
+            }
+            const RopeLane<D> rope = a.rope_cos != nullptr
+                ? rope_lane_from_tables<D>(a.rope_cos + (int64_t)b * a.rope_row_sb * D,
+                                           a.rope_sin + (int64_t)b * a.rope_row_sb * D, lane)
+                : rope_lane_compute<D>(a.positions[(int64_t)b * a.pos_sb], lane, a.log_theta);
+            __nv_bfloat16 yk[NI];
+            if (last) {
+                // the new K row (norm + RoPE) and V row, appended to cache row L-1
+                float xk[NI];
+#pragma unroll
+                for (int i = 0; i < NI; ++i) xk[i] = __bfloat162float(rk[i]);
+                const float rr = norm ? rms_scale<D>(row_sum_squares<NI>(xk, lane), a.eps) : 1.f;
+                qk_norm_rope_row<D>(xk, norm, gk, rr, rope, yk);
+                const int64_t crow = (int64_t)b * a.c_sb + (int64_t)g * a.c_sh + (int64_t)(L - 1) * a.c_st;
+#pragma unroll
+                for (int i = 0; i < NI; ++i) {
+                    const __nv_bfloat16 yv = rv[i];
+                    a.k_cache[crow + lane + 32 * i] = yk[i];
+                    a.v_cache[crow + lane + 32 * i] = yv;
+                    f_vnew[p * D + lane + 32 * i] = yv;
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < kMaxGroup; ++r) {
+                if (r >= a.n_rep) break;
+                float xq[NI];
+#pragma unroll
+                for (int i = 0; i < NI; ++i) xq[i] = __bfloat162float(rq[r][i]);
+                const float rr = norm ? rms_scale<D>(row_sum_squares<NI>(xq, lane), a.eps) : 1.f;
+                __nv_bfloat16 yq[NI];
+                qk_norm_rope_row<D>(xq, norm, gq, rr, rope, yq);
+#pragma unroll
+                for (int i = 0; i < NI; ++i) f_q[r * D + lane + 32 * i] = yq[i];
+                if (last) {
+                    // the new row's score for this head, fp32 over the bf16 rows: lanes sum
+                    // their columns in order, then a butterfly over the warp
+                    float acc = 0.f;
+#pragma unroll
+                    for (int i = 0; i < NI; ++i) acc = fmaf(__bfloat162float(yq[i]), __bfloat162float(yk[i]), acc);
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+                    if (lane == 0) f_snew[p * kMaxGroup + r] = acc * a.scale_log2;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(f_qfull);
+            ++n_act;
+        }
+        return;
+    }
     if (warp == kConsumerWarps) {
         // ------------------------------ producer ------------------------------
         if (lane == 0) {
@@ -137,12 +278,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     constexpr int KS = D / 16;   // k-steps of S = Q K^T
     constexpr int NB = D / 8;    // n-blocks of O
     bool alive = true;
+    int n_act = 0;               // fused: active items so far (matches the producer's count)
 
     for (int item = blockIdx.x; item < a.items && alive; item += gridDim.x) {
         int b, g, c, t0, t1, L;
         item_range(item, b, g, c, t0, t1, L);
         const int nch_b = (L + a.chunk - 1) / a.chunk;
-        if (t1 <= t0) {
+        // the fused step's last chunk owns the new row, even when no cached row is left for it
+        const bool last = kFused && c == nch_b - 1;
+        if (t1 <= t0 && !last) {
             if (L == 0 && c == 0) {  // empty sequence: the reference would produce no row; emit zeros
                 for (int i = threadIdx.x; i < a.n_rep * D; i += kConsumerWarps * 32)
                     a.out[(int64_t)b * a.H * D + (int64_t)g * a.n_rep * D + i] = __float2bfloat16_rn(0.f);
@@ -153,15 +297,26 @@ __global__ void __launch_bounds__(kThreads, 2)
 
         // Q fragments (A operand): rows = heads of the group, cols = head_dim.
         uint32_t qa[KS][2];
-        {
-            const __nv_bfloat16* qrow = a.q + ((int64_t)b * a.H + (int64_t)g * a.n_rep + (row_ok ? grp : 0)) * D;
+        const __nv_bfloat16* qrow;
+        const int slot = n_act & 1;   // fused: this item's new-row data slot
+        if constexpr (kFused) {
+            // the producer warp computed this item's q rows (and new-row data) into the slot
+            if (!mbar_wait(f_qfull, n_act & 1)) { alive = false; break; }
+            qrow = f_q + (row_ok ? grp : 0) * D;
+        } else {
+            qrow = a.q + ((int64_t)b * a.H + (int64_t)g * a.n_rep + (row_ok ? grp : 0)) * D;
+        }
 #pragma unroll
-            for (int ks = 0; ks < KS; ++ks) {
-                const uint32_t lo = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + tig * 2);
-                const uint32_t hi = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + tig * 2 + 8);
-                qa[ks][0] = row_ok ? lo : 0u;
-                qa[ks][1] = row_ok ? hi : 0u;
-            }
+        for (int ks = 0; ks < KS; ++ks) {
+            const uint32_t lo = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + tig * 2);
+            const uint32_t hi = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + tig * 2 + 8);
+            qa[ks][0] = row_ok ? lo : 0u;
+            qa[ks][1] = row_ok ? hi : 0u;
+        }
+        if constexpr (kFused) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(f_qfree);
+            ++n_act;
         }
         float o[NB][4];
 #pragma unroll
@@ -281,6 +436,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             float M = m_run;
 #pragma unroll
             for (int w = 1; w < kConsumerWarps; ++w) M = fmaxf(M, red_m[w * kMaxGroup + grp]);
+            const float s_new = last ? f_snew[slot * kMaxGroup + grp] : -INFINITY;   // the fused step's new row
+            M = fmaxf(M, s_new);
             const float Mu = (M == -INFINITY) ? 0.f : M;
             float sc[kConsumerWarps];
             sc[0] = ex2_approx(m_run - Mu);
@@ -290,6 +447,10 @@ __global__ void __launch_bounds__(kThreads, 2)
                 sc[w] = ex2_approx(red_m[w * kMaxGroup + grp] - Mu);
                 Ltot += red_l[w * kMaxGroup + grp] * sc[w];
             }
+            // the new row enters like a tile row: fp32 p in the sum, p rounded to bf16 for P.V
+            const float p_new = last ? ex2_approx(s_new - Mu) : 0.f;
+            const float p_new_bf = __bfloat162float(__float2bfloat16_rn(p_new));
+            Ltot += p_new;
             const int head = g * a.n_rep + grp;
             if (nch_b == 1) {
                 const float inv = (Ltot > 0.f) ? 1.f / Ltot : 0.f;
@@ -303,6 +464,10 @@ __global__ void __launch_bounds__(kThreads, 2)
                                                                           j * 8 + tig * 2);
                         x0 += r.x * sc[w];
                         x1 += r.y * sc[w];
+                    }
+                    if (last) {
+                        x0 += p_new_bf * __bfloat162float(f_vnew[slot * D + j * 8 + tig * 2]);
+                        x1 += p_new_bf * __bfloat162float(f_vnew[slot * D + j * 8 + tig * 2 + 1]);
                     }
                     *reinterpret_cast<uint32_t*>(orow + j * 8 + tig * 2) = pack_bf16x2(x0 * inv, x1 * inv);
                 }
@@ -319,12 +484,22 @@ __global__ void __launch_bounds__(kThreads, 2)
                         x0 += r.x * sc[w];
                         x1 += r.y * sc[w];
                     }
+                    if (last) {
+                        x0 += p_new_bf * __bfloat162float(f_vnew[slot * D + j * 8 + tig * 2]);
+                        x1 += p_new_bf * __bfloat162float(f_vnew[slot * D + j * 8 + tig * 2 + 1]);
+                    }
                     *reinterpret_cast<float2*>(prow + j * 8 + tig * 2) = make_float2(x0, x1);
                 }
                 if (tig == 0) {
                     a.part_ml[pidx * 2 + 0] = M;
                     a.part_ml[pidx * 2 + 1] = Ltot;
                 }
+            }
+        }
+        if constexpr (kFused) {
+            if (warp == 0) {   // warp 0 alone read the slot's new-row data
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&f_vsfree[slot]);
             }
         }
         asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
@@ -423,6 +598,41 @@ size_t workspace_bytes_for(int B, int H, int Hkv, int D, int max_len) {
     return (bytes + 255) & ~size_t(255);
 }
 
+// Plans the chunks, places the partials in `workspace` and launches the split kernel (and,
+// when a sequence spans several chunks, the combine kernel), both with programmatic
+// dependent launch.  `a` arrives with its per-call fields set.
+template <int D, bool kFused>
+int launch_decode_d(DecodeArgs& a, const CUtensorMap& tmK, const CUtensorMap& tmV, int num_sms, void* workspace,
+                    cudaStream_t s) {
+    plan_chunks(a.B, a.Hkv, a.max_len, 2 * num_sms, a.chunk, a.nch);
+    const size_t parts = (size_t)a.B * a.Hkv * a.nch * a.n_rep;
+    a.part_o = reinterpret_cast<float*>(workspace);
+    a.part_ml = a.part_o + parts * D;
+    a.items = a.B * a.Hkv * a.nch;
+    const int grid = std::min(a.items, 2 * num_sms);
+    auto kern = decode_split_kernel<D, kFused>;
+    const int smem = kFused ? DecodeCfg<D>::kSmemBytesFused : DecodeCfg<D>::kSmemBytes;
+    if (int st = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                            "decode smem attribute"))
+        return st;
+    if (int st = check_cuda(launch_pdl(kern, dim3(grid), dim3(kFused ? kThreadsFused : kThreads), smem, s, tmK, tmV, a),
+                            "decode_split_kernel launch"))
+        return st;
+    if (a.nch > 1) {
+        if (int st = check_cuda(launch_pdl(decode_combine_kernel<D>, dim3(a.Hkv, a.B), dim3(128), 0, s, a),
+                                "decode_combine_kernel launch"))
+            return st;
+    }
+    return MLLM_OK;
+}
+
+template <bool kFused>
+int launch_decode(DecodeArgs& a, int head_dim, const CUtensorMap& tmK, const CUtensorMap& tmV, int num_sms,
+                  void* workspace, cudaStream_t s) {
+    return head_dim == 128 ? launch_decode_d<128, kFused>(a, tmK, tmV, num_sms, workspace, s)
+                           : launch_decode_d<64, kFused>(a, tmK, tmV, num_sms, workspace, s);
+}
+
 }  // namespace
 
 MLLM_DEFINE_STATUS_READER(decode)
@@ -473,7 +683,7 @@ extern "C" int mllm_decode_attention_bf16(const void* q, const void* k_cache, co
                                64, kTile))
         return st;
 
-    DecodeArgs a;
+    DecodeArgs a = {};
     a.q = (const __nv_bfloat16*)q;
     a.kv_lens = kv_lens;
     a.out = (__nv_bfloat16*)out;
@@ -482,43 +692,8 @@ extern "C" int mllm_decode_attention_bf16(const void* q, const void* k_cache, co
     a.Hkv = num_kv_heads;
     a.n_rep = n_rep;
     a.max_len = max_kv_len;
-    plan_chunks(batch, num_kv_heads, max_kv_len, 2 * num_sms, a.chunk, a.nch);
-    const size_t parts = (size_t)batch * num_kv_heads * a.nch * n_rep;
-    a.part_o = reinterpret_cast<float*>(workspace);
-    a.part_ml = a.part_o + parts * head_dim;
-    a.items = batch * num_kv_heads * a.nch;
     a.scale_log2 = (float)((double)softmax_scale * 1.4426950408889634);
-
-    const int grid = std::min(a.items, 2 * num_sms);
-    cudaStream_t s = (cudaStream_t)stream;
-    if (head_dim == 128) {
-        auto kern = decode_split_kernel<128>;
-        const int smem = DecodeCfg<128>::kSmemBytes;
-        if (int st = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-                                "decode smem attribute"))
-            return st;
-        if (int st = check_cuda(launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, tmK, tmV, a),
-                                "decode_split_kernel launch"))
-            return st;
-        if (a.nch > 1 &&
-            check_cuda(launch_pdl(decode_combine_kernel<128>, dim3(num_kv_heads, batch), dim3(128), 0, s, a),
-                       "decode_combine_kernel launch"))
-            return MLLM_ERR_CUDA;
-    } else {
-        auto kern = decode_split_kernel<64>;
-        const int smem = DecodeCfg<64>::kSmemBytes;
-        if (int st = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-                                "decode smem attribute"))
-            return st;
-        if (int st = check_cuda(launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, tmK, tmV, a),
-                                "decode_split_kernel launch"))
-            return st;
-        if (a.nch > 1 &&
-            check_cuda(launch_pdl(decode_combine_kernel<64>, dim3(num_kv_heads, batch), dim3(128), 0, s, a),
-                       "decode_combine_kernel launch"))
-            return MLLM_ERR_CUDA;
-    }
-    if (int st = check_cuda(cudaGetLastError(), "decode_combine_kernel launch")) return st;
+    if (int st = launch_decode<false>(a, head_dim, tmK, tmV, num_sms, workspace, (cudaStream_t)stream)) return st;
     return ok();
 }
 
@@ -612,7 +787,7 @@ extern "C" int mllm_decode_attention_noalloc_bf16(const void* q, const void* k_c
 
     // Every partial the combine step reads is written earlier in the same call, so the scratch
     // needs no clearing between calls.
-    DecodeArgs a;
+    DecodeArgs a = {};
     a.q = (const __nv_bfloat16*)q;
     a.kv_lens = kv_lens;
     a.out = (__nv_bfloat16*)out;
@@ -621,42 +796,88 @@ extern "C" int mllm_decode_attention_noalloc_bf16(const void* q, const void* k_c
     a.Hkv = num_kv_heads;
     a.n_rep = n_rep;
     a.max_len = max_kv_len;
-    plan_chunks(batch, num_kv_heads, max_kv_len, 2 * num_sms, a.chunk, a.nch);
-    const size_t parts = (size_t)batch * num_kv_heads * a.nch * n_rep;
-    a.part_o = reinterpret_cast<float*>(scratch);
-    a.part_ml = a.part_o + parts * head_dim;
-    a.items = batch * num_kv_heads * a.nch;
     a.scale_log2 = (float)((double)softmax_scale * 1.4426950408889634);
+    if (int st = launch_decode<false>(a, head_dim, tmK, tmV, num_sms, scratch, (cudaStream_t)stream)) return st;
+    return ok();
+}
 
-    const int grid = std::min(a.items, 2 * num_sms);
-    cudaStream_t s = (cudaStream_t)stream;
-    if (head_dim == 128) {
-        const int smem = DecodeCfg<128>::kSmemBytes;
-        if (int st = check_cuda(cudaFuncSetAttribute(decode_split_kernel<128>,
-                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-                                "decode smem attribute"))
-            return st;
-        if (int st = check_cuda(launch_pdl(decode_split_kernel<128>, dim3(grid), dim3(kThreads), smem, s, tmK, tmV, a),
-                                "decode_split_kernel launch"))
-            return st;
-        if (a.nch > 1 &&
-            check_cuda(launch_pdl(decode_combine_kernel<128>, dim3(num_kv_heads, batch), dim3(128), 0, s, a),
-                       "decode_combine_kernel launch"))
-            return MLLM_ERR_CUDA;
-    } else {
-        const int smem = DecodeCfg<64>::kSmemBytes;
-        if (int st = check_cuda(cudaFuncSetAttribute(decode_split_kernel<64>,
-                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-                                "decode smem attribute"))
-            return st;
-        if (int st = check_cuda(launch_pdl(decode_split_kernel<64>, dim3(grid), dim3(kThreads), smem, s, tmK, tmV, a),
-                                "decode_split_kernel launch"))
-            return st;
-        if (a.nch > 1 &&
-            check_cuda(launch_pdl(decode_combine_kernel<64>, dim3(num_kv_heads, batch), dim3(128), 0, s, a),
-                       "decode_combine_kernel launch"))
-            return MLLM_ERR_CUDA;
-    }
-    if (int st = check_cuda(cudaGetLastError(), "decode_combine_kernel launch")) return st;
+// ---------------------------------------------------------------------------------------------
+// Fused decode step: the QKV epilogue of one new token per sequence (QK-RMSNorm, RoPE, KV
+// append) and the decode attention over the cache including that token, in one launch of the
+// split kernel (plus the combine kernel when a sequence spans several chunks).
+// ---------------------------------------------------------------------------------------------
+extern "C" int mllm_decode_step_bf16(const void* q, int64_t q_sb, int64_t q_sh, const void* k, int64_t k_sb,
+                                     int64_t k_sh, const void* v, int64_t v_sb, int64_t v_sh,
+                                     const int64_t* positions, int64_t pos_sb, double rope_theta,
+                                     const float* rope_cos, const float* rope_sin, int64_t rope_row_sb,
+                                     const void* q_norm_weight, const void* k_norm_weight, double rms_norm_eps,
+                                     void* k_cache, void* v_cache, int64_t cache_sb, int64_t cache_sh,
+                                     int64_t cache_st, const int32_t* kv_lens, int batch, int num_heads,
+                                     int num_kv_heads, int head_dim, int max_kv_len, float softmax_scale, void* out,
+                                     void* workspace, size_t workspace_bytes, mllm_stream_t stream) {
+    if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_kv_len <= 0)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_step: bad sizes");
+    if (num_heads % num_kv_heads != 0)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "Attention: num_heads must be divisible by num_kv_heads.");
+    if (head_dim != 64 && head_dim != 128) return fail(MLLM_ERR_UNSUPPORTED, "decode_step: head_dim must be 64 or 128");
+    const int n_rep = num_heads / num_kv_heads;
+    if (n_rep > kMaxGroup) return fail(MLLM_ERR_UNSUPPORTED, "decode_step: GQA group larger than 8");
+    if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale))
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_step: softmax_scale must be positive");
+    if ((q_norm_weight == nullptr) != (k_norm_weight == nullptr))
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_step: give both q/k norm weights or neither");
+    if ((rope_cos == nullptr) != (rope_sin == nullptr))
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_step: give both rope tables or neither");
+    if (rope_cos == nullptr && positions == nullptr)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_step: positions or rope tables required");
+    if (rope_cos == nullptr && !(rope_theta > 0.0))
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_step: rope_theta must be positive");
+    if (batch == 0) return ok();
+    if (!q || !k || !v || !k_cache || !v_cache || !out)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_step: null pointer");
+    if (!aligned(out, 4)) return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_step: out misaligned");
+    const size_t need = workspace_bytes_for(batch, num_heads, num_kv_heads, head_dim, max_kv_len);
+    if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+        return fail(MLLM_ERR_WORKSPACE, "decode_step: workspace missing, misaligned or smaller than "
+                                        "mllm_decode_attention_workspace_size()");
+    int num_sms = 0;
+    if (int st = require_sm100(&num_sms)) return st;
+
+    CUtensorMap tmK, tmV;
+    if (int st = encode_kv_map(&tmK, k_cache, head_dim, max_kv_len, num_kv_heads, batch, cache_st, cache_sh, cache_sb,
+                               64, kTile))
+        return st;
+    if (int st = encode_kv_map(&tmV, v_cache, head_dim, max_kv_len, num_kv_heads, batch, cache_st, cache_sh, cache_sb,
+                               64, kTile))
+        return st;
+
+    DecodeArgs a = {};
+    a.kv_lens = kv_lens;
+    a.out = (__nv_bfloat16*)out;
+    a.B = batch;
+    a.H = num_heads;
+    a.Hkv = num_kv_heads;
+    a.n_rep = n_rep;
+    a.max_len = max_kv_len;
+    a.scale_log2 = (float)((double)softmax_scale * 1.4426950408889634);
+    a.q_in = (const __nv_bfloat16*)q;
+    a.k_in = (const __nv_bfloat16*)k;
+    a.v_in = (const __nv_bfloat16*)v;
+    a.q_sb = q_sb; a.q_sh = q_sh;
+    a.k_sb = k_sb; a.k_sh = k_sh;
+    a.v_sb = v_sb; a.v_sh = v_sh;
+    a.positions = positions;
+    a.pos_sb = pos_sb;
+    a.log_theta = rope_cos ? 0.f : rope_log_theta(rope_theta);
+    a.rope_cos = rope_cos;
+    a.rope_sin = rope_sin;
+    a.rope_row_sb = rope_row_sb;
+    a.q_gamma = (const __nv_bfloat16*)q_norm_weight;
+    a.k_gamma = (const __nv_bfloat16*)k_norm_weight;
+    a.eps = (float)rms_norm_eps;   // the reference adds the double eps to a float tensor
+    a.k_cache = (__nv_bfloat16*)k_cache;
+    a.v_cache = (__nv_bfloat16*)v_cache;
+    a.c_sb = cache_sb; a.c_sh = cache_sh; a.c_st = cache_st;
+    if (int st = launch_decode<true>(a, head_dim, tmK, tmV, num_sms, workspace, (cudaStream_t)stream)) return st;
     return ok();
 }

@@ -5,19 +5,14 @@
 //   Attention.h:157-177                 RoPE on q and k (RoPE.h:68-89), fp32, cast bf16
 //   Attention.h:183-208                 KV append -- rows written in place (no torch::cat)
 //
-// Work split: one warp per (token, head).  Lane L holds the elements d = L + 32*i
-// (i < D/32).  That layout gives two things at once:
-//   * RMSNorm's fp32 sum of squares in exactly the reference CPU LibTorch order
-//     (8-wide vectors with 4 interleaved accumulators: lane L = 8k + j holds accumulator
-//     P_k[j]; then ((P0+P1)+P2)+P3 per j, then j = 0..7 in sequence), so the bf16 result is
-//     bit-identical to the reference;
-//   * both halves of every RoPE pair (d, d + D/2) in the same lane: no shuffles.
-// Every fp32 step uses explicit round-to-nearest intrinsics so no FMA contraction occurs.
+// Work split: one warp per (token, head), lane L holding the elements d = L + 32*i; the
+// per-row arithmetic (reference reduction order, explicit rounding) is in qkv_math.cuh and is
+// shared with the fused decode step.
 //
 // Memory: each head row is read once (D*2 bytes) and written once (q_out or the cache row).
 #include "common.cuh"
 #include "host_util.h"
-#include "rope_math.cuh"
+#include "qkv_math.cuh"
 
 namespace mllm_b200 {
 namespace {
@@ -46,24 +41,6 @@ struct EpilogueArgs {
 };
 
 constexpr int kWarps = 8;
-
-// Sum of squares of a head row in the reference's reduction order (see file comment).
-template <int NI>
-__device__ __forceinline__ float row_sum_squares(const float (&x)[NI], int lane) {
-    float p = 0.f;
-#pragma unroll
-    for (int i = 0; i < NI; ++i) p = __fadd_rn(p, __fmul_rn(x[i], x[i]));
-    const int j = lane & 7;
-    const float p0 = __shfl_sync(0xffffffffu, p, j);
-    const float p1 = __shfl_sync(0xffffffffu, p, j + 8);
-    const float p2 = __shfl_sync(0xffffffffu, p, j + 16);
-    const float p3 = __shfl_sync(0xffffffffu, p, j + 24);
-    const float acc = __fadd_rn(__fadd_rn(__fadd_rn(p0, p1), p2), p3);
-    float total = 0.f;
-#pragma unroll
-    for (int jj = 0; jj < 8; ++jj) total = __fadd_rn(total, __shfl_sync(0xffffffffu, acc, jj));
-    return total;
-}
 
 // Locates head `head` (q heads first, then k, then v) of token (b, s).
 struct HeadRef {
@@ -100,8 +77,6 @@ __device__ __forceinline__ HeadRef locate_head(const EpilogueArgs& a, int head, 
 template <int D, int HPW>
 __global__ void __launch_bounds__(kWarps * 32, 6) qkv_epilogue_kernel(EpilogueArgs a) {
     constexpr int NI = D / 32;     // elements per lane
-    constexpr int HALF = D / 2;
-    constexpr int PAIR = NI / 2;   // slot i pairs with slot i + PAIR (distance D/2)
     __shared__ float s_cos[D];
     __shared__ float s_sin[D];
     __shared__ float s_gamma[2][D];   // q / k per-head norm weights (fp32 copies of the bf16 values)
@@ -144,15 +119,8 @@ __global__ void __launch_bounds__(kWarps * 32, 6) qkv_epilogue_kernel(EpilogueAr
             s_sin[d] = a.rope_sin[row * D + d];
         }
     } else {
-        const int64_t pos = a.positions[(int64_t)b * a.pos_sb + (int64_t)s * a.pos_ss];
-        for (int j = tid; j < HALF; j += blockDim.x) {
-            float c, sn;
-            rope_angle_cos_sin(pos, j, D, a.log_theta, c, sn);
-            s_cos[j] = c;
-            s_cos[j + HALF] = c;
-            s_sin[j] = sn;
-            s_sin[j + HALF] = sn;
-        }
+        rope_angles_for_position<D>(a.positions[(int64_t)b * a.pos_sb + (int64_t)s * a.pos_ss], tid, blockDim.x,
+                                    a.log_theta, s_cos, s_sin);
     }
     __syncthreads();
 
@@ -166,29 +134,17 @@ __global__ void __launch_bounds__(kWarps * 32, 6) qkv_epilogue_kernel(EpilogueAr
 #pragma unroll
             for (int i = 0; i < NI; ++i) y[i] = __float2bfloat16_rn(x[t][i]);   // exact: x came from bf16
         } else {
+            // RMSNorm.h:48-63 (var = mean(x^2); x * rsqrt(var + eps) * w; cast to bf16), then
+            // RoPE.h:77-88 on the pairs (d, d + D/2).
             float xv[NI];
 #pragma unroll
             for (int i = 0; i < NI; ++i) xv[i] = x[t][i];
-            if (r.gamma != nullptr) {
-                // RMSNorm.h:48-63: var = mean(x^2); x * rsqrt(var + eps) * w; cast to bf16.
-                const float var = __fdiv_rn(row_sum_squares<NI>(xv, lane), (float)D);
-                const float rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));
-                const float* gw = s_gamma[r.kind];
+            const bool norm = r.gamma != nullptr;
+            const float rr = norm ? rms_scale<D>(row_sum_squares<NI>(xv, lane), a.eps) : 1.f;
+            float gl[NI];
 #pragma unroll
-                for (int i = 0; i < NI; ++i) {
-                    const float w = gw[lane + 32 * i];
-                    xv[i] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(xv[i], rr), w)));
-                }
-            }
-            // RoPE.h:77-88 on the pairs (d, d + D/2).
-#pragma unroll
-            for (int i = 0; i < PAIR; ++i) {
-                const int j = lane + 32 * i;
-                float lo, hi;
-                rope_rotate_pair(xv[i], xv[i + PAIR], s_cos[j], s_sin[j], s_cos[j + HALF], s_sin[j + HALF], lo, hi);
-                y[i] = __float2bfloat16_rn(lo);
-                y[i + PAIR] = __float2bfloat16_rn(hi);
-            }
+            for (int i = 0; i < NI; ++i) gl[i] = norm ? s_gamma[r.kind][lane + 32 * i] : 0.f;
+            qk_norm_rope_row<D>(xv, norm, gl, rr, rope_lane_from_tables<D>(s_cos, s_sin, lane), y);
         }
         __nv_bfloat16* dst;
         if (r.kind == 0) {

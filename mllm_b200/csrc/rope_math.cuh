@@ -12,14 +12,19 @@ namespace mllm_b200 {
 // float tensor op (RoPE.h:48-50: `idx / D * log_theta` on a float tensor).
 inline float rope_log_theta(double theta) { return static_cast<float>(std::log(theta)); }
 
-// cos/sin of the RoPE angle for column j (< D/2) at integer position `pos`.
-__device__ __forceinline__ void rope_angle_cos_sin(int64_t pos, int j, int head_dim, float log_theta, float& c,
-                                                   float& s) {
+// The RoPE angle for column j (< D/2) at integer position `pos`.
+__device__ __forceinline__ float rope_angle(int64_t pos, int j, int head_dim, float log_theta) {
     const float idx = (float)(2 * j);
     const float ratio = __fdiv_rn(idx, (float)head_dim);            // idx / D
     const float arg = -__fmul_rn(ratio, log_theta);                 // (.. * log_theta).neg()
     const float inv_freq = expf(arg);                               // .exp()
-    const float angle = __fmul_rn((float)pos, inv_freq);            // pos_f32 * inv_freq
+    return __fmul_rn((float)pos, inv_freq);                         // pos_f32 * inv_freq
+}
+
+// cos/sin of the RoPE angle for column j (< D/2) at integer position `pos`.
+__device__ __forceinline__ void rope_angle_cos_sin(int64_t pos, int j, int head_dim, float log_theta, float& c,
+                                                   float& s) {
+    const float angle = rope_angle(pos, j, head_dim, log_theta);
     c = cosf(angle);
     s = sinf(angle);
 }

@@ -5,10 +5,11 @@
 //   Attention::ForwardProjected (Attention.h:100-326) RoPE, KV append, GQA attention, o_proj
 // and the same argument checks and messages (Attention.h:42-47, 129-144).  Behind them the
 // LibTorch chain (RoPE ops, torch::cat, repeat_interleave, fp32 score matrix, mask, softmax,
-// two matmuls, merge) becomes three B200 kernels reached through the C ABI (mllm_attn.h):
-//   mllm_qkv_epilogue_bf16       RoPE (+ optional per-head QK-RMSNorm) + in-place KV append
-//   mllm_prefill_attention_bf16  S > 1: causal GQA attention on tcgen05 tensor cores
-//   mllm_decode_attention_bf16   S == 1: split-K flash-decode over the cache
+// two matmuls, merge) becomes B200 kernels reached through the C ABI (mllm_attn.h):
+//   S > 1:  mllm_qkv_epilogue_bf16 (RoPE + optional per-head QK-RMSNorm + in-place KV append),
+//           then mllm_prefill_attention_bf16 (causal GQA attention on tcgen05 tensor cores)
+//   S == 1: mllm_decode_step_bf16 (the same epilogue for the new token fused into split-K
+//           flash-decode over the cache, one launch)
 // The projections stay LibTorch GEMMs (Linear::Forward), as in the reference.
 //
 // ForwardProjectedNormed is the one addition: it takes the per-head q/k RMSNorm weights that
@@ -136,39 +137,46 @@ namespace mllm
                     throw std::runtime_error("RMSNorm: last dim of x must match weight length.");
                 }
             }
-            auto q_rot = torch::empty({B, num_heads, S, head_dim}, q.options());
             const mllm_stream_t stream = b200::CurrentStream();
-            b200::Check(
-                mllm_qkv_epilogue_bf16(
-                    q.data_ptr(), q.stride(0), q.stride(2), q.stride(1),
-                    k.data_ptr(), k.stride(0), k.stride(2), k.stride(1),
-                    v.data_ptr(), v.stride(0), v.stride(2), v.stride(1),
-                    (int)B, (int)S, num_heads, num_kv_heads, head_dim,
-                    pos.data_ptr<int64_t>(), 0, pos.stride(0), rope_theta,
-                    nullptr, nullptr, 0, 0,
-                    qn.defined() ? qn.data_ptr() : nullptr, kn.defined() ? kn.data_ptr() : nullptr,
-                    rms_norm_eps, q_rot.data_ptr(),
-                    ks.data_ptr(), vs.data_ptr(), ks.stride(0), ks.stride(1), ks.stride(2), cache->Capacity(),
-                    nullptr, start, stream),
-                "Attention (QKV epilogue)");
-            cache->SetLength(start + S);
-            const int64_t L = cache->length;
-
             const float scale = (float)(1.0 / std::sqrt((double)head_dim));
             auto out = torch::empty({B, S, (int64_t)num_heads * head_dim}, q.options());
             if (S == 1)
             {
+                // decode: the new token's epilogue (QK-norm, RoPE, append at row `start`) and the
+                // attention over all start + 1 rows in one fused launch
+                const int64_t L = start + 1;
                 const size_t bytes =
                     mllm_decode_attention_workspace_size((int)B, num_heads, num_kv_heads, head_dim, (int)L);
                 auto ws = b200::DecodeWorkspace(bytes, q.device());
-                b200::Check(mllm_decode_attention_bf16(q_rot.data_ptr(), ks.data_ptr(), vs.data_ptr(), ks.stride(0),
-                                                       ks.stride(1), ks.stride(2), nullptr, (int)B, num_heads,
-                                                       num_kv_heads, head_dim, (int)L, scale, out.data_ptr(),
-                                                       ws.data_ptr(), (size_t)ws.numel(), stream),
-                            "Attention (decode)");
+                b200::Check(
+                    mllm_decode_step_bf16(
+                        q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), k.stride(1),
+                        v.data_ptr(), v.stride(0), v.stride(1), pos.data_ptr<int64_t>(), 0, rope_theta,
+                        nullptr, nullptr, 0, qn.defined() ? qn.data_ptr() : nullptr,
+                        kn.defined() ? kn.data_ptr() : nullptr, rms_norm_eps, ks.data_ptr(), vs.data_ptr(),
+                        ks.stride(0), ks.stride(1), ks.stride(2), nullptr, (int)B, num_heads, num_kv_heads,
+                        head_dim, (int)L, scale, out.data_ptr(), ws.data_ptr(), (size_t)ws.numel(), stream),
+                    "Attention (decode step)");
+                cache->SetLength(L);
             }
             else
             {
+                auto q_rot = torch::empty({B, num_heads, S, head_dim}, q.options());
+                b200::Check(
+                    mllm_qkv_epilogue_bf16(
+                        q.data_ptr(), q.stride(0), q.stride(2), q.stride(1),
+                        k.data_ptr(), k.stride(0), k.stride(2), k.stride(1),
+                        v.data_ptr(), v.stride(0), v.stride(2), v.stride(1),
+                        (int)B, (int)S, num_heads, num_kv_heads, head_dim,
+                        pos.data_ptr<int64_t>(), 0, pos.stride(0), rope_theta,
+                        nullptr, nullptr, 0, 0,
+                        qn.defined() ? qn.data_ptr() : nullptr, kn.defined() ? kn.data_ptr() : nullptr,
+                        rms_norm_eps, q_rot.data_ptr(),
+                        ks.data_ptr(), vs.data_ptr(), ks.stride(0), ks.stride(1), ks.stride(2), cache->Capacity(),
+                        nullptr, start, stream),
+                    "Attention (QKV epilogue)");
+                cache->SetLength(start + S);
+                const int64_t L = cache->length;
                 b200::Check(mllm_prefill_attention_bf16(q_rot.data_ptr(), ks.data_ptr(), vs.data_ptr(), ks.stride(0),
                                                         ks.stride(1), ks.stride(2), (int)B, num_heads, num_kv_heads,
                                                         head_dim, (int)S, (int)L, scale, out.data_ptr(), stream),

@@ -219,6 +219,45 @@ def decode_attention(q: torch.Tensor, kv_cache: KVCache, num_kv_heads: int,
     return out
 
 
+def decode_step(q, k, v, kv_cache: KVCache, positions: torch.Tensor, rope_theta: float, num_kv_heads: int,
+                q_norm_weight=None, k_norm_weight=None, eps: float = 1e-6, rope_table=None) -> torch.Tensor:
+    """One new token per sequence through the fused step: QK-RMSNorm (optional) + RoPE + KV
+    append + decode attention in one launch.  q [B,H,1,D], k/v [B,Hkv,1,D] (strided views of the
+    projections); positions int64 [1] (shared) or [B] / [B, 1].  The new rows go to slot
+    lengths[b] of each sequence and the lengths advance by one.  Returns [B, 1, H*D]."""
+    for n, t in (("q", q), ("k", k), ("v", v)):
+        _check_cuda_bf16(n, t)
+        if t.dim() != 4 or t.size(2) != 1 or t.stride(3) != 1:
+            raise RuntimeError(f"Attention: {n} must be [B, h, 1, D] with D contiguous")
+    B, H, _, D = q.shape
+    if H % num_kv_heads != 0:
+        raise RuntimeError("Attention: num_heads must be divisible by num_kv_heads.")
+    pos = positions.to(torch.int64).reshape(-1)
+    pos_sb = 0 if pos.numel() == 1 else pos.stride(0)
+    cos = sin = None
+    rsb = 0
+    if rope_table is not None:
+        cos, sin = (t.to(torch.float32).contiguous() for t in rope_table)
+        rsb = 0 if cos.shape[0] == 1 else 1
+    qn = kn = None
+    if q_norm_weight is not None:
+        qn = q_norm_weight.to(BF16).contiguous()
+        kn = k_norm_weight.to(BF16).contiguous()
+    kv_cache.advance(1)   # raises before any launch if the cache is full
+    L = min(max(kv_cache.host_lengths()), kv_cache.capacity)
+    out = torch.empty((B, 1, H * D), dtype=BF16, device=q.device)
+    lib = abi.load()
+    nbytes = lib.mllm_decode_attention_workspace_size(B, H, num_kv_heads, D, L)
+    ws = _WS.get(nbytes, q.device)
+    csb, csh, cst = kv_cache.strides
+    abi.call("mllm_decode_step_bf16",
+             _ptr(q), q.stride(0), q.stride(1), _ptr(k), k.stride(0), k.stride(1), _ptr(v), v.stride(0), v.stride(1),
+             _ptr(pos), pos_sb, float(rope_theta), _ptr(cos), _ptr(sin), rsb, _ptr(qn), _ptr(kn), float(eps),
+             _ptr(kv_cache.key_buf), _ptr(kv_cache.value_buf), csb, csh, cst, _ptr(kv_cache.lengths),
+             B, H, num_kv_heads, D, L, 1.0 / math.sqrt(D), _ptr(out), _ptr(ws), ws.numel(), abi.stream_handle())
+    return out
+
+
 def _linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """Linear::Forward (Linear.h:33-68): x @ w.T in the input dtype (a cuBLAS GEMM)."""
     if x.size(-1) != w.size(1):
@@ -243,10 +282,11 @@ class Attention:
         if cache is None:  # no cache: attend over this call's rows only (Attention.h:183 skipped)
             cache = KVCache(B, num_kv_heads, D, S, device=q.device)
         pos = position_ids.to(device=q.device)
-        qr = qkv_epilogue(q, k, v, cache, pos, rope_theta, q_norm_weight, k_norm_weight, rms_norm_eps)
-        if S == 1:
-            out = decode_attention(qr, cache, num_kv_heads)
+        if S == 1:   # decode: epilogue and attention fused in one launch
+            out = decode_step(q, k, v, cache, pos, rope_theta, num_kv_heads, q_norm_weight, k_norm_weight,
+                              rms_norm_eps)
         else:
+            qr = qkv_epilogue(q, k, v, cache, pos, rope_theta, q_norm_weight, k_norm_weight, rms_norm_eps)
             out = prefill_attention(qr, cache, num_kv_heads)
         return _linear(out, w_o)
 

@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_status_strings(lib):
-    assert lib.mllm_attn_abi_version() == 1
+    assert lib.mllm_attn_abi_version() == 2
     for code in abi.STATUS_NAMES:
         assert lib.mllm_attn_status_string(code)
     assert lib.mllm_attn_status_string(99) == b"unknown status"
@@ -53,6 +53,15 @@ def test_host_side_argument_validation(lib):
     st = lib.mllm_decode_attention_bf16(None, None, None, 0, 0, 0, None, 1, 32, 2, 128, 16, 0.1, None,
                                         None, 0, None)
     assert st == 2
+    # fused decode step: the decode checks plus the epilogue's pairing rules
+    def step(H, Hkv, D, q_norm=None, k_norm=None, theta=1e6):
+        return lib.mllm_decode_step_bf16(None, 0, 0, None, 0, 0, None, 0, 0, None, 0, theta, None, None, 0,
+                                         q_norm, k_norm, 1e-6, None, None, 0, 0, 0, None, 1, H, Hkv, D, 16, 0.1,
+                                         None, None, 0, None)
+    assert step(6, 4, 128) == 1 and b"divisible" in lib.mllm_attn_last_error()
+    assert step(8, 2, 96) == 2
+    assert step(8, 2, 128, q_norm=1) == 1 and b"norm weights" in lib.mllm_attn_last_error()
+    assert step(8, 2, 128, theta=0.0) == 1 and b"positions" in lib.mllm_attn_last_error()
 
 
 def test_workspace_size(lib):

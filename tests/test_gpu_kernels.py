@@ -172,6 +172,68 @@ def test_decode_vs_oracle(rt, B, H, Hkv, D, lens):
 
 
 # ---------------------------------------------------------------------------------------
+# Fused decode step (epilogue of the new token + decode in one launch)
+# ---------------------------------------------------------------------------------------
+
+DECODE_STEP_CASES = [
+    # B, H, Hkv, D, cache rows before the new token (per sequence), QK-norm, rope table
+    (4, 32, 8, 128, [0, 1, 63, 64], True, False),          # first token of a sequence; tile edges
+    (3, 32, 8, 128, [255, 256, 1023], True, False),        # the new row alone in the last chunk
+    (8, 40, 8, 128, [5000, 17, 4096, 300, 2047, 2048, 999, 12000], True, False),   # ragged, GQA 5
+    (2, 32, 4, 64, [511, 70], False, False),               # TinyLlama geometry (no QK-norm)
+    (2, 16, 4, 128, [100, 4095], True, True),              # caller-given RoPE table rows
+]
+
+
+@pytest.mark.parametrize("B,H,Hkv,D,prior,qk_norm,table", DECODE_STEP_CASES)
+def test_decode_step_equals_epilogue_then_decode(rt, B, H, Hkv, D, prior, qk_norm, table):
+    """The fused step writes bit-identical cache rows to the epilogue kernel and the same
+    attention output as the epilogue + decode pair (up to fp32 summation order); both are also
+    checked against the oracle."""
+    rng = np.random.default_rng(sum(prior) + H)
+    cap = max(prior) + 1 + 40
+    g = torch.Generator(device="cuda").manual_seed(len(prior))
+    a = rt.KVCache(B, Hkv, D, cap, zero=False)
+    a.key_buf.normal_(generator=g)
+    a.value_buf.normal_(generator=g)
+    a.key_buf[:, :, max(prior):].fill_(float("nan"))   # nothing past the new rows may leak
+    a.value_buf[:, :, max(prior):].fill_(float("nan"))
+    for bb, L in enumerate(prior):
+        a.key_buf[bb, :, L:].fill_(float("nan"))
+        a.value_buf[bb, :, L:].fill_(float("nan"))
+    a.set_lengths(prior)
+    bcache = rt.KVCache(B, Hkv, D, cap, zero=False)
+    bcache.key_buf.copy_(a.key_buf)
+    bcache.value_buf.copy_(a.value_buf)
+    bcache.set_lengths(prior)
+    row = (H + 2 * Hkv) * D
+    proj = f32_to_torch_bf16(O.round_bf16((rng.standard_normal((B, 1, row)) * 0.7).astype(np.float32)), "cuda")
+    q = proj[:, :, : H * D].view(B, 1, H, D).transpose(1, 2)
+    k = proj[:, :, H * D:(H + Hkv) * D].view(B, 1, Hkv, D).transpose(1, 2)
+    v = proj[:, :, (H + Hkv) * D:].view(B, 1, Hkv, D).transpose(1, 2)
+    gq = gk = None
+    if qk_norm:
+        gq = f32_to_torch_bf16(O.round_bf16((1 + 0.1 * rng.standard_normal(D)).astype(np.float32)), "cuda")
+        gk = f32_to_torch_bf16(O.round_bf16((1 + 0.1 * rng.standard_normal(D)).astype(np.float32)), "cuda")
+    pos = torch.tensor(prior, dtype=torch.int64, device="cuda")      # each sequence at its own position
+    rope_table = rt.RoPE.build_cos_sin(pos, D, 1e6) if table else None
+    # the separate pair: epilogue (positions [B, 1]) then decode
+    qr = rt.qkv_epilogue(q, k, v, a, pos.view(B, 1), 1e6, gq, gk, 1e-6, rope_table=rope_table)
+    want = rt.decode_attention(qr, a, Hkv).float()
+    got = rt.decode_step(q, k, v, bcache, pos, 1e6, Hkv, gq, gk, 1e-6, rope_table=rope_table).float()
+    assert bcache.host_lengths() == [L + 1 for L in prior]
+    assert torch.equal(bcache.key_buf.view(torch.int16), a.key_buf.view(torch.int16))
+    assert torch.equal(bcache.value_buf.view(torch.int16), a.value_buf.view(torch.int16))
+    assert torch.isfinite(got).all()
+    torch.testing.assert_close(got, want, rtol=1e-2, atol=1e-2)
+    # against the oracle on the appended cache
+    kc = a.key_buf.float().cpu().numpy()
+    vc = a.value_buf.float().cpu().numpy()
+    ref = O.decode_attention(qr.float().cpu().numpy().reshape(B, H, D), kc, vc, [L + 1 for L in prior], H, Hkv, D)
+    np.testing.assert_allclose(got.cpu().numpy().reshape(B, H * D), ref, rtol=RTOL, atol=ATOL)
+
+
+# ---------------------------------------------------------------------------------------
 # Prefill
 # ---------------------------------------------------------------------------------------
 
