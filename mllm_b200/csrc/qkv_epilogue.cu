@@ -162,6 +162,145 @@ __global__ void __launch_bounds__(kWarps * 32, 6) qkv_epilogue_kernel(EpilogueAr
     }
 }
 
+// Many tokens (prefill): a quarter-warp (8 lanes) per head row, lane j holding the columns
+// d = j + 8m (m < D/8).  All four of the reference's accumulators for column class j then sit
+// in one lane -- P_k[j] sums x[d]^2 over d = j + 8k + 32i, i.e. m = k + 4i, in order of i -- so
+// acc_j = ((P0+P1)+P2)+P3 needs no exchange; only the final sum over j = 0..7, in order, crosses
+// lanes (8 shuffles inside the quarter-warp, serving four rows per warp instruction).  The
+// reduction order, and every rounding step, is that of qkv_math.cuh, so the results are
+// bit-identical to the warp-per-row kernel.  RoPE pairs (d, d + D/2) are m and m + D/16: the
+// same lane.  A block takes kQwTokens tokens; 16 quarter-warps per token, RPQ rows each.
+constexpr int kQwTokens = 2;
+
+template <int D, int RPQ>
+__global__ void __launch_bounds__(256, (D == 128 && RPQ >= 4) ? 2 : 3) qkv_epilogue_qw_kernel(EpilogueArgs a, int ntok) {
+    constexpr int NE = D / 8;        // elements per lane per row
+    constexpr int HM = NE / 2;       // slot m pairs with slot m + HM (distance D/2)
+    constexpr int NI = D / 32;       // accumulation steps per accumulator
+    constexpr int kQwPerTok = 32 / kQwTokens;
+    __shared__ float s_cos[kQwTokens][D];
+    __shared__ float s_sin[kQwTokens][D];
+    __shared__ float s_gamma[2][D];
+    __shared__ int64_t s_slot[kQwTokens];
+
+    pdl_trigger();   // a decode launched next may start its set-up (it waits for this grid)
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int j = lane & 7;
+    const int qbase = lane & ~7;
+    const int qw = tid >> 3;
+    const int tl = qw / kQwPerTok;          // token of this quarter-warp within the block
+    const int hq = qw % kQwPerTok;          // its rows: heads hq + kQwPerTok * t
+    const int token = blockIdx.x * kQwTokens + tl;
+    const bool tok_ok = token < ntok;
+    const int b = tok_ok ? token / a.S : 0;
+    const int s = tok_ok ? token - b * a.S : 0;
+    const int total_heads = a.H + 2 * a.Hkv;
+
+    float x[RPQ][NE];
+#pragma unroll
+    for (int t = 0; t < RPQ; ++t) {
+        const int head = hq + kQwPerTok * t;
+        if (tok_ok && head < total_heads) {
+            const HeadRef r = locate_head(a, head, b, s);
+#pragma unroll
+            for (int m = 0; m < NE; ++m) x[t][m] = __bfloat162float(r.src[j + 8 * m]);
+        }
+    }
+
+    // staged once per block while the row loads are in flight
+    if (a.q_gamma != nullptr) {
+        for (int d = tid; d < D; d += blockDim.x) {
+            s_gamma[0][d] = __bfloat162float(a.q_gamma[d]);
+            s_gamma[1][d] = __bfloat162float(a.k_gamma[d]);
+        }
+    }
+    if (tid < kQwTokens) {
+        const int tk = blockIdx.x * kQwTokens + tid;
+        if (tk < ntok) {
+            const int bb = tk / a.S, ss = tk - bb * a.S;
+            s_slot[tid] = (a.cache_start ? (int64_t)a.cache_start[bb] : a.uniform_start) + ss;
+        }
+    }
+    for (int idx = tid; idx < kQwTokens * D; idx += blockDim.x) {
+        const int t2 = idx / D, col = idx - t2 * D;
+        const int tk = blockIdx.x * kQwTokens + t2;
+        if (tk >= ntok) continue;
+        const int bb = tk / a.S, ss = tk - bb * a.S;
+        if (a.rope_cos != nullptr) {
+            const int64_t row = (int64_t)bb * a.rope_row_sb + (int64_t)ss * a.rope_row_ss;
+            s_cos[t2][col] = a.rope_cos[row * D + col];
+            s_sin[t2][col] = a.rope_sin[row * D + col];
+        } else if (col < D / 2) {
+            float c, sn;
+            rope_angle_cos_sin(a.positions[(int64_t)bb * a.pos_sb + (int64_t)ss * a.pos_ss], col, D, a.log_theta, c,
+                               sn);
+            s_cos[t2][col] = c;
+            s_cos[t2][col + D / 2] = c;
+            s_sin[t2][col] = sn;
+            s_sin[t2][col + D / 2] = sn;
+        }
+    }
+    __syncthreads();
+    if (!tok_ok) return;
+
+    const int64_t slot = s_slot[tl];
+#pragma unroll
+    for (int t = 0; t < RPQ; ++t) {
+        const int head = hq + kQwPerTok * t;
+        if (head >= total_heads) break;
+        const HeadRef r = locate_head(a, head, b, s);
+        __nv_bfloat16 y[NE];
+        if (r.kind == 2) {
+#pragma unroll
+            for (int m = 0; m < NE; ++m) y[m] = __float2bfloat16_rn(x[t][m]);   // exact: x came from bf16
+        } else {
+            if (r.gamma != nullptr) {
+                // RMSNorm.h:48-63 in the reference's reduction order (see above)
+                float acc = 0.f;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    float pk = 0.f;
+#pragma unroll
+                    for (int i = 0; i < NI; ++i) pk = __fadd_rn(pk, __fmul_rn(x[t][k + 4 * i], x[t][k + 4 * i]));
+                    acc = k == 0 ? pk : __fadd_rn(acc, pk);
+                }
+                float total = 0.f;
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) total = __fadd_rn(total, __shfl_sync(0xffffffffu, acc, qbase + jj));
+                const float rr = rms_scale<D>(total, a.eps);
+                const float* gw = s_gamma[r.kind];
+#pragma unroll
+                for (int m = 0; m < NE; ++m)
+                    x[t][m] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[t][m], rr), gw[j + 8 * m])));
+            }
+            // RoPE.h:77-88 on the pairs (d, d + D/2)
+#pragma unroll
+            for (int m = 0; m < HM; ++m) {
+                const int d = j + 8 * m;
+                float lo, hi;
+                rope_rotate_pair(x[t][m], x[t][m + HM], s_cos[tl][d], s_sin[tl][d], s_cos[tl][d + D / 2],
+                                 s_sin[tl][d + D / 2], lo, hi);
+                y[m] = __float2bfloat16_rn(lo);
+                y[m + HM] = __float2bfloat16_rn(hi);
+            }
+        }
+        __nv_bfloat16* dst;
+        if (r.kind == 0) {
+            dst = a.q_out + (((int64_t)b * a.H + r.h) * a.S + s) * D;
+        } else {
+            if (slot < 0 || slot >= a.capacity) {
+                if (j == 0) record_error(kErrBadLength);
+                continue;
+            }
+            __nv_bfloat16* base = (r.kind == 1) ? a.k_cache : a.v_cache;
+            dst = base + b * a.c_sb + r.h * a.c_sh + slot * a.c_st;
+        }
+#pragma unroll
+        for (int m = 0; m < NE; ++m) dst[j + 8 * m] = y[m];
+    }
+}
+
 }  // namespace
 
 MLLM_DEFINE_STATUS_READER(epilogue)
@@ -228,10 +367,30 @@ extern "C" int mllm_qkv_epilogue_bf16(const void* q, int64_t q_sb, int64_t q_ss,
     // (decode): one head per warp spreads the little work over more SMs.
     const int total_heads = num_heads + 2 * num_kv_heads;
     const int64_t tokens = (int64_t)batch * seq_len;
+    cudaStream_t st = (cudaStream_t)stream;
+    // Many tokens: the quarter-warp kernel (rows per quarter-warp = ceil(heads / 16)).
+    const int rpq = (total_heads + 15) / 16;
+    if (tokens >= 1024 && rpq <= 4) {
+        const unsigned blocks = (unsigned)((tokens + kQwTokens - 1) / kQwTokens);
+        const int nt = (int)tokens;
+        auto launch = [&](auto kern) { kern<<<blocks, 256, 0, st>>>(a, nt); };
+        if (head_dim == 128) {
+            if (rpq == 1) launch(qkv_epilogue_qw_kernel<128, 1>);
+            else if (rpq == 2) launch(qkv_epilogue_qw_kernel<128, 2>);
+            else if (rpq == 3) launch(qkv_epilogue_qw_kernel<128, 3>);
+            else launch(qkv_epilogue_qw_kernel<128, 4>);
+        } else {
+            if (rpq == 1) launch(qkv_epilogue_qw_kernel<64, 1>);
+            else if (rpq == 2) launch(qkv_epilogue_qw_kernel<64, 2>);
+            else if (rpq == 3) launch(qkv_epilogue_qw_kernel<64, 3>);
+            else launch(qkv_epilogue_qw_kernel<64, 4>);
+        }
+        if (int e = check_cuda(cudaGetLastError(), "qkv_epilogue launch")) return e;
+        return ok();
+    }
     const int hpw = tokens >= 1024 ? 4 : 1;
     dim3 grid((unsigned)tokens, (unsigned)((total_heads + kWarps * hpw - 1) / (kWarps * hpw)));
     if (grid.y > 65535) return fail(MLLM_ERR_UNSUPPORTED, "qkv_epilogue: too many heads");
-    cudaStream_t st = (cudaStream_t)stream;
     if (head_dim == 128) {
         if (hpw == 4) qkv_epilogue_kernel<128, 4><<<grid, kWarps * 32, 0, st>>>(a);
         else qkv_epilogue_kernel<128, 1><<<grid, kWarps * 32, 0, st>>>(a);

@@ -115,6 +115,37 @@ def test_epilogue_kv_cache_bit_exact(rt, c):
         np.testing.assert_array_equal(torch_to_bits(qr), O.bf16_bits(q_ref), err_msg=tag)
 
 
+@pytest.mark.parametrize("H,Hkv,D,qk_norm,table", [(32, 8, 128, True, False), (40, 8, 128, True, True),
+                                                   (32, 4, 64, False, False)])
+def test_epilogue_many_tokens_equals_chunked(rt, H, Hkv, D, qk_norm, table):
+    """A call over many tokens (the quarter-warp kernel) writes bit-identical q rows and cache rows to
+    the same tokens epilogued in small chunks (the warp-per-row kernel, pinned bit-exact to the
+    reference above): Qwen3-8B, Qwen3-14B with a RoPE table, TinyLlama geometry."""
+    B, S, chunk = 2, 1536, 256
+    g = torch.Generator(device="cuda").manual_seed(H + D)
+    proj = (torch.randn(B, S, (H + 2 * Hkv) * D, device="cuda", generator=g) * 0.7).bfloat16()
+    q = proj[..., : H * D].view(B, S, H, D).transpose(1, 2)
+    k = proj[..., H * D:(H + Hkv) * D].view(B, S, Hkv, D).transpose(1, 2)
+    v = proj[..., (H + Hkv) * D:].view(B, S, Hkv, D).transpose(1, 2)
+    gq = (1 + 0.1 * torch.randn(D, device="cuda", generator=g)).bfloat16() if qk_norm else None
+    gk = (1 + 0.1 * torch.randn(D, device="cuda", generator=g)).bfloat16() if qk_norm else None
+    pos = torch.arange(S, device="cuda") + 3
+    tab = rt.RoPE.build_cos_sin(pos, D, 1e6) if table else None
+    whole = rt.KVCache(B, Hkv, D, S)
+    q_whole = rt.qkv_epilogue(q, k, v, whole, pos, 1e6, gq, gk, 1e-6, rope_table=tab)
+    parts = rt.KVCache(B, Hkv, D, S)
+    q_parts = []
+    for s0 in range(0, S, chunk):
+        sl = slice(s0, s0 + chunk)
+        tp = (tab[0][sl], tab[1][sl]) if table else None
+        q_parts.append(rt.qkv_epilogue(q[:, :, sl], k[:, :, sl], v[:, :, sl], parts, pos[sl], 1e6, gq, gk, 1e-6,
+                                       rope_table=tp))
+    as_bits = lambda t: t.contiguous().view(torch.int16)
+    assert torch.equal(as_bits(q_whole), as_bits(torch.cat(q_parts, dim=2)))
+    assert torch.equal(as_bits(whole.key_buf), as_bits(parts.key_buf))
+    assert torch.equal(as_bits(whole.value_buf), as_bits(parts.value_buf))
+
+
 def test_epilogue_rejects_bad_slots(rt):
     """A cache slot past the capacity is not written and is reported on the device status."""
     from mllm_b200 import abi
