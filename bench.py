@@ -515,8 +515,44 @@ def run_gpu(args, rank, world, device):
         barrier()
         rag = {"ms": max_over_ranks(r0.elapsed_time(r1) / rsteps), "steps": rsteps,
                "bytes_per_rank": int(lens_np.sum()) * 2 * Hkvr * D * 2, "sum_len": int(lens_np.sum()),
-               "max_len": Lmax}
-        del kr, vr, qr, orr, ws_r
+               "max_len": Lmax, "contiguous_cache_bytes": 2 * kr.numel() * 2}
+        del kr, vr
+        # the same batch over a paged cache: blocks of 256 rows handed out in a shuffled order,
+        # the pool holding exactly the blocks the sequences need (no padding to the longest)
+        import random
+        from mllm_b200.runtime import PagedKVCache
+        torch.cuda.empty_cache()
+        bs = 256
+        nblk = int(sum(-(-int(x) // bs) for x in lens_np))
+        pk = PagedKVCache(num_blocks=nblk, num_kv_heads=Hkvr, head_dim=D, block_size=bs, max_seqs=RAG_B,
+                          max_blocks_per_seq=-(-Lmax // bs), device=device)
+        random.Random(RAG_SEED).shuffle(pk._free)
+        pk.set_lengths([int(x) for x in lens_np])
+        pk.k_pool.normal_(generator=gen)
+        pk.v_pool.normal_(generator=gen)
+        kvd = pk.descriptor()
+        import ctypes as C
+
+        def decode_p():
+            st = lib.mllm_decode_attention_paged_bf16(qr.data_ptr(), C.byref(kvd), pk.lengths.data_ptr(), RAG_B, Hr,
+                                                      Hkvr, D, Lmax, scale, orr.data_ptr(), ws_r.data_ptr(),
+                                                      ws_r_bytes, sh)
+            assert st == 0, lib.mllm_attn_last_error()
+
+        for _ in range(args.warmup):
+            decode_p()
+        barrier()
+        torch.cuda.synchronize()
+        r0.record(stream)
+        for i in range(rsteps):
+            decode_p()
+        r1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        rag["paged_ms"] = max_over_ranks(r0.elapsed_time(r1) / rsteps)
+        rag["paged_pool_bytes"] = 2 * pk.k_pool.numel() * 2
+        rag["paged_block_size"] = bs
+        del pk, qr, orr, ws_r
 
     clocks = sampler.stop() if rank == 0 else None
     return {"elapsed_ms": elapsed_ms, "dec_ms": dec_ms, "unfused_ms": unfused_ms, "e2e_ms": e2e_ms, "pre": pre,
@@ -763,7 +799,13 @@ def main():
             "scaling": "strong", "higher_is_better": True,
             "roofline": {"bound": "hbm", "kernel": "decode_split_kernel<128> + decode_combine_kernel",
                          "achieved": ach, "peak": hbm_peak, "unit": "GB/s", "frac": ach / hbm_peak,
-                         "peak_source": peak_src}}
+                         "peak_source": peak_src},
+            "paged": {"value": r["bytes_per_rank"] * n / (r["paged_ms"] * 1e-3) / 1e9, "unit": "GB/s",
+                      "ms_per_layer": r["paged_ms"], "block_size": r["paged_block_size"],
+                      "cache_bytes_per_rank": r["paged_pool_bytes"],
+                      "contiguous_cache_bytes_per_rank": r["contiguous_cache_bytes"],
+                      "note": "mllm_decode_attention_paged_bf16 over a pool holding exactly the blocks the "
+                              "sequences need, handed out in a shuffled order"}}
     print(json.dumps(line))
 
 

@@ -9,6 +9,7 @@
  *   mllm_prefill_attention_bf16 causal GQA attention over the cache (tcgen05 / TMEM / TMA)
  *   mllm_decode_attention_bf16  split-K flash-decode over the cache (HBM-bound)
  *   mllm_decode_step_bf16       the epilogue of one new token per sequence fused into decode
+ *   mllm_*_paged_bf16           the same four over a paged KV cache (block tables)
  *
  * plus the RoPE table builder and RoPE apply that back the `mllm::RoPE` facade.
  *
@@ -211,6 +212,71 @@ MLLM_API int mllm_decode_step_bf16(const void* q, int64_t q_sb, int64_t q_sh, co
                                    int64_t cache_st, const int32_t* kv_lens, int batch, int num_heads,
                                    int num_kv_heads, int head_dim, int max_kv_len, float softmax_scale, void* out,
                                    void* workspace, size_t workspace_bytes, mllm_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------
+ * Paged KV cache (the serving format; no counterpart in the reference, whose KVCache is one
+ * contiguous tensor per layer grown by torch::cat, KVCache.h:9-28 / Attention.h:189-207).
+ * Rows of all sequences live in fixed-size blocks of one pool per layer, and each sequence
+ * owns a list of blocks, so sequences of any length share the memory without padding to the
+ * longest (the natural step toward the batched Generate the reference lacks,
+ * QwenRunner.cpp:459-473).
+ *   k_pool / v_pool: bf16; row r of block n for kv head h at
+ *       pool + n*block_stride + h*head_stride + r*row_stride    (elements; row_stride and
+ *       head_stride multiples of 8, pool 16-byte aligned)
+ *   block_size: rows per block, a multiple of 128 (one attention tile never straddles blocks)
+ *   block_table: int32 device; block i of sequence b is block_table[b*table_stride + i], and
+ *       cache row t of sequence b is row t % block_size of block block_table[b*table_stride +
+ *       t / block_size].  Entries must lie in [0, num_blocks); a bad entry records
+ *       MLLM_ERR_DEVICE_LENGTH and reads block 0 instead (writes to it are skipped).
+ *   max_blocks_per_seq: entries per sequence; rows beyond max_blocks_per_seq*block_size are
+ *       rejected like rows beyond a contiguous cache's capacity.
+ * Rows of a sequence's last block beyond its length may hold any finite value for prefill
+ * (they are masked) and any bits at all for decode; a freshly allocated block should be
+ * zero-filled.
+ * The paged entry points take the same arguments as their contiguous counterparts with the
+ * cache pointers, strides and capacity replaced by the descriptor. */
+typedef struct mllm_paged_kv {
+    void* k_pool;
+    void* v_pool;
+    int64_t block_stride;
+    int64_t head_stride;
+    int64_t row_stride;
+    int32_t num_blocks;
+    int32_t block_size;
+    const int32_t* block_table;
+    int64_t table_stride;
+    int32_t max_blocks_per_seq;
+} mllm_paged_kv;
+
+MLLM_API int mllm_qkv_epilogue_paged_bf16(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh,
+                                          const void* k, int64_t k_sb, int64_t k_ss, int64_t k_sh,
+                                          const void* v, int64_t v_sb, int64_t v_ss, int64_t v_sh,
+                                          int batch, int seq_len, int num_heads, int num_kv_heads, int head_dim,
+                                          const int64_t* positions, int64_t pos_sb, int64_t pos_ss,
+                                          double rope_theta, const float* rope_cos, const float* rope_sin,
+                                          int64_t rope_row_sb, int64_t rope_row_ss, const void* q_norm_weight,
+                                          const void* k_norm_weight, double rms_norm_eps, void* q_out,
+                                          const mllm_paged_kv* kv, const int32_t* cache_start,
+                                          int64_t uniform_cache_start, mllm_stream_t stream);
+
+MLLM_API int mllm_prefill_attention_paged_bf16(const void* q, const mllm_paged_kv* kv, int batch, int num_heads,
+                                               int num_kv_heads, int head_dim, int q_len, int kv_len,
+                                               float softmax_scale, void* out, mllm_stream_t stream);
+
+MLLM_API int mllm_decode_attention_paged_bf16(const void* q, const mllm_paged_kv* kv, const int32_t* kv_lens,
+                                              int batch, int num_heads, int num_kv_heads, int head_dim,
+                                              int max_kv_len, float softmax_scale, void* out, void* workspace,
+                                              size_t workspace_bytes, mllm_stream_t stream);
+
+MLLM_API int mllm_decode_step_paged_bf16(const void* q, int64_t q_sb, int64_t q_sh, const void* k, int64_t k_sb,
+                                         int64_t k_sh, const void* v, int64_t v_sb, int64_t v_sh,
+                                         const int64_t* positions, int64_t pos_sb, double rope_theta,
+                                         const float* rope_cos, const float* rope_sin, int64_t rope_row_sb,
+                                         const void* q_norm_weight, const void* k_norm_weight, double rms_norm_eps,
+                                         const mllm_paged_kv* kv, const int32_t* kv_lens, int batch,
+                                         int num_heads, int num_kv_heads, int head_dim, int max_kv_len,
+                                         float softmax_scale, void* out, void* workspace, size_t workspace_bytes,
+                                         mllm_stream_t stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -31,6 +31,18 @@ _d = C.c_double
 _f = C.c_float
 _sz = C.c_size_t
 
+
+
+class PagedKV(C.Structure):
+    """struct mllm_paged_kv (include/mllm_attn.h): a paged KV cache's pools and block table."""
+    _fields_ = [("k_pool", C.c_void_p), ("v_pool", C.c_void_p), ("block_stride", C.c_int64),
+                ("head_stride", C.c_int64), ("row_stride", C.c_int64), ("num_blocks", C.c_int32),
+                ("block_size", C.c_int32), ("block_table", C.c_void_p), ("table_stride", C.c_int64),
+                ("max_blocks_per_seq", C.c_int32)]
+
+
+_kv = C.POINTER(PagedKV)
+
 # name -> (restype, argtypes); mirrors include/mllm_attn.h one to one
 SIGNATURES = {
     "mllm_attn_abi_version": (_i, []),
@@ -51,6 +63,13 @@ SIGNATURES = {
     "mllm_decode_step_bf16": (_i, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _d, _p, _p, _i64,
                                    _p, _p, _d, _p, _p, _i64, _i64, _i64, _p, _i, _i, _i, _i, _i, _f, _p, _p,
                                    _sz, _p]),
+    "mllm_qkv_epilogue_paged_bf16": (_i, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64,
+                                          _i, _i, _i, _i, _i, _p, _i64, _i64, _d, _p, _p, _i64, _i64,
+                                          _p, _p, _d, _p, _kv, _p, _i64, _p]),
+    "mllm_prefill_attention_paged_bf16": (_i, [_p, _kv, _i, _i, _i, _i, _i, _i, _f, _p, _p]),
+    "mllm_decode_attention_paged_bf16": (_i, [_p, _kv, _p, _i, _i, _i, _i, _i, _f, _p, _p, _sz, _p]),
+    "mllm_decode_step_paged_bf16": (_i, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _d, _p, _p,
+                                         _i64, _p, _p, _d, _kv, _p, _i, _i, _i, _i, _i, _f, _p, _p, _sz, _p]),
 }
 
 

@@ -41,6 +41,7 @@
 
 #include "common.cuh"
 #include "host_util.h"
+#include "kv_layout.cuh"
 #include "qkv_math.cuh"
 
 namespace mllm_b200 {
@@ -77,6 +78,7 @@ struct DecodeArgs {
     float* part_ml;             // [B*Hkv*nch, n_rep, 2]
     int B, H, Hkv, n_rep, max_len, chunk, nch, items;
     float scale_log2;
+    KvLayout lay;                // contiguous, or the paged cache's block table
     // fused step only: the new token's projections, RoPE, norm weights and the cache to append to
     const __nv_bfloat16* q_in;   // q head h of sequence b at q_in + b*q_sb + h*q_sh
     const __nv_bfloat16* k_in;
@@ -93,7 +95,7 @@ struct DecodeArgs {
     float eps;
     __nv_bfloat16* k_cache;
     __nv_bfloat16* v_cache;
-    int64_t c_sb, c_sh, c_st;
+    int64_t c_sb, c_sh, c_st;    // per sequence (contiguous) or per block (paged)
 };
 
 template <int D, bool kFused>
@@ -205,12 +207,16 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 2)
                 for (int i = 0; i < NI; ++i) xk[i] = __bfloat162float(rk[i]);
                 const float rr = norm ? rms_scale<D>(row_sum_squares<NI>(xk, lane), a.eps) : 1.f;
                 qk_norm_rope_row<D>(xk, norm, gk, rr, rope, yk);
-                const int64_t crow = (int64_t)b * a.c_sb + (int64_t)g * a.c_sh + (int64_t)(L - 1) * a.c_st;
+                int blk, row;
+                const bool at = kv_locate(a.lay, b, L - 1, blk, row);
+                const int64_t crow = (int64_t)blk * a.c_sb + (int64_t)g * a.c_sh + (int64_t)row * a.c_st;
 #pragma unroll
                 for (int i = 0; i < NI; ++i) {
                     const __nv_bfloat16 yv = rv[i];
-                    a.k_cache[crow + lane + 32 * i] = yk[i];
-                    a.v_cache[crow + lane + 32 * i] = yv;
+                    if (at) {
+                        a.k_cache[crow + lane + 32 * i] = yk[i];
+                        a.v_cache[crow + lane + 32 * i] = yv;
+                    }
                     f_vnew[p * D + lane + 32 * i] = yv;
                 }
             }
@@ -258,10 +264,12 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 2)
                     mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
                     uint8_t* kdst = smem + stage * Cfg::kStageBytes;
                     uint8_t* vdst = kdst + Cfg::kTileBytes;
+                    int blk, row;
+                    kv_locate(a.lay, b, t, blk, row);   // a bad table entry reads block 0 (and is recorded)
 #pragma unroll
                     for (int bx = 0; bx < Cfg::kBoxes; ++bx) {
-                        tma_load_4d(kdst + bx * kBoxBytes, &tmK, &full[stage], bx * 64, t, g, b);
-                        tma_load_4d(vdst + bx * kBoxBytes, &tmV, &full[stage], bx * 64, t, g, b);
+                        tma_load_4d(kdst + bx * kBoxBytes, &tmK, &full[stage], bx * 64, row, g, blk);
+                        tma_load_4d(vdst + bx * kBoxBytes, &tmV, &full[stage], bx * 64, row, g, blk);
                     }
                     if (++stage == NS) { stage = 0; phase ^= 1; }
                 }
@@ -697,6 +705,55 @@ extern "C" int mllm_decode_attention_bf16(const void* q, const void* k_cache, co
     return ok();
 }
 
+extern "C" int mllm_decode_attention_paged_bf16(const void* q, const mllm_paged_kv* kv, const int32_t* kv_lens,
+                                                int batch, int num_heads, int num_kv_heads, int head_dim,
+                                                int max_kv_len, float softmax_scale, void* out, void* workspace,
+                                                size_t workspace_bytes, mllm_stream_t stream) {
+    if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_kv_len <= 0)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention: bad sizes");
+    if (num_heads % num_kv_heads != 0)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "Attention: num_heads must be divisible by num_kv_heads.");
+    if (head_dim != 64 && head_dim != 128)
+        return fail(MLLM_ERR_UNSUPPORTED, "decode_attention: head_dim must be 64 or 128");
+    const int n_rep = num_heads / num_kv_heads;
+    if (n_rep > kMaxGroup) return fail(MLLM_ERR_UNSUPPORTED, "decode_attention: GQA group larger than 8");
+    if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale))
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention: softmax_scale must be positive");
+    if (batch == 0) return ok();
+    if (!q || !out) return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention: null pointer");
+    KvLayout lay;
+    if (int st = paged_layout(kv, max_kv_len, head_dim, "decode_attention_paged", &lay)) return st;
+    if (!aligned(q, 4) || !aligned(out, 4)) return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention: q/out misaligned");
+    const size_t need = workspace_bytes_for(batch, num_heads, num_kv_heads, head_dim, max_kv_len);
+    if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+        return fail(MLLM_ERR_WORKSPACE, "decode_attention: workspace missing, misaligned or smaller than "
+                                        "mllm_decode_attention_workspace_size()");
+    int num_sms = 0;
+    if (int st = require_sm100(&num_sms)) return st;
+
+    CUtensorMap tmK, tmV;
+    if (int st = encode_kv_map(&tmK, kv->k_pool, head_dim, kv->block_size, num_kv_heads, kv->num_blocks,
+                               kv->row_stride, kv->head_stride, kv->block_stride, 64, kTile))
+        return st;
+    if (int st = encode_kv_map(&tmV, kv->v_pool, head_dim, kv->block_size, num_kv_heads, kv->num_blocks,
+                               kv->row_stride, kv->head_stride, kv->block_stride, 64, kTile))
+        return st;
+
+    DecodeArgs a = {};
+    a.lay = lay;
+    a.q = (const __nv_bfloat16*)q;
+    a.kv_lens = kv_lens;
+    a.out = (__nv_bfloat16*)out;
+    a.B = batch;
+    a.H = num_heads;
+    a.Hkv = num_kv_heads;
+    a.n_rep = n_rep;
+    a.max_len = max_kv_len;
+    a.scale_log2 = (float)((double)softmax_scale * 1.4426950408889634);
+    if (int st = launch_decode<false>(a, head_dim, tmK, tmV, num_sms, workspace, (cudaStream_t)stream)) return st;
+    return ok();
+}
+
 // ---------------------------------------------------------------------------------------------
 // Decode without a caller workspace.
 //
@@ -806,15 +863,19 @@ extern "C" int mllm_decode_attention_noalloc_bf16(const void* q, const void* k_c
 // append) and the decode attention over the cache including that token, in one launch of the
 // split kernel (plus the combine kernel when a sequence spans several chunks).
 // ---------------------------------------------------------------------------------------------
-extern "C" int mllm_decode_step_bf16(const void* q, int64_t q_sb, int64_t q_sh, const void* k, int64_t k_sb,
-                                     int64_t k_sh, const void* v, int64_t v_sb, int64_t v_sh,
-                                     const int64_t* positions, int64_t pos_sb, double rope_theta,
-                                     const float* rope_cos, const float* rope_sin, int64_t rope_row_sb,
-                                     const void* q_norm_weight, const void* k_norm_weight, double rms_norm_eps,
-                                     void* k_cache, void* v_cache, int64_t cache_sb, int64_t cache_sh,
-                                     int64_t cache_st, const int32_t* kv_lens, int batch, int num_heads,
-                                     int num_kv_heads, int head_dim, int max_kv_len, float softmax_scale, void* out,
-                                     void* workspace, size_t workspace_bytes, mllm_stream_t stream) {
+namespace {
+
+// Shared by mllm_decode_step_bf16 and its paged form.  The cache is addressed per sequence
+// (contiguous: map_rows = max_kv_len rows, map_batch = batch) or per block (paged: map_rows =
+// block_size, map_batch = num_blocks), with `lay` saying which.
+int decode_step_entry(const void* q, int64_t q_sb, int64_t q_sh, const void* k, int64_t k_sb, int64_t k_sh,
+                      const void* v, int64_t v_sb, int64_t v_sh, const int64_t* positions, int64_t pos_sb,
+                      double rope_theta, const float* rope_cos, const float* rope_sin, int64_t rope_row_sb,
+                      const void* q_norm_weight, const void* k_norm_weight, double rms_norm_eps, void* k_cache,
+                      void* v_cache, int64_t cache_sb, int64_t cache_sh, int64_t cache_st, int64_t map_rows,
+                      int64_t map_batch, const KvLayout& lay, const int32_t* kv_lens, int batch, int num_heads,
+                      int num_kv_heads, int head_dim, int max_kv_len, float softmax_scale, void* out,
+                      void* workspace, size_t workspace_bytes, mllm_stream_t stream) {
     if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_kv_len <= 0)
         return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_step: bad sizes");
     if (num_heads % num_kv_heads != 0)
@@ -844,14 +905,15 @@ extern "C" int mllm_decode_step_bf16(const void* q, int64_t q_sb, int64_t q_sh, 
     if (int st = require_sm100(&num_sms)) return st;
 
     CUtensorMap tmK, tmV;
-    if (int st = encode_kv_map(&tmK, k_cache, head_dim, max_kv_len, num_kv_heads, batch, cache_st, cache_sh, cache_sb,
-                               64, kTile))
+    if (int st = encode_kv_map(&tmK, k_cache, head_dim, map_rows, num_kv_heads, map_batch, cache_st, cache_sh,
+                               cache_sb, 64, kTile))
         return st;
-    if (int st = encode_kv_map(&tmV, v_cache, head_dim, max_kv_len, num_kv_heads, batch, cache_st, cache_sh, cache_sb,
-                               64, kTile))
+    if (int st = encode_kv_map(&tmV, v_cache, head_dim, map_rows, num_kv_heads, map_batch, cache_st, cache_sh,
+                               cache_sb, 64, kTile))
         return st;
 
     DecodeArgs a = {};
+    a.lay = lay;
     a.kv_lens = kv_lens;
     a.out = (__nv_bfloat16*)out;
     a.B = batch;
@@ -880,4 +942,40 @@ extern "C" int mllm_decode_step_bf16(const void* q, int64_t q_sb, int64_t q_sh, 
     a.c_sb = cache_sb; a.c_sh = cache_sh; a.c_st = cache_st;
     if (int st = launch_decode<true>(a, head_dim, tmK, tmV, num_sms, workspace, (cudaStream_t)stream)) return st;
     return ok();
+}
+
+}  // namespace
+
+extern "C" int mllm_decode_step_bf16(const void* q, int64_t q_sb, int64_t q_sh, const void* k, int64_t k_sb,
+                                     int64_t k_sh, const void* v, int64_t v_sb, int64_t v_sh,
+                                     const int64_t* positions, int64_t pos_sb, double rope_theta,
+                                     const float* rope_cos, const float* rope_sin, int64_t rope_row_sb,
+                                     const void* q_norm_weight, const void* k_norm_weight, double rms_norm_eps,
+                                     void* k_cache, void* v_cache, int64_t cache_sb, int64_t cache_sh,
+                                     int64_t cache_st, const int32_t* kv_lens, int batch, int num_heads,
+                                     int num_kv_heads, int head_dim, int max_kv_len, float softmax_scale, void* out,
+                                     void* workspace, size_t workspace_bytes, mllm_stream_t stream) {
+    return decode_step_entry(q, q_sb, q_sh, k, k_sb, k_sh, v, v_sb, v_sh, positions, pos_sb, rope_theta, rope_cos,
+                             rope_sin, rope_row_sb, q_norm_weight, k_norm_weight, rms_norm_eps, k_cache, v_cache,
+                             cache_sb, cache_sh, cache_st, max_kv_len, batch, KvLayout{}, kv_lens, batch, num_heads,
+                             num_kv_heads, head_dim, max_kv_len, softmax_scale, out, workspace, workspace_bytes,
+                             stream);
+}
+
+extern "C" int mllm_decode_step_paged_bf16(const void* q, int64_t q_sb, int64_t q_sh, const void* k, int64_t k_sb,
+                                           int64_t k_sh, const void* v, int64_t v_sb, int64_t v_sh,
+                                           const int64_t* positions, int64_t pos_sb, double rope_theta,
+                                           const float* rope_cos, const float* rope_sin, int64_t rope_row_sb,
+                                           const void* q_norm_weight, const void* k_norm_weight,
+                                           double rms_norm_eps, const mllm_paged_kv* kv, const int32_t* kv_lens,
+                                           int batch, int num_heads, int num_kv_heads, int head_dim, int max_kv_len,
+                                           float softmax_scale, void* out, void* workspace, size_t workspace_bytes,
+                                           mllm_stream_t stream) {
+    KvLayout lay;
+    if (int st = paged_layout(kv, max_kv_len, head_dim, "decode_step_paged", &lay)) return st;
+    return decode_step_entry(q, q_sb, q_sh, k, k_sb, k_sh, v, v_sb, v_sh, positions, pos_sb, rope_theta, rope_cos,
+                             rope_sin, rope_row_sb, q_norm_weight, k_norm_weight, rms_norm_eps, kv->k_pool,
+                             kv->v_pool, kv->block_stride, kv->head_stride, kv->row_stride, kv->block_size,
+                             kv->num_blocks, lay, kv_lens, batch, num_heads, num_kv_heads, head_dim, max_kv_len,
+                             softmax_scale, out, workspace, workspace_bytes, stream);
 }

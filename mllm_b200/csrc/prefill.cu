@@ -38,6 +38,7 @@
 
 #include "common.cuh"
 #include "host_util.h"
+#include "kv_layout.cuh"
 #include "tcgen05.cuh"
 
 namespace mllm_b200 {
@@ -78,6 +79,7 @@ struct PrefillArgs {
     __nv_bfloat16* out;   // [B, q_len, H*D]
     int B, H, Hkv, n_rep, q_len, kv_len, n_mblocks;
     float scale_log2;
+    KvLayout lay;         // contiguous, or the paged cache's block table
 };
 
 __device__ __forceinline__ uint32_t col_s(int i) { return (uint32_t)(i * kBN); }
@@ -164,16 +166,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t phase = ((j / ST) & 1) ^ 1;
                 uint8_t* sk = sKV + stage * Cfg::kStageBytes;
                 uint8_t* sv = sk + Cfg::kKVBytes;
+                // cache rows j*kBN .. +kBN: one block of a paged cache (block_size % kBN == 0)
+                int kblk, krow;
+                kv_locate(a.lay, b, (int64_t)j * kBN, kblk, krow);   // a bad table entry reads block 0
                 if (!mbar_wait(&k_empty[stage], phase)) break;
                 mbar_arrive_expect_tx(&k_full[stage], Cfg::kKVBytes);
 #pragma unroll
                 for (int bx = 0; bx < Cfg::kBoxes; ++bx)
-                    tma_load_4d(sk + bx * kBox, &tmK, &k_full[stage], bx * 64, j * kBN, g, b);
+                    tma_load_4d(sk + bx * kBox, &tmK, &k_full[stage], bx * 64, krow, g, kblk);
                 if (!mbar_wait(&v_empty[stage], phase)) break;
                 mbar_arrive_expect_tx(&v_full[stage], Cfg::kKVBytes);
 #pragma unroll
                 for (int bx = 0; bx < Cfg::kBoxes; ++bx)
-                    tma_load_4d(sv + bx * kBox, &tmV, &v_full[stage], bx * 64, j * kBN, g, b);
+                    tma_load_4d(sv + bx * kBox, &tmV, &v_full[stage], bx * 64, krow, g, kblk);
             }
         }
       } else if (warp == 1) {
@@ -363,10 +368,14 @@ MLLM_DEFINE_STATUS_READER(prefill)
 
 using namespace mllm_b200;
 
-extern "C" int mllm_prefill_attention_bf16(const void* q, const void* k_cache, const void* v_cache, int64_t cache_sb,
-                                           int64_t cache_sh, int64_t cache_st, int batch, int num_heads,
-                                           int num_kv_heads, int head_dim, int q_len, int kv_len, float softmax_scale,
-                                           void* out, mllm_stream_t stream) {
+namespace {
+
+// Shared by the contiguous and the paged entry point: the K/V maps cover map_rows rows of
+// map_batch sequences (contiguous) or blocks (paged), and `lay` says which.
+int prefill_entry(const void* q, const void* k_cache, const void* v_cache, int64_t cache_sb, int64_t cache_sh,
+                  int64_t cache_st, int64_t map_rows, int64_t map_batch, const KvLayout& lay, int batch,
+                  int num_heads, int num_kv_heads, int head_dim, int q_len, int kv_len, float softmax_scale,
+                  void* out, mllm_stream_t stream) {
     if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || q_len < 0 || kv_len < 0)
         return fail(MLLM_ERR_INVALID_ARGUMENT, "prefill_attention: bad sizes");
     if (num_heads % num_kv_heads != 0)
@@ -388,12 +397,15 @@ extern "C" int mllm_prefill_attention_bf16(const void* q, const void* k_cache, c
     if (int st = encode_kv_map(&tmQ, q, D, q_len, num_heads, batch, D, (int64_t)q_len * D,
                                (int64_t)num_heads * q_len * D, 64, kBM))
         return st;
-    if (int st = encode_kv_map(&tmK, k_cache, D, kv_len, num_kv_heads, batch, cache_st, cache_sh, cache_sb, 64, kBN))
+    if (int st = encode_kv_map(&tmK, k_cache, D, map_rows, num_kv_heads, map_batch, cache_st, cache_sh, cache_sb, 64,
+                               kBN))
         return st;
-    if (int st = encode_kv_map(&tmV, v_cache, D, kv_len, num_kv_heads, batch, cache_st, cache_sh, cache_sb, 64, kBN))
+    if (int st = encode_kv_map(&tmV, v_cache, D, map_rows, num_kv_heads, map_batch, cache_st, cache_sh, cache_sb, 64,
+                               kBN))
         return st;
 
     PrefillArgs a;
+    a.lay = lay;
     a.out = (__nv_bfloat16*)out;
     a.B = batch;
     a.H = num_heads;
@@ -440,4 +452,25 @@ extern "C" int mllm_prefill_attention_bf16(const void* q, const void* k_cache, c
     }
     if (int st = check_cuda(cudaGetLastError(), "prefill_kernel launch")) return st;
     return ok();
+}
+
+}  // namespace
+
+extern "C" int mllm_prefill_attention_bf16(const void* q, const void* k_cache, const void* v_cache, int64_t cache_sb,
+                                           int64_t cache_sh, int64_t cache_st, int batch, int num_heads,
+                                           int num_kv_heads, int head_dim, int q_len, int kv_len, float softmax_scale,
+                                           void* out, mllm_stream_t stream) {
+    // the K/V maps stop at kv_len: rows past it read as zero
+    return prefill_entry(q, k_cache, v_cache, cache_sb, cache_sh, cache_st, kv_len, batch, KvLayout{}, batch,
+                         num_heads, num_kv_heads, head_dim, q_len, kv_len, softmax_scale, out, stream);
+}
+
+extern "C" int mllm_prefill_attention_paged_bf16(const void* q, const mllm_paged_kv* kv, int batch, int num_heads,
+                                                 int num_kv_heads, int head_dim, int q_len, int kv_len,
+                                                 float softmax_scale, void* out, mllm_stream_t stream) {
+    KvLayout lay;
+    if (int st = paged_layout(kv, kv_len, head_dim, "prefill_attention_paged", &lay)) return st;
+    return prefill_entry(q, kv->k_pool, kv->v_pool, kv->block_stride, kv->head_stride, kv->row_stride,
+                         kv->block_size, kv->num_blocks, lay, batch, num_heads, num_kv_heads, head_dim, q_len,
+                         kv_len, softmax_scale, out, stream);
 }

@@ -12,6 +12,7 @@
 // Memory: each head row is read once (D*2 bytes) and written once (q_out or the cache row).
 #include "common.cuh"
 #include "host_util.h"
+#include "kv_layout.cuh"
 #include "qkv_math.cuh"
 
 namespace mllm_b200 {
@@ -35,7 +36,8 @@ struct EpilogueArgs {
     __nv_bfloat16* q_out;
     __nv_bfloat16* k_cache;
     __nv_bfloat16* v_cache;
-    int64_t c_sb, c_sh, c_st, capacity;
+    int64_t c_sb, c_sh, c_st, capacity;   // paged: block, head and row strides; rows per sequence
+    KvLayout lay;                          // contiguous, or the paged cache's block table
     const int32_t* cache_start;   // NULL: uniform_start for every sequence
     int64_t uniform_start;
 };
@@ -150,12 +152,13 @@ __global__ void __launch_bounds__(kWarps * 32, 6) qkv_epilogue_kernel(EpilogueAr
         if (r.kind == 0) {
             dst = a.q_out + (((int64_t)b * a.H + r.h) * a.S + s) * D;
         } else {
-            if (slot < 0 || slot >= a.capacity) {
+            int blk, row;
+            if (slot < 0 || slot >= a.capacity || !kv_locate(a.lay, b, slot, blk, row)) {
                 if (lane == 0) record_error(kErrBadLength);
                 continue;
             }
             __nv_bfloat16* base = (r.kind == 1) ? a.k_cache : a.v_cache;
-            dst = base + b * a.c_sb + r.h * a.c_sh + slot * a.c_st;
+            dst = base + blk * a.c_sb + r.h * a.c_sh + row * a.c_st;
         }
 #pragma unroll
         for (int i = 0; i < NI; ++i) dst[lane + 32 * i] = y[i];
@@ -289,12 +292,13 @@ __global__ void __launch_bounds__(256, (D == 128 && RPQ >= 4) ? 2 : 3) qkv_epilo
         if (r.kind == 0) {
             dst = a.q_out + (((int64_t)b * a.H + r.h) * a.S + s) * D;
         } else {
-            if (slot < 0 || slot >= a.capacity) {
+            int blk, row;
+            if (slot < 0 || slot >= a.capacity || !kv_locate(a.lay, b, slot, blk, row)) {
                 if (j == 0) record_error(kErrBadLength);
                 continue;
             }
             __nv_bfloat16* base = (r.kind == 1) ? a.k_cache : a.v_cache;
-            dst = base + b * a.c_sb + r.h * a.c_sh + slot * a.c_st;
+            dst = base + blk * a.c_sb + r.h * a.c_sh + row * a.c_st;
         }
 #pragma unroll
         for (int m = 0; m < NE; ++m) dst[j + 8 * m] = y[m];
@@ -309,17 +313,18 @@ MLLM_DEFINE_STATUS_READER(epilogue)
 
 using namespace mllm_b200;
 
-extern "C" int mllm_qkv_epilogue_bf16(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh,
-                                      const void* k, int64_t k_sb, int64_t k_ss, int64_t k_sh,
-                                      const void* v, int64_t v_sb, int64_t v_ss, int64_t v_sh,
-                                      int batch, int seq_len, int num_heads, int num_kv_heads, int head_dim,
-                                      const int64_t* positions, int64_t pos_sb, int64_t pos_ss, double rope_theta,
-                                      const float* rope_cos, const float* rope_sin, int64_t rope_row_sb,
-                                      int64_t rope_row_ss, const void* q_norm_weight, const void* k_norm_weight,
-                                      double rms_norm_eps, void* q_out, void* k_cache, void* v_cache,
-                                      int64_t cache_sb, int64_t cache_sh, int64_t cache_st, int64_t cache_capacity,
-                                      const int32_t* cache_start, int64_t uniform_cache_start,
-                                      mllm_stream_t stream) {
+namespace {
+
+// Shared by the contiguous and the paged entry point: `lay` is contiguous (cache strides per
+// sequence) or paged (strides per block, capacity = rows per sequence).
+int epilogue_entry(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh, const void* k, int64_t k_sb,
+                   int64_t k_ss, int64_t k_sh, const void* v, int64_t v_sb, int64_t v_ss, int64_t v_sh, int batch,
+                   int seq_len, int num_heads, int num_kv_heads, int head_dim, const int64_t* positions,
+                   int64_t pos_sb, int64_t pos_ss, double rope_theta, const float* rope_cos, const float* rope_sin,
+                   int64_t rope_row_sb, int64_t rope_row_ss, const void* q_norm_weight, const void* k_norm_weight,
+                   double rms_norm_eps, void* q_out, void* k_cache, void* v_cache, int64_t cache_sb,
+                   int64_t cache_sh, int64_t cache_st, int64_t cache_capacity, const KvLayout& lay,
+                   const int32_t* cache_start, int64_t uniform_cache_start, mllm_stream_t stream) {
     if (batch < 0 || seq_len < 0 || num_heads <= 0 || num_kv_heads <= 0)
         return fail(MLLM_ERR_INVALID_ARGUMENT, "qkv_epilogue: bad sizes");
     if (num_heads % num_kv_heads != 0)
@@ -360,6 +365,7 @@ extern "C" int mllm_qkv_epilogue_bf16(const void* q, int64_t q_sb, int64_t q_ss,
     a.k_cache = (__nv_bfloat16*)k_cache;
     a.v_cache = (__nv_bfloat16*)v_cache;
     a.c_sb = cache_sb; a.c_sh = cache_sh; a.c_st = cache_st; a.capacity = cache_capacity;
+    a.lay = lay;
     a.cache_start = cache_start;
     a.uniform_start = uniform_cache_start;
 
@@ -400,4 +406,44 @@ extern "C" int mllm_qkv_epilogue_bf16(const void* q, int64_t q_sb, int64_t q_ss,
     }
     if (int st = check_cuda(cudaGetLastError(), "qkv_epilogue launch")) return st;
     return ok();
+}
+
+}  // namespace
+
+extern "C" int mllm_qkv_epilogue_bf16(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh,
+                                      const void* k, int64_t k_sb, int64_t k_ss, int64_t k_sh,
+                                      const void* v, int64_t v_sb, int64_t v_ss, int64_t v_sh,
+                                      int batch, int seq_len, int num_heads, int num_kv_heads, int head_dim,
+                                      const int64_t* positions, int64_t pos_sb, int64_t pos_ss, double rope_theta,
+                                      const float* rope_cos, const float* rope_sin, int64_t rope_row_sb,
+                                      int64_t rope_row_ss, const void* q_norm_weight, const void* k_norm_weight,
+                                      double rms_norm_eps, void* q_out, void* k_cache, void* v_cache,
+                                      int64_t cache_sb, int64_t cache_sh, int64_t cache_st, int64_t cache_capacity,
+                                      const int32_t* cache_start, int64_t uniform_cache_start,
+                                      mllm_stream_t stream) {
+    return epilogue_entry(q, q_sb, q_ss, q_sh, k, k_sb, k_ss, k_sh, v, v_sb, v_ss, v_sh, batch, seq_len, num_heads,
+                          num_kv_heads, head_dim, positions, pos_sb, pos_ss, rope_theta, rope_cos, rope_sin,
+                          rope_row_sb, rope_row_ss, q_norm_weight, k_norm_weight, rms_norm_eps, q_out, k_cache,
+                          v_cache, cache_sb, cache_sh, cache_st, cache_capacity, KvLayout{}, cache_start,
+                          uniform_cache_start, stream);
+}
+
+extern "C" int mllm_qkv_epilogue_paged_bf16(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh,
+                                            const void* k, int64_t k_sb, int64_t k_ss, int64_t k_sh,
+                                            const void* v, int64_t v_sb, int64_t v_ss, int64_t v_sh,
+                                            int batch, int seq_len, int num_heads, int num_kv_heads, int head_dim,
+                                            const int64_t* positions, int64_t pos_sb, int64_t pos_ss,
+                                            double rope_theta, const float* rope_cos, const float* rope_sin,
+                                            int64_t rope_row_sb, int64_t rope_row_ss, const void* q_norm_weight,
+                                            const void* k_norm_weight, double rms_norm_eps, void* q_out,
+                                            const mllm_paged_kv* kv, const int32_t* cache_start,
+                                            int64_t uniform_cache_start, mllm_stream_t stream) {
+    KvLayout lay;
+    if (int st = paged_layout(kv, 0, head_dim, "qkv_epilogue_paged", &lay)) return st;
+    return epilogue_entry(q, q_sb, q_ss, q_sh, k, k_sb, k_ss, k_sh, v, v_sb, v_ss, v_sh, batch, seq_len, num_heads,
+                          num_kv_heads, head_dim, positions, pos_sb, pos_ss, rope_theta, rope_cos, rope_sin,
+                          rope_row_sb, rope_row_ss, q_norm_weight, k_norm_weight, rms_norm_eps, q_out, kv->k_pool,
+                          kv->v_pool, kv->block_stride, kv->head_stride, kv->row_stride,
+                          (int64_t)kv->max_blocks_per_seq * kv->block_size, lay, cache_start, uniform_cache_start,
+                          stream);
 }

@@ -17,6 +17,7 @@ tensors are required and anything else raises RuntimeError, like the reference's
 """
 from __future__ import annotations
 
+import ctypes as C
 import math
 
 import torch
@@ -129,6 +130,103 @@ class RoPE:
         return out
 
 
+class PagedKVCache:
+    """Paged KV cache for one layer (the mllm_paged_kv layout): K and V pools of `num_blocks`
+    blocks, each `block_size` rows for every kv head ([num_blocks, Hkv, block_size, D] bf16), and
+    per-sequence block tables and lengths.  Sequences of any length share the pool without
+    padding to the longest.  Blocks are handed out from a free list as sequences grow (`reserve`)
+    and zeroed when freed (`release`), so the rows past a sequence's length in its last block are
+    always finite.  The reference's KVCache (KVCache.h:9-28) is one contiguous tensor per layer;
+    this is the serving-format step beyond it."""
+
+    def __init__(self, num_blocks: int, num_kv_heads: int, head_dim: int, block_size: int = 256,
+                 max_seqs: int = 64, max_blocks_per_seq: int | None = None, device="cuda"):
+        if block_size <= 0 or block_size % 128 != 0:
+            raise RuntimeError("PagedKVCache: block_size must be a positive multiple of 128")
+        self.block_size = block_size
+        self.num_blocks = num_blocks
+        self.max_blocks_per_seq = max_blocks_per_seq or num_blocks
+        self.k_pool = torch.zeros((num_blocks, num_kv_heads, block_size, head_dim), dtype=BF16, device=device)
+        self.v_pool = torch.zeros_like(self.k_pool)
+        self.block_table = torch.zeros((max_seqs, self.max_blocks_per_seq), dtype=torch.int32, device=device)
+        self.lengths = torch.zeros(max_seqs, dtype=torch.int32, device=device)
+        self._blocks = [[] for _ in range(max_seqs)]
+        self._host_lengths = [0] * max_seqs
+        self._free = list(range(num_blocks - 1, -1, -1))   # pop() hands out block 0 first
+
+    @property
+    def capacity(self) -> int:
+        """Rows one sequence can hold."""
+        return self.max_blocks_per_seq * self.block_size
+
+    @property
+    def free_blocks(self) -> int:
+        return len(self._free)
+
+    def blocks_of(self, seq: int) -> list[int]:
+        return list(self._blocks[seq])
+
+    def reserve(self, seq: int, rows: int) -> None:
+        """Make sure sequence `seq` has blocks for `rows` rows."""
+        need = -(-rows // self.block_size)
+        if need > self.max_blocks_per_seq:
+            raise RuntimeError("PagedKVCache: sequence exceeds max_blocks_per_seq * block_size rows")
+        blocks = self._blocks[seq]
+        if need > len(blocks):
+            if need - len(blocks) > len(self._free):
+                raise RuntimeError("PagedKVCache: out of blocks")
+            start = len(blocks)
+            while len(blocks) < need:
+                blocks.append(self._free.pop())
+            self.block_table[seq, start:need] = torch.tensor(blocks[start:need], dtype=torch.int32)
+
+    def release(self, seq: int) -> None:
+        """Return sequence `seq`'s blocks to the pool (zeroed) and reset its length."""
+        blocks = self._blocks[seq]
+        if blocks:
+            idx = torch.tensor(blocks, dtype=torch.long, device=self.k_pool.device)
+            self.k_pool.index_fill_(0, idx, 0)
+            self.v_pool.index_fill_(0, idx, 0)
+            self._free.extend(reversed(blocks))
+        self._blocks[seq] = []
+        self._host_lengths[seq] = 0
+        self.lengths[seq] = 0
+
+    # -- the KVCache interface the attention functions use --
+    def host_lengths(self) -> list[int]:
+        return list(self._host_lengths)
+
+    def set_lengths(self, lens: list[int]) -> None:
+        for b, n in enumerate(lens):
+            self.reserve(b, n)
+        self._host_lengths[:len(lens)] = list(lens)
+        self.lengths[:len(lens)].copy_(torch.tensor(lens, dtype=torch.int32), non_blocking=True)
+
+    def advance(self, n: int | list[int], batch: int | None = None) -> None:
+        B = batch if batch is not None else (len(n) if isinstance(n, list) else len(self._host_lengths))
+        add = n if isinstance(n, list) else [n] * B
+        self.set_lengths([self._host_lengths[b] + add[b] for b in range(B)])
+
+    def length_of(self, batch: int) -> int:
+        lens = set(self._host_lengths[:batch])
+        if len(lens) != 1:
+            raise RuntimeError("PagedKVCache: ragged batch has no single length")
+        return lens.pop()
+
+    def descriptor(self) -> abi.PagedKV:
+        s = self.k_pool.stride()
+        return abi.PagedKV(self.k_pool.data_ptr(), self.v_pool.data_ptr(), s[0], s[1], s[2], self.num_blocks,
+                           self.block_size, self.block_table.data_ptr(), self.block_table.stride(0),
+                           self.max_blocks_per_seq)
+
+    def gather(self, seq: int, rows: int):
+        """K and V rows [Hkv, rows, D] of sequence `seq`, copied out of the pool (for tests)."""
+        blocks = self._blocks[seq][: -(-rows // self.block_size)]
+        k = torch.cat([self.k_pool[b] for b in blocks], dim=1)[:, :rows]
+        v = torch.cat([self.v_pool[b] for b in blocks], dim=1)[:, :rows]
+        return k, v
+
+
 class DecodeWorkspace:
     """Grow-only device scratch for the split-K decode partials (the C ABI never allocates)."""
 
@@ -173,6 +271,20 @@ def qkv_epilogue(q, k, v, kv_cache: KVCache, positions: torch.Tensor, rope_theta
     if q_norm_weight is not None:
         qn = q_norm_weight.to(BF16).contiguous()
         kn = k_norm_weight.to(BF16).contiguous()
+    if isinstance(kv_cache, PagedKVCache):
+        start = kv_cache.lengths[:B].clone()   # slots of the new rows: the lengths before this call
+        for b in range(B):
+            kv_cache.reserve(b, kv_cache.host_lengths()[b] + S)
+        kv = kv_cache.descriptor()
+        abi.call("mllm_qkv_epilogue_paged_bf16",
+                 _ptr(q), q.stride(0), q.stride(2), q.stride(1),
+                 _ptr(k), k.stride(0), k.stride(2), k.stride(1),
+                 _ptr(v), v.stride(0), v.stride(2), v.stride(1),
+                 B, S, H, Hkv, D, _ptr(pos), pos_sb, pos_ss, float(rope_theta),
+                 _ptr(cos), _ptr(sin), rsb, rss, _ptr(qn), _ptr(kn), float(eps), _ptr(q_out),
+                 C.byref(kv), _ptr(start), 0, abi.stream_handle())
+        kv_cache.advance(S, batch=B)
+        return q_out
     csb, csh, cst = kv_cache.strides
     abi.call("mllm_qkv_epilogue_bf16",
              _ptr(q), q.stride(0), q.stride(2), q.stride(1),
@@ -189,8 +301,13 @@ def qkv_epilogue(q, k, v, kv_cache: KVCache, positions: torch.Tensor, rope_theta
 def prefill_attention(q: torch.Tensor, kv_cache: KVCache, num_kv_heads: int) -> torch.Tensor:
     """Causal attention of Q [B,H,S,D] (the newest S rows) over the cache -> [B, S, H*D]."""
     B, H, S, D = q.shape
-    kv_len = kv_cache.length
     out = torch.empty((B, S, H * D), dtype=BF16, device=q.device)
+    if isinstance(kv_cache, PagedKVCache):
+        kv = kv_cache.descriptor()
+        abi.call("mllm_prefill_attention_paged_bf16", _ptr(q), C.byref(kv), B, H, num_kv_heads, D, S,
+                 kv_cache.length_of(B), 1.0 / math.sqrt(D), _ptr(out), abi.stream_handle())
+        return out
+    kv_len = kv_cache.length
     csb, csh, cst = kv_cache.strides
     abi.call("mllm_prefill_attention_bf16", _ptr(q), _ptr(kv_cache.key_buf), _ptr(kv_cache.value_buf),
              csb, csh, cst, B, H, num_kv_heads, D, S, kv_len, 1.0 / math.sqrt(D), _ptr(out),
@@ -206,12 +323,17 @@ def decode_attention(q: torch.Tensor, kv_cache: KVCache, num_kv_heads: int,
     qq = q.reshape(B, H, D)
     if not qq.is_contiguous():
         qq = qq.contiguous()
-    L = max_kv_len or max(kv_cache.host_lengths())
+    L = max_kv_len or max(kv_cache.host_lengths()[:B])
     L = min(L, kv_cache.capacity)
     out = torch.empty((B, 1, H * D), dtype=BF16, device=q.device)
     lib = abi.load()
     nbytes = lib.mllm_decode_attention_workspace_size(B, H, num_kv_heads, D, L)
     ws = _WS.get(nbytes, q.device)
+    if isinstance(kv_cache, PagedKVCache):
+        kv = kv_cache.descriptor()
+        abi.call("mllm_decode_attention_paged_bf16", _ptr(qq), C.byref(kv), _ptr(kv_cache.lengths), B, H,
+                 num_kv_heads, D, L, 1.0 / math.sqrt(D), _ptr(out), _ptr(ws), ws.numel(), abi.stream_handle())
+        return out
     csb, csh, cst = kv_cache.strides
     abi.call("mllm_decode_attention_bf16", _ptr(qq), _ptr(kv_cache.key_buf), _ptr(kv_cache.value_buf),
              csb, csh, cst, _ptr(kv_cache.lengths), B, H, num_kv_heads, D, L, 1.0 / math.sqrt(D),
@@ -243,12 +365,23 @@ def decode_step(q, k, v, kv_cache: KVCache, positions: torch.Tensor, rope_theta:
     if q_norm_weight is not None:
         qn = q_norm_weight.to(BF16).contiguous()
         kn = k_norm_weight.to(BF16).contiguous()
-    kv_cache.advance(1)   # raises before any launch if the cache is full
-    L = min(max(kv_cache.host_lengths()), kv_cache.capacity)
+    if isinstance(kv_cache, PagedKVCache):
+        kv_cache.advance(1, batch=B)   # reserves the blocks; raises before any launch if the pool is full
+    else:
+        kv_cache.advance(1)   # raises before any launch if the cache is full
+    L = min(max(kv_cache.host_lengths()[:B]), kv_cache.capacity)
     out = torch.empty((B, 1, H * D), dtype=BF16, device=q.device)
     lib = abi.load()
     nbytes = lib.mllm_decode_attention_workspace_size(B, H, num_kv_heads, D, L)
     ws = _WS.get(nbytes, q.device)
+    if isinstance(kv_cache, PagedKVCache):
+        kv = kv_cache.descriptor()
+        abi.call("mllm_decode_step_paged_bf16",
+                 _ptr(q), q.stride(0), q.stride(1), _ptr(k), k.stride(0), k.stride(1), _ptr(v), v.stride(0),
+                 v.stride(1), _ptr(pos), pos_sb, float(rope_theta), _ptr(cos), _ptr(sin), rsb, _ptr(qn), _ptr(kn),
+                 float(eps), C.byref(kv), _ptr(kv_cache.lengths), B, H, num_kv_heads, D, L, 1.0 / math.sqrt(D),
+                 _ptr(out), _ptr(ws), ws.numel(), abi.stream_handle())
+        return out
     csb, csh, cst = kv_cache.strides
     abi.call("mllm_decode_step_bf16",
              _ptr(q), q.stride(0), q.stride(1), _ptr(k), k.stride(0), k.stride(1), _ptr(v), v.stride(0), v.stride(1),

@@ -265,6 +265,54 @@ def test_decode_step_equals_epilogue_then_decode(rt, B, H, Hkv, D, prior, qk_nor
 
 
 # ---------------------------------------------------------------------------------------
+# Paged KV cache
+# ---------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("B,H,Hkv,D,S,block,qk_norm", [(3, 32, 8, 128, 300, 128, True),
+                                                         (2, 40, 8, 128, 513, 256, True),
+                                                         (2, 32, 4, 64, 200, 128, False)])
+def test_paged_cache_equals_contiguous(rt, B, H, Hkv, D, S, block, qk_norm):
+    """The same layer steps over a paged cache (blocks handed out in a shuffled order) and over a
+    contiguous cache: bit-identical q rows, cache rows, prefill output, fused decode steps and a
+    ragged decode."""
+    import random
+    g = torch.Generator(device="cuda").manual_seed(S + H)
+    steps = 4
+    cont = rt.KVCache(B, Hkv, D, S + steps + 8)
+    paged = rt.PagedKVCache(num_blocks=B * (-(-(S + steps + 8) // block)) + 3, num_kv_heads=Hkv, head_dim=D,
+                            block_size=block, max_seqs=B)
+    random.Random(S).shuffle(paged._free)
+    row = (H + 2 * Hkv) * D
+    gq = (1 + 0.1 * torch.randn(D, device="cuda", generator=g)).bfloat16() if qk_norm else None
+    gk = (1 + 0.1 * torch.randn(D, device="cuda", generator=g)).bfloat16() if qk_norm else None
+    views = lambda pr, n: (pr[..., : H * D].view(B, n, H, D).transpose(1, 2),
+                           pr[..., H * D:(H + Hkv) * D].view(B, n, Hkv, D).transpose(1, 2),
+                           pr[..., (H + Hkv) * D:].view(B, n, Hkv, D).transpose(1, 2))
+    bits = lambda t: t.contiguous().view(torch.int16)
+    proj = (torch.randn(B, S, row, device="cuda", generator=g) * 0.7).bfloat16()
+    pos = torch.arange(S, device="cuda")
+    qc = rt.qkv_epilogue(*views(proj, S), cont, pos, 1e6, gq, gk, 1e-6)
+    qp = rt.qkv_epilogue(*views(proj, S), paged, pos, 1e6, gq, gk, 1e-6)
+    assert torch.equal(bits(qc), bits(qp))
+    assert torch.equal(bits(rt.prefill_attention(qc, cont, Hkv)), bits(rt.prefill_attention(qp, paged, Hkv)))
+    for step in range(steps):
+        x = (torch.randn(B, 1, row, device="cuda", generator=g) * 0.7).bfloat16()
+        p1 = torch.tensor([S + step], device="cuda")
+        oc = rt.decode_step(*views(x, 1), cont, p1, 1e6, Hkv, gq, gk, 1e-6)
+        op = rt.decode_step(*views(x, 1), paged, p1, 1e6, Hkv, gq, gk, 1e-6)
+        assert torch.equal(bits(oc), bits(op)), f"decode step {step}"
+    L = S + steps
+    for b in range(B):
+        kp, vp = paged.gather(b, L)
+        assert torch.equal(bits(kp), bits(cont.key_buf[b, :, :L])) and torch.equal(bits(vp), bits(cont.value_buf[b, :, :L]))
+    lens = [L - 3 * b for b in range(B)]      # ragged: attend over fewer rows for later sequences
+    cont.set_lengths(lens)
+    paged.set_lengths(lens)
+    q1 = torch.randn(B, H, D, device="cuda", generator=g).bfloat16()
+    assert torch.equal(bits(rt.decode_attention(q1, cont, Hkv)), bits(rt.decode_attention(q1, paged, Hkv)))
+
+
+# ---------------------------------------------------------------------------------------
 # Prefill
 # ---------------------------------------------------------------------------------------
 
