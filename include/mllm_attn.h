@@ -10,6 +10,7 @@
  *   mllm_decode_attention_bf16  split-K flash-decode over the cache (HBM-bound)
  *   mllm_decode_step_bf16       the epilogue of one new token per sequence fused into decode
  *   mllm_*_paged_bf16           the same four over a paged KV cache (block tables)
+ *   mllm_sample                 Sampler::Sample on the device (penalty, greedy / top-k / top-p)
  *
  * plus the RoPE table builder and RoPE apply that back the `mllm::RoPE` facade.
  *
@@ -277,6 +278,37 @@ MLLM_API int mllm_decode_step_paged_bf16(const void* q, int64_t q_sb, int64_t q_
                                          int num_heads, int num_kv_heads, int head_dim, int max_kv_len,
                                          float softmax_scale, void* out, void* workspace, size_t workspace_bytes,
                                          mllm_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------
+ * Token sampling on the device.  Replaces src/core/runtime/Sampler.cpp:49-232
+ * (Sampler::Sample) for `batch` logit rows at once, with no host round trip (the reference's
+ * repetition penalty, Sampler.cpp:12-46, reads and writes one logit per previous token with a
+ * device sync each).
+ *   logits: bf16 (logits_bf16 != 0) or fp32, row b at logits + b*row_stride, `vocab` entries.
+ *       The repetition penalty is applied IN PLACE, as the reference does to its argument: each
+ *       occurrence of a token in the history divides a non-negative logit by the penalty or
+ *       multiplies a negative one, the result rounded to the logits' dtype each time.
+ *   prev_tokens / prev_counts: int64 / int32 device; row b's history is prev_counts[b] tokens at
+ *       prev_tokens + b*prev_stride (both NULL: no history).  Out-of-range ids are ignored.
+ *   temperature, top_k, top_p, use_greedy, repetition_penalty: as Sampler::Sample, with its
+ *       argument errors (non-finite temperature; top_p outside (0, 1]; empty logits).  Greedy
+ *       (use_greedy, or temperature <= 0) is the argmax, first index winning ties, NaN above
+ *       every number.  Otherwise: softmax(logits / temperature) in fp32; top_k > 0 keeps the
+ *       scores >= the top_k-th largest; top_p < 1 keeps the largest scores whose renormalised
+ *       mass, summed from the top, stays <= top_p, always keeping the top one; one draw picks the
+ *       token.  Ties at a top-k/top-p cut are all kept.
+ *   seed, offset: the draw of row b is the first output of Philox-4x32-10 with key `seed` and
+ *       counter (offset, b, 0); advance `offset` for every call.
+ *   out_tokens: int64 device [batch].
+ *   workspace: mllm_sample_workspace_size(batch, vocab) bytes when the penalty applies (> 1
+ *       with a history); contents need not be initialised. */
+MLLM_API size_t mllm_sample_workspace_size(int batch, int vocab);
+
+MLLM_API int mllm_sample(void* logits, int logits_bf16, int64_t row_stride, int batch, int vocab,
+                         const int64_t* prev_tokens, int64_t prev_stride, const int32_t* prev_counts,
+                         float temperature, int top_k, float top_p, int use_greedy, float repetition_penalty,
+                         uint64_t seed, uint64_t offset, int64_t* out_tokens, void* workspace,
+                         size_t workspace_bytes, mllm_stream_t stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

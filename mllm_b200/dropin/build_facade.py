@@ -110,7 +110,9 @@ def build_runner_module(flavor: str, reference: str = REFERENCE, verbose: bool =
     obj_dir = os.path.join(BUILD, "runner_" + flavor)
     os.makedirs(obj_dir, exist_ok=True)
     os.makedirs(os.path.dirname(out), exist_ok=True)
-    srcs = [binding] + [os.path.join(reference, "src", s) for s in RUNNER_SOURCES]
+    # the drop-in Sampler.h is header-only: the reference's Sampler.cpp is not linked with it
+    sources = [x for x in RUNNER_SOURCES if not (flavor == "dropin" and x == "core/runtime/Sampler.cpp")]
+    srcs = [binding] + [os.path.join(reference, "src", x) for x in sources]
     cflags = ["g++", "-std=c++17", "-O2", "-fPIC", "-w", *defs, "-DTORCH_EXTENSION_NAME=" + os.path.basename(out).split(".")[0],
               f"-I{sysconfig.get_paths()['include']}", *incs, *inc]
 

@@ -391,6 +391,47 @@ def decode_step(q, k, v, kv_cache: KVCache, positions: torch.Tensor, rope_theta:
     return out
 
 
+_SAMPLE_WS = DecodeWorkspace()
+
+
+def sample(logits: torch.Tensor, temperature: float = 1.0, top_k: int = 0, top_p: float = 1.0,
+           use_greedy: bool = False, previous_tokens=None, repetition_penalty: float = 1.0,
+           seed: int = 0, offset: int = 0) -> torch.Tensor:
+    """Sampler::Sample (Sampler.cpp:49-232) on the device for a batch of rows: logits [B, V] (or
+    [V]) bf16 or fp32 CUDA, penalised IN PLACE like the reference; previous_tokens: a list of
+    per-row token lists (or one list for a single row).  Returns the int64 token ids [B] on the
+    device, without a host round trip.  The sampling draw of row b comes from Philox-4x32-10 with
+    key `seed` and counter (offset, b, 0)."""
+    if not logits.is_cuda:
+        raise RuntimeError("Sampler: logits must be a CUDA tensor (no CPU fallback)")
+    if logits.dtype not in (BF16, torch.float32):
+        raise RuntimeError("Sampler: logits must be bf16 or fp32")
+    x = logits if logits.dim() == 2 else logits.view(1, -1)
+    if x.stride(1) != 1:
+        raise RuntimeError("Sampler: logits rows must be contiguous")
+    B, V = x.shape
+    prev = cnt = None
+    if previous_tokens is not None:
+        rows = previous_tokens if (len(previous_tokens) and isinstance(previous_tokens[0], (list, tuple))) \
+            else [previous_tokens]
+        if len(rows) != B:
+            raise RuntimeError("Sampler: one history per row")
+        T = max(1, max(len(r) for r in rows))
+        h = torch.full((B, T), -1, dtype=torch.int64)
+        for b, r in enumerate(rows):
+            h[b, : len(r)] = torch.tensor(list(r), dtype=torch.int64)
+        prev = h.to(x.device, non_blocking=True)
+        cnt = torch.tensor([len(r) for r in rows], dtype=torch.int32).to(x.device, non_blocking=True)
+    out = torch.empty(B, dtype=torch.int64, device=x.device)
+    lib = abi.load()
+    ws = _SAMPLE_WS.get(lib.mllm_sample_workspace_size(B, V), x.device)
+    abi.call("mllm_sample", _ptr(x), int(x.dtype == BF16), x.stride(0), B, V, _ptr(prev),
+             prev.stride(0) if prev is not None else 0, _ptr(cnt), float(temperature), int(top_k), float(top_p),
+             int(bool(use_greedy)), float(repetition_penalty), int(seed), int(offset), _ptr(out), _ptr(ws),
+             ws.numel(), abi.stream_handle())
+    return out
+
+
 def _linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """Linear::Forward (Linear.h:33-68): x @ w.T in the input dtype (a cuBLAS GEMM)."""
     if x.size(-1) != w.size(1):

@@ -52,7 +52,8 @@ def build(reference: str = DEFAULT_REFERENCE, force: bool = False, verbose: bool
            f"-I{os.path.join(src_root, 'core', 'runtime')}"]
     for p in ce.include_paths():
         cmd.append(f"-I{p}")
-    cmd += [binding, "-o", out]
+    # the runtime is header-only except the sampler, whose source is compiled alongside
+    cmd += [binding, os.path.join(src_root, "core", "runtime", "Sampler.cpp"), "-o", out]
     for p in ce.library_paths():
         cmd += [f"-L{p}", f"-Wl,-rpath,{p}"]
     cmd += ["-ltorch", "-ltorch_cpu", "-lc10", "-ltorch_python"]

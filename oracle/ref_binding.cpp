@@ -8,6 +8,7 @@
 #include <torch/extension.h>
 
 #include "core/runtime/TransformerBlock.h"  // Attention.h, RoPE.h, KVCache.h, RMSNorm.h, MLP.h, Linear.h
+#include "core/runtime/Sampler.h"
 
 #include <tuple>
 
@@ -102,6 +103,16 @@ std::tuple<Tensor, Tensor, Tensor> transformer_block_forward(
     return {out, cache.key, cache.value};
 }
 
+// Sampler::Sample (Sampler.cpp:49-232) on a copy of `logits`; returns the token and the copy,
+// which the reference's repetition penalty modifies in place.
+std::tuple<int64_t, Tensor> sample(Tensor logits, double temperature, int64_t top_k, double top_p, bool use_greedy,
+                                   std::vector<int64_t> previous_tokens, double repetition_penalty) {
+    Tensor x = logits.clone();
+    const int64_t tok = mllm::Sampler::Sample(x, (float)temperature, (int)top_k, (float)top_p, use_greedy,
+                                              previous_tokens, (float)repetition_penalty);
+    return {tok, x};
+}
+
 void set_num_threads(int64_t n) { at::set_num_threads((int)n); }
 int64_t get_num_threads() { return at::get_num_threads(); }
 
@@ -116,6 +127,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("attention_forward", &attention_forward);
     m.def("attention_forward_projected", &attention_forward_projected);
     m.def("transformer_block_forward", &transformer_block_forward);
+    m.def("sample", &sample);
     m.def("set_num_threads", &set_num_threads);
     m.def("get_num_threads", &get_num_threads);
 }

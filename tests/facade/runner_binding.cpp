@@ -34,11 +34,11 @@ public:
     void reset_cache() { bundle_.runner->InitKVCache(0, 0); }
     std::string model_type() const { return bundle_.runner->GetModelType(); }
     // IModelRunner::Generate with greedy sampling (batch 1, the reference's own loop).
-    std::vector<int64_t> generate(const std::vector<int64_t>& ids, int max_new_tokens) {
+    std::vector<int64_t> generate(const std::vector<int64_t>& ids, int max_new_tokens, float repetition_penalty) {
         mllm::GenerateOptions o;
         o.max_new_tokens = max_new_tokens;
         o.use_greedy = true;
-        o.repetition_penalty = 1.0f;
+        o.repetition_penalty = repetition_penalty;
         o.eos_token_id = -1;   // random weights: never stop early
         return bundle_.runner->Generate(ids, o).tokens;
     }
@@ -86,7 +86,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         .def("forward", &Runner::forward)
         .def("reset_cache", &Runner::reset_cache)
         .def("model_type", &Runner::model_type)
-        .def("generate", &Runner::generate);
+        .def("generate", &Runner::generate, pybind11::arg("ids"), pybind11::arg("max_new_tokens"),
+             pybind11::arg("repetition_penalty") = 1.0f);
     pybind11::class_<Cache>(m, "Cache")
         .def(pybind11::init<>())
         .def("key", &Cache::key)

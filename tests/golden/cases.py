@@ -79,3 +79,28 @@ ROPE_TABLE_CASES = [(64, 1e4), (128, 1e4), (128, 1e6)]
 ROPE_POSITIONS = np.concatenate([np.arange(0, 96), np.array([255, 511, 1023, 2047, 2048, 4095,
                                                               4096, 8191, 8192, 16383, 32767, 32768]),
                                  np.random.default_rng(7).integers(0, 32769, size=64)]).astype(np.int64)
+
+
+# ---------------------------------------------------------------------------------------
+# Sampler (Sampler.cpp): logit rows with repeated maxima, negative and positive values, and
+# histories with repeats and out-of-range ids.
+# ---------------------------------------------------------------------------------------
+SAMPLER_VOCAB = 1000
+SAMPLER_PENALTIES = (1.0, 1.3, 2.0)
+
+
+def make_sampler_inputs(seed: int = 21):
+    """(logits [4, V] fp32 values that are exact bf16, histories: list of 4 int lists)."""
+    rng = np.random.default_rng(seed)
+    V = SAMPLER_VOCAB
+    logits = (rng.standard_normal((4, V)) * 3).astype(np.float32)
+    logits[1, 17] = logits[1, 900] = logits[1].max() + 1.0     # tie at the top: first index wins
+    logits[2, :] = -np.abs(logits[2, :])                        # all negative
+    logits = round_bf16(np.clip(logits, -60, 60).astype(np.float32))   # exact bf16 values
+    hist = [
+        [int(x) for x in rng.integers(0, V, 40)],
+        [17, 17, 17, 900, -1, V + 5, 3],
+        [int(x) for x in np.argsort(logits[2])[-8:]] * 2,       # the largest (closest to 0) twice
+        [int(x) for x in rng.integers(0, V, 300)],
+    ]
+    return logits, hist

@@ -30,7 +30,8 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 
 from oracle import build_ref  # noqa: E402
-from tests.golden.cases import CASES, ROPE_POSITIONS, ROPE_TABLE_CASES, make_inputs  # noqa: E402
+from tests.golden.cases import (CASES, ROPE_POSITIONS, ROPE_TABLE_CASES, SAMPLER_PENALTIES,  # noqa: E402
+                                make_inputs, make_sampler_inputs)
 
 
 def load_ref():
@@ -123,6 +124,19 @@ def main() -> None:
     rope["positions"] = ROPE_POSITIONS
     path = os.path.join(HERE, "rope_tables.npz")
     np.savez_compressed(path, **rope)
+    print(f"wrote {path} ({os.path.getsize(path)} B)")
+    # Sampler::Sample, greedy branch with the repetition penalty, in bf16 and fp32
+    logits, hist = make_sampler_inputs()
+    samp = {"logits": logits}
+    for dn, dt in (("bf16", torch.bfloat16), ("f32", torch.float32)):
+        for pen in SAMPLER_PENALTIES:
+            for r in range(logits.shape[0]):
+                tok, x = R.sample(torch.from_numpy(logits[r]).to(dt), 1.0, 0, 1.0, True, hist[r], pen)
+                tag = f"{dn}_p{int(pen * 10)}_r{r}"
+                samp["token_" + tag] = np.array(tok)
+                samp["logits_" + tag] = x.float().numpy()
+    path = os.path.join(HERE, "sampler.npz")
+    np.savez_compressed(path, **samp)
     print(f"wrote {path} ({os.path.getsize(path)} B)")
 
 

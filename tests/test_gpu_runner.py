@@ -80,3 +80,22 @@ def test_generate_greedy_tokens(runners):
         logits = ref.forward(torch.tensor([prompt + t_ref[:k]]))[0, -1].float()
         top2 = torch.topk(logits, 2).values
         assert (top2[0] - top2[1]).item() < 0.05, f"diverged at step {k} with a clear margin"
+
+
+def test_generate_greedy_with_repetition_penalty(runners):
+    """The same with the repetition penalty (1.3): the drop-in Sampler penalises on the device
+    (mllm_sample) what the reference penalises one .item() at a time."""
+    from oracle import sampler_oracle as SO
+    ref, new = runners
+    prompt = list(np.random.default_rng(11).integers(0, TINY.vocab, size=19))
+    t_ref = ref.generate(prompt, 24, 1.3)
+    t_new = new.generate(prompt, 24, 1.3)
+    assert len(t_ref) == len(t_new) == 24
+    if t_ref != t_new:
+        k = next(i for i, (a, b) in enumerate(zip(t_ref, t_new)) if a != b)
+        ref.reset_cache()
+        ctx = prompt + t_ref[:k]
+        logits = ref.forward(torch.tensor([ctx]))[0, -1].float().cpu().numpy()
+        pen = SO.apply_repetition_penalty(logits, ctx, 1.3, "bf16")
+        top2 = np.sort(pen)[-2:]
+        assert top2[1] - top2[0] < 0.05, f"diverged at step {k} with a clear margin"

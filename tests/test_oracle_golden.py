@@ -143,3 +143,20 @@ def test_oracle_planted_mistake_is_caught():
     wrong = np.concatenate([k[..., half:], -k[..., :half]], axis=-1)   # cat(x2, -x1): sign flip
     bad = O.round_bf16((k * cos).astype(np.float32) + (wrong * sin).astype(np.float32))
     assert not np.array_equal(O.bf16_bits(bad), g["prefill_key_bits"][:, :, : k.shape[2]])
+
+
+def test_sampler_oracle_matches_reference_fixture():
+    """oracle/sampler_oracle.py against the compiled reference Sampler (tests/golden/sampler.npz):
+    the penalised logits bit for bit and the greedy token, bf16 and fp32, penalties 1.0/1.3/2.0."""
+    from oracle import sampler_oracle as SO
+    from tests.golden.cases import SAMPLER_PENALTIES, make_sampler_inputs
+    g = np.load(os.path.join(GOLDEN_DIR, "sampler.npz"))
+    logits, hist = make_sampler_inputs()
+    np.testing.assert_array_equal(logits, g["logits"])
+    for dn in ("bf16", "f32"):
+        for pen in SAMPLER_PENALTIES:
+            for r in range(logits.shape[0]):
+                tag = f"{dn}_p{int(pen * 10)}_r{r}"
+                tok, x = SO.sample_greedy(logits[r], hist[r], pen, dn)
+                assert tok == int(g["token_" + tag]), tag
+                np.testing.assert_array_equal(x.view(np.uint32), g["logits_" + tag].view(np.uint32), err_msg=tag)
