@@ -470,7 +470,40 @@ def run_gpu(args, rank, world, device):
         oproj_ms = max_over_ranks(statistics.mean(e[0].elapsed_time(e[1]) for e in evo))
         ar_ms = max_over_ranks(statistics.mean(e[1].elapsed_time(e[2]) for e in evo))
         ar_bytes = o_part.numel() * 2
-        pre = {"pre_ms": pre_ms, "attn_ms": attn_ms, "steps": ksteps, "oproj_ms": oproj_ms,
+        # the same exchange as tp_attention_block runs it: o_proj in 4 row pieces, each piece's
+        # all-reduce overlapping the next piece's GEMM (mllm_b200.tp.oproj_allreduce)
+        from mllm_b200.tp import oproj_allreduce
+        attn2d = op.view(Bp * S, Hr * D)
+        for _ in range(2):
+            oproj_allreduce(attn2d, w_o)
+        barrier()
+        torch.cuda.synchronize()
+        p0.record(stream)
+        for i in range(ksteps):
+            oproj_allreduce(attn2d, w_o)
+        p1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        overlap_ms = max_over_ranks(p0.elapsed_time(p1)) / ksteps
+        # the exchange over NVLink copy engines: partial rows copied to their owner as each GEMM
+        # piece finishes, summed there, final rows copied back (mllm_b200.tp.PeerExchange)
+        peer_ms = None
+        if world > 1:
+            from mllm_b200.tp import PeerExchange
+            ex = PeerExchange(Bp * S, HIDDEN, sub=4)
+            for _ in range(2):
+                ex(attn2d, w_o)
+            barrier()
+            torch.cuda.synchronize()
+            p0.record(stream)
+            for i in range(ksteps):
+                ex(attn2d, w_o)
+            p1.record(stream)
+            torch.cuda.synchronize()
+            barrier()
+            peer_ms = max_over_ranks(p0.elapsed_time(p1)) / ksteps
+            ex.close()
+        pre = {"peer_ms": peer_ms, "pre_ms": pre_ms, "attn_ms": attn_ms, "steps": ksteps, "oproj_ms": oproj_ms, "overlap_ms": overlap_ms,
                "allreduce_ms": ar_ms if world > 1 else 0.0, "allreduce_bytes": ar_bytes if world > 1 else 0,
                "allreduce_busbw_gbs": (2 * (world - 1) / world * ar_bytes / (ar_ms * 1e-3) / 1e9)
                if world > 1 and ar_ms > 0 else None}
@@ -781,8 +814,12 @@ def main():
             "value": fl / (p["pre_ms"] * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": p["pre_ms"],
             "steps": p["steps"],
             "tp_exchange": {"o_proj_ms": p["oproj_ms"], "allreduce_ms": p["allreduce_ms"],
+                            "overlapped_ms": p["overlap_ms"], "peer_exchange_ms": p["peer_ms"],
                             "allreduce_bytes": p["allreduce_bytes"], "allreduce_busbw_gbs": p["allreduce_busbw_gbs"],
-                            "note": "column-sharded o_proj GEMM + NCCL all-reduce of the [B*S, hidden] partials"},
+                            "note": "column-sharded o_proj GEMM + NCCL all-reduce of the [B*S, hidden] partials; "
+                                    "overlapped_ms: GEMM in 4 pieces, each piece's all-reduce overlapping the "
+                                    "next GEMM; peer_exchange_ms: GEMM pieces sent to their owner rank over "
+                                    "NVLink copy engines, summed there and copied back (no NCCL)"},
             "roofline": {"bound": "tensor", "kernel": "prefill_kernel<128>",
                          "achieved": fl / n / (p["attn_ms"] * 1e-3) / 1e12, "peak": tf_peak, "unit": "TFLOP/s",
                          "frac": fl / n / (p["attn_ms"] * 1e-3) / 1e12 / tf_peak, "peak_source": peak_src,

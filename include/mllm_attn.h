@@ -310,6 +310,32 @@ MLLM_API int mllm_sample(void* logits, int logits_bf16, int64_t row_stride, int 
                          uint64_t seed, uint64_t offset, int64_t* out_tokens, void* workspace,
                          size_t workspace_bytes, mllm_stream_t stream);
 
+/* ----------------------------------------------------------------------------------------
+ * Peer-memory plumbing for the tensor-parallel o_proj exchange (no reference counterpart: the
+ * reference runs on one device, QwenRunner.cpp:236,328).  mllm_b200/tp.py's PeerExchange
+ * sums the ranks' o_proj partials with these: copies over NVLink on the copy engines, flags
+ * raised in the owner's memory, a bounded wait, and the sum.
+ *   mllm_ipc_alloc/free: cudaMalloc'd, zero-filled device memory to share (setup, not per call)
+ *   mllm_ipc_get_handle / open_handle / close_handle: CUDA IPC of such an allocation's base;
+ *       the handle is MLLM_IPC_HANDLE_BYTES bytes
+ *   mllm_copy_async: device-to-device copy (either side may be a peer's opened allocation)
+ *   mllm_signal_u32: after the stream's earlier work, store `value` to *flag with system-scope
+ *       release (flag may be a peer's memory)
+ *   mllm_wait_u32: the stream's later work waits until (int32)(*flag - value) >= 0; gives up
+ *       after about a second and records MLLM_ERR_DEVICE_TIMEOUT (mllm_attn_device_status)
+ *   mllm_sum_bf16: out[i] = sum over the n (<= 8) sources in order, fp32, one rounding; count
+ *       is even */
+#define MLLM_IPC_HANDLE_BYTES 64
+MLLM_API int mllm_ipc_alloc(size_t bytes, void** ptr);
+MLLM_API int mllm_ipc_free(void* ptr);
+MLLM_API int mllm_ipc_get_handle(const void* ptr, void* handle);
+MLLM_API int mllm_ipc_open_handle(const void* handle, void** ptr);
+MLLM_API int mllm_ipc_close_handle(void* ptr);
+MLLM_API int mllm_copy_async(void* dst, const void* src, size_t bytes, mllm_stream_t stream);
+MLLM_API int mllm_signal_u32(uint32_t* flag, uint32_t value, mllm_stream_t stream);
+MLLM_API int mllm_wait_u32(const uint32_t* flag, uint32_t value, mllm_stream_t stream);
+MLLM_API int mllm_sum_bf16(void* out, const void* const* srcs, int n, int64_t count, mllm_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

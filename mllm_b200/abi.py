@@ -70,6 +70,15 @@ SIGNATURES = {
     "mllm_decode_attention_paged_bf16": (_i, [_p, _kv, _p, _i, _i, _i, _i, _i, _f, _p, _p, _sz, _p]),
     "mllm_decode_step_paged_bf16": (_i, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _d, _p, _p,
                                          _i64, _p, _p, _d, _kv, _p, _i, _i, _i, _i, _i, _f, _p, _p, _sz, _p]),
+    "mllm_ipc_alloc": (_i, [_sz, C.POINTER(C.c_void_p)]),
+    "mllm_ipc_free": (_i, [_p]),
+    "mllm_ipc_get_handle": (_i, [_p, _p]),
+    "mllm_ipc_open_handle": (_i, [_p, C.POINTER(C.c_void_p)]),
+    "mllm_ipc_close_handle": (_i, [_p]),
+    "mllm_copy_async": (_i, [_p, _p, _sz, _p]),
+    "mllm_signal_u32": (_i, [_p, C.c_uint32, _p]),
+    "mllm_wait_u32": (_i, [_p, C.c_uint32, _p]),
+    "mllm_sum_bf16": (_i, [_p, C.POINTER(C.c_void_p), _i, _i64, _p]),
     "mllm_sample_workspace_size": (_sz, [_i, _i]),
     "mllm_sample": (_i, [_p, _i, _i64, _i, _i, _p, _i64, _p, _f, _i, _f, _i, _f, C.c_uint64, C.c_uint64, _p, _p,
                          _sz, _p]),

@@ -123,15 +123,17 @@ extern "C" const char* mllm_attn_last_error(void) { return t_last_error.c_str();
 
 extern "C" int mllm_attn_device_status(mllm_stream_t stream) {
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    unsigned v[3] = {0u, 0u, 0u};
-    int (*readers[3])(cudaStream_t, unsigned*) = {read_clear_status_decode, read_clear_status_prefill,
-                                                   read_clear_status_epilogue};
-    for (int i = 0; i < 3; ++i) {
+    constexpr int kReaders = 4;
+    unsigned v[kReaders] = {0u, 0u, 0u, 0u};
+    int (*readers[kReaders])(cudaStream_t, unsigned*) = {read_clear_status_decode, read_clear_status_prefill,
+                                                         read_clear_status_epilogue, read_clear_status_peer};
+    for (int i = 0; i < kReaders; ++i) {
         const int e = readers[i](s, &v[i]);
         if (e != 0) return check_cuda((cudaError_t)e, "read device status");
     }
     if (int st = check_cuda(cudaStreamSynchronize(s), "synchronize")) return st;
-    const unsigned all = v[0] | v[1] | v[2];
+    unsigned all = 0u;
+    for (int i = 0; i < kReaders; ++i) all |= v[i];
     if (all & kErrTimeout) return fail(MLLM_ERR_DEVICE_TIMEOUT, "a kernel's bounded wait expired");
     if (all & kErrBadLength) return fail(MLLM_ERR_DEVICE_LENGTH, "a device-side length exceeded its capacity");
     return ok();

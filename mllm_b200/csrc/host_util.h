@@ -47,6 +47,7 @@ inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintp
 int read_clear_status_decode(cudaStream_t s, unsigned* out);
 int read_clear_status_prefill(cudaStream_t s, unsigned* out);
 int read_clear_status_epilogue(cudaStream_t s, unsigned* out);
+int read_clear_status_peer(cudaStream_t s, unsigned* out);
 
 // Encodes a 4-D bf16 tensor map {d (inner), rows, heads, batch} with 128-byte swizzle and a
 // {box_d, box_rows, 1, 1} box.  Strides are in elements.  Returns MLLM_OK or an error.

@@ -462,7 +462,7 @@ class Attention:
         else:
             qr = qkv_epilogue(q, k, v, cache, pos, rope_theta, q_norm_weight, k_norm_weight, rms_norm_eps)
             out = prefill_attention(qr, cache, num_kv_heads)
-        return _linear(out, w_o)
+        return out if w_o is None else _linear(out, w_o)   # w_o None: the unprojected [B, S, H*D]
 
     @staticmethod
     def forward(hidden, w_q, w_k, w_v, w_o, num_heads: int, num_kv_heads: int, head_dim: int,

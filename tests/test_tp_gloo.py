@@ -103,3 +103,36 @@ def test_shard_heads_layout():
         tp.shard_heads(32, 8, 3, 0)
     with pytest.raises(RuntimeError, match="divisible"):
         tp.shard_heads(30, 8, 2, 0)
+
+
+def _oproj_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(7)
+        attn_full = torch.randn(37, 2 * 48, generator=g)          # 37 rows, 2 ranks x 48 columns
+        w_o_full = torch.randn(64, 2 * 48, generator=g)
+        sl = slice(rank * 48, (rank + 1) * 48)
+        out = tp.oproj_allreduce(attn_full[:, sl].contiguous(), w_o_full[:, sl].contiguous(), chunks=5)
+        q.put((rank, out.numpy(), (attn_full @ w_o_full.t()).numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_oproj_allreduce_chunks_equal_the_whole_exchange():
+    """o_proj in row pieces, each piece all-reduced asynchronously while the next piece's GEMM
+    runs: every rank holds the full projection (2 gloo ranks, 37 rows in 5 pieces)."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_oproj_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, out, ref in res:
+        np.testing.assert_allclose(out, ref, rtol=1e-5, atol=1e-4, err_msg=f"rank {rank}")
