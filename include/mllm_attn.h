@@ -311,6 +311,32 @@ MLLM_API int mllm_sample(void* logits, int logits_bf16, int64_t row_stride, int 
                          size_t workspace_bytes, mllm_stream_t stream);
 
 /* ----------------------------------------------------------------------------------------
+ * Projections for decode-sized token counts.  Replaces Linear::Forward (Linear.h:33-68,
+ * F::linear(x, w) = x w^T in bf16) for the attention step's q/k/v projections
+ * (TransformerBlock.h:82-96, Attention.h:52-54: three calls become one launch) and o_proj
+ * (Attention.h:322-325) when tokens <= 256.
+ *   x: bf16 [tokens, in_features], row stride x_stride (elements, multiple of 8; 16-byte aligned);
+ *       in_features a multiple of 64
+ *   weights[i]: bf16 [out_features[i], in_features], row stride weight_strides[i] (multiple of
+ *       8; 16-byte aligned); 1 <= num_weights <= 4; out_features[i] a multiple of 128
+ *   out: bf16 [tokens, out_stride], 16-byte aligned, out_stride a multiple of 8; weight i's
+ *       rows land in columns [c_i, c_i + out_features[i]), c_i = out_features[0..i) summed
+ *   workspace: mllm_linear_workspace_size(...) bytes (0 when no split is needed), 256-byte
+ *       aligned.  Its first 4096 bytes are tile counters, which must be zero before the first
+ *       use and which every call leaves at zero, so one workspace serves any number of calls of
+ *       any shapes in one stream (not concurrent calls); the rest needs no initialisation
+ * fp32 accumulation on the tensor cores, one rounding to bf16 per output.  The k range of a
+ * 128-row tile may be split over up to 8 CTAs whose fp32 partials are added in split order,
+ * so results are deterministic.  0 <= tokens <= 256. */
+MLLM_API size_t mllm_linear_workspace_size(int tokens, int num_weights, const int64_t* out_features,
+                                           int64_t in_features);
+
+MLLM_API int mllm_linear_bf16(const void* x, int64_t x_stride, int tokens, int64_t in_features, int num_weights,
+                              const void* const* weights, const int64_t* weight_strides,
+                              const int64_t* out_features, void* out, int64_t out_stride, void* workspace,
+                              size_t workspace_bytes, mllm_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------
  * Peer-memory plumbing for the tensor-parallel o_proj exchange (no reference counterpart: the
  * reference runs on one device, QwenRunner.cpp:236,328).  mllm_b200/tp.py's PeerExchange
  * sums the ranks' o_proj partials with these: copies over NVLink on the copy engines, flags
@@ -322,7 +348,7 @@ MLLM_API int mllm_sample(void* logits, int logits_bf16, int64_t row_stride, int 
  *   mllm_signal_u32: after the stream's earlier work, store `value` to *flag with system-scope
  *       release (flag may be a peer's memory)
  *   mllm_wait_u32: the stream's later work waits until (int32)(*flag - value) >= 0; gives up
- *       after about a second and records MLLM_ERR_DEVICE_TIMEOUT (mllm_attn_device_status)
+ *       after about four seconds and records MLLM_ERR_DEVICE_TIMEOUT (mllm_attn_device_status)
  *   mllm_sum_bf16: out[i] = sum over the n (<= 8) sources in order, fp32, one rounding; count
  *       is even */
 #define MLLM_IPC_HANDLE_BYTES 64

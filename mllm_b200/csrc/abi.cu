@@ -73,7 +73,7 @@ int require_sm100(int* num_sms) {
 
 int encode_kv_map(CUtensorMap* map, const void* base, int64_t d, int64_t rows, int64_t heads, int64_t batch,
                   int64_t stride_row, int64_t stride_head, int64_t stride_batch, uint32_t box_d,
-                  uint32_t box_rows) {
+                  uint32_t box_rows, uint32_t box_heads) {
     auto fn = get_encode_fn();
     if (!fn) return fail(MLLM_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
     if (!aligned(base, 16)) return fail(MLLM_ERR_INVALID_ARGUMENT, "TMA base address must be 16-byte aligned");
@@ -85,7 +85,7 @@ int encode_kv_map(CUtensorMap* map, const void* base, int64_t d, int64_t rows, i
     cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)rows, (cuuint64_t)heads, (cuuint64_t)batch};
     cuuint64_t strides[3] = {(cuuint64_t)(stride_row * es), (cuuint64_t)(stride_head * es),
                              (cuuint64_t)(stride_batch * es)};
-    cuuint32_t box[4] = {box_d, box_rows, 1, 1};
+    cuuint32_t box[4] = {box_d, box_rows, box_heads, 1};
     cuuint32_t elem_strides[4] = {1, 1, 1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box,
                     elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

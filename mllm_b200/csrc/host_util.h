@@ -50,9 +50,11 @@ int read_clear_status_epilogue(cudaStream_t s, unsigned* out);
 int read_clear_status_peer(cudaStream_t s, unsigned* out);
 
 // Encodes a 4-D bf16 tensor map {d (inner), rows, heads, batch} with 128-byte swizzle and a
-// {box_d, box_rows, 1, 1} box.  Strides are in elements.  Returns MLLM_OK or an error.
+// {box_d, box_rows, box_heads, 1} box.  Strides are in elements and need not be ordered (a
+// weight matrix is viewed as {64 columns, rows, column blocks} with the blocks 128 B apart).
+// Returns MLLM_OK or an error.
 int encode_kv_map(CUtensorMap* map, const void* base, int64_t d, int64_t rows, int64_t heads, int64_t batch,
                   int64_t stride_row, int64_t stride_head, int64_t stride_batch, uint32_t box_d,
-                  uint32_t box_rows);
+                  uint32_t box_rows, uint32_t box_heads = 1);
 
 }  // namespace mllm_b200

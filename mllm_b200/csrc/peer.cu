@@ -6,7 +6,7 @@
 // A transfer is: (sender) cudaMemcpyAsync of rows into the owner's buffer, then, on the same
 // stream, mllm_signal_u32 of a monotonically increasing value into the owner's flag (a
 // system-scope release after the copy completed); (owner) mllm_wait_u32 on its local flag (an
-// acquire; bounded: after about a second it records MLLM_ERR_DEVICE_TIMEOUT and returns), then
+// acquire; bounded: after about four seconds it records MLLM_ERR_DEVICE_TIMEOUT and returns), then
 // kernels that read the rows.  The data moves over NVLink on the copy engines, so it overlaps
 // the GEMM running on the SMs.  No multicast object or multicast load is involved.
 #include <algorithm>
@@ -23,8 +23,12 @@ __global__ void signal_kernel(uint32_t* flag, uint32_t value) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(value) : "memory");
 }
 
+// A peer's flag depends on another process's host-side progress (its launches can lag this
+// rank's by a scheduling hiccup), so this wait allows about four seconds, not one.
+constexpr uint32_t kPeerSpinLimit = 4u * kSpinLimit;
+
 __global__ void wait_kernel(const uint32_t* flag, uint32_t value) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    for (uint32_t i = 0; i < kPeerSpinLimit; ++i) {
         uint32_t v;
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
         if ((int32_t)(v - value) >= 0) return;

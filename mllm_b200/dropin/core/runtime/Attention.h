@@ -10,7 +10,8 @@
 //           then mllm_prefill_attention_bf16 (causal GQA attention on tcgen05 tensor cores)
 //   S == 1: mllm_decode_step_bf16 (the same epilogue for the new token fused into split-K
 //           flash-decode over the cache, one launch)
-// The projections stay LibTorch GEMMs (Linear::Forward), as in the reference.
+// The projections stay LibTorch GEMMs (Linear::Forward), as in the reference, except that up to
+// 256 tokens q/k/v come from one mllm_linear_bf16 launch (b200::ProjectQKV).
 //
 // ForwardProjectedNormed is the one addition: it takes the per-head q/k RMSNorm weights that
 // the reference applies in TransformerBlock.h:103-134 and fuses that norm into the epilogue.
@@ -51,9 +52,13 @@ namespace mllm
             const auto B = hidden.size(0);
             const auto S = hidden.size(1);
             // [B, S, h*D] -> [B, h, S, D] views; the epilogue reads them through their strides.
-            auto q = Linear::Forward(hidden, w_q).view({B, S, num_heads, head_dim}).transpose(1, 2);
-            auto k = Linear::Forward(hidden, w_k).view({B, S, num_kv_heads, head_dim}).transpose(1, 2);
-            auto v = Linear::Forward(hidden, w_v).view({B, S, num_kv_heads, head_dim}).transpose(1, 2);
+            torch::Tensor q, k, v;
+            if (!b200::ProjectQKV(hidden, w_q, w_k, w_v, num_heads, num_kv_heads, head_dim, &q, &k, &v))
+            {
+                q = Linear::Forward(hidden, w_q).view({B, S, num_heads, head_dim}).transpose(1, 2);
+                k = Linear::Forward(hidden, w_k).view({B, S, num_kv_heads, head_dim}).transpose(1, 2);
+                v = Linear::Forward(hidden, w_v).view({B, S, num_kv_heads, head_dim}).transpose(1, 2);
+            }
             return ForwardProjected(q, k, v, w_o, num_heads, num_kv_heads, head_dim, rope_theta,
                                     position_ids, kv_cache);
         }

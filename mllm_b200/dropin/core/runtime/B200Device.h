@@ -47,6 +47,67 @@ namespace mllm
             }
         }
 
+        // Grow-only, zero-filled scratch for mllm_linear_bf16's split partials and tile counters
+        // (every call leaves the counters at zero, so the buffer is reused as is).
+        inline torch::Tensor LinearWorkspace(size_t bytes, const torch::Device& dev)
+        {
+            thread_local torch::Tensor ws;
+            if (!ws.defined() || (size_t)ws.numel() < bytes || ws.device() != dev)
+            {
+                ws = torch::zeros({(int64_t)std::max<size_t>(bytes, (size_t)1 << 20)},
+                                  torch::TensorOptions().dtype(torch::kUInt8).device(dev));
+            }
+            return ws;
+        }
+
+        // The attention step's q/k/v projections (Linear.h:33-68, three F::linear calls in
+        // TransformerBlock.h:82-96 / Attention.h:52-54) as ONE mllm_linear_bf16 launch when the
+        // shapes allow it (bf16 CUDA, at most 256 tokens, hidden a multiple of 64, projection rows
+        // multiples of 128): q|k|v side by side in one [B, S, (H + 2 Hkv) D] tensor, returned as
+        // the same [B, h, S, D] views the three GEMMs would give.  Returns false (and touches
+        // nothing) when the shapes do not fit; the caller then runs the three GEMMs.
+        inline bool ProjectQKV(const torch::Tensor& x, const torch::Tensor& w_q, const torch::Tensor& w_k,
+                               const torch::Tensor& w_v, int64_t num_heads, int64_t num_kv_heads,
+                               int64_t head_dim, torch::Tensor* q, torch::Tensor* k, torch::Tensor* v)
+        {
+            if (x.dim() != 3 || !x.is_cuda() || x.scalar_type() != torch::kBFloat16)
+                return false;
+            const int64_t B = x.size(0), S = x.size(1), K = x.size(2);
+            if (B * S > 256 || B * S == 0 || K % 64 != 0)
+                return false;
+            const torch::Tensor* ws_[3] = {&w_q, &w_k, &w_v};
+            for (const torch::Tensor* w : ws_)
+            {
+                if (!w->defined() || !w->is_cuda() || w->scalar_type() != torch::kBFloat16 || w->dim() != 2 ||
+                    w->size(1) != K || w->stride(1) != 1 || w->size(0) % 128 != 0 || w->stride(0) % 8 != 0 ||
+                    reinterpret_cast<uintptr_t>(w->data_ptr()) % 16 != 0)
+                    return false;
+            }
+            const int64_t hq = num_heads * head_dim, hk = num_kv_heads * head_dim;
+            if (w_q.size(0) != hq || w_k.size(0) != hk || w_v.size(0) != hk)
+                return false;
+            torch::Tensor x2 = x.reshape({B * S, K});
+            if (x2.stride(1) != 1 || x2.stride(0) % 8 != 0 || reinterpret_cast<uintptr_t>(x2.data_ptr()) % 16 != 0)
+                x2 = x2.contiguous();
+            auto qkv = torch::empty({B * S, hq + 2 * hk}, x.options());
+            const void* wp[3] = {w_q.data_ptr(), w_k.data_ptr(), w_v.data_ptr()};
+            const int64_t wst[3] = {w_q.stride(0), w_k.stride(0), w_v.stride(0)};
+            const int64_t nf[3] = {hq, hk, hk};
+            const size_t bytes = mllm_linear_workspace_size((int)(B * S), 3, nf, K);
+            torch::Tensor ws;
+            if (bytes > 0)
+                ws = LinearWorkspace(bytes, x.device());
+            Check(mllm_linear_bf16(x2.data_ptr(), x2.stride(0), (int)(B * S), K, 3, wp, wst, nf, qkv.data_ptr(),
+                                   qkv.stride(0), bytes > 0 ? ws.data_ptr() : nullptr,
+                                   bytes > 0 ? (size_t)ws.numel() : 0, CurrentStream()),
+                  "Linear");
+            auto q3 = qkv.view({B, S, hq + 2 * hk});
+            *q = q3.narrow(2, 0, hq).view({B, S, num_heads, head_dim}).transpose(1, 2);
+            *k = q3.narrow(2, hq, hk).view({B, S, num_kv_heads, head_dim}).transpose(1, 2);
+            *v = q3.narrow(2, hq + hk, hk).view({B, S, num_kv_heads, head_dim}).transpose(1, 2);
+            return true;
+        }
+
         // Grow-only scratch for the split-K decode partials (the C ABI never allocates).
         inline torch::Tensor DecodeWorkspace(size_t bytes, const torch::Device& dev)
         {

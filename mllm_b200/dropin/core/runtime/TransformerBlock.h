@@ -6,7 +6,8 @@
 // its sequence of steps: pre-norm (RMSNorm), attention, residual add, post-norm, SwiGLU MLP,
 // residual add.  The only change is inside the Qwen3 branch (use_qk_norm): the per-head q/k
 // RMSNorm (TransformerBlock.h:103-107,130-134) moves into the fused QKV epilogue kernel, so
-// the projections go straight from the q/k/v GEMMs into Attention::ForwardProjectedNormed.
+// the projections go straight from the q/k/v GEMMs into Attention::ForwardProjectedNormed, and up
+// to 256 tokens the three GEMMs are one mllm_linear_bf16 launch (b200::ProjectQKV).
 // RMSNorm, Linear and MLP are the reference's own headers, unchanged.
 #pragma once
 
@@ -69,9 +70,14 @@ namespace mllm
             {
                 const auto B = attn_in.size(0);
                 const auto S = attn_in.size(1);
-                auto q = Linear::Forward(attn_in, lw.w_q).view({B, S, num_heads, head_dim}).transpose(1, 2);
-                auto k = Linear::Forward(attn_in, lw.w_k).view({B, S, num_kv_heads, head_dim}).transpose(1, 2);
-                auto v = Linear::Forward(attn_in, lw.w_v).view({B, S, num_kv_heads, head_dim}).transpose(1, 2);
+                torch::Tensor q, k, v;
+                if (!b200::ProjectQKV(attn_in, lw.w_q, lw.w_k, lw.w_v, num_heads, num_kv_heads, head_dim, &q, &k,
+                                      &v))
+                {
+                    q = Linear::Forward(attn_in, lw.w_q).view({B, S, num_heads, head_dim}).transpose(1, 2);
+                    k = Linear::Forward(attn_in, lw.w_k).view({B, S, num_kv_heads, head_dim}).transpose(1, 2);
+                    v = Linear::Forward(attn_in, lw.w_v).view({B, S, num_kv_heads, head_dim}).transpose(1, 2);
+                }
                 attn_out = Attention::ForwardProjectedNormed(q, k, v, lw.w_o, num_heads, num_kv_heads, head_dim,
                                                              rope_theta, position_ids, kv_cache, lw.w_q_norm,
                                                              lw.w_k_norm, rms_norm_eps);

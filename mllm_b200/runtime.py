@@ -432,11 +432,89 @@ def sample(logits: torch.Tensor, temperature: float = 1.0, top_k: int = 0, top_p
     return out
 
 
+LINEAR_MAX_TOKENS = 256
+
+
+def linear_supported(x: torch.Tensor, weights) -> bool:
+    """Whether mllm_linear_bf16 takes this projection: bf16 CUDA tensors, at most 256 rows of x,
+    K a multiple of 64, each weight's rows a multiple of 128, unit inner strides."""
+    if not (x.is_cuda and x.dtype == BF16 and x.stride(-1) == 1 and 0 < len(weights) <= 4):
+        return False
+    T = x.numel() // x.size(-1) if x.size(-1) else 0
+    K = x.size(-1)
+    if T > LINEAR_MAX_TOKENS or K % 64 != 0:
+        return False
+    return all(w.is_cuda and w.dtype == BF16 and w.dim() == 2 and w.size(1) == K and w.stride(1) == 1
+               and w.size(0) % 128 == 0 and w.stride(0) % 8 == 0 and w.data_ptr() % 16 == 0 for w in weights)
+
+
+def linear(x: torch.Tensor, weights) -> torch.Tensor:
+    """Linear::Forward (Linear.h:33-68) of up to four weights in one launch (mllm_linear_bf16):
+    x [..., K] bf16 with at most 256 rows -> [..., sum of out_features], the weights' outputs
+    side by side (q | k | v for the three attention projections).  fp32 accumulation, one
+    rounding to bf16."""
+    weights = list(weights)
+    if not linear_supported(x, weights):
+        raise RuntimeError("linear: needs bf16 CUDA tensors, <= 256 rows, K % 64 == 0, weight rows % 128 == 0")
+    lead = x.shape[:-1]
+    K = x.size(-1)
+    x2 = x.reshape(-1, K)
+    if x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
+        x2 = x2.contiguous()
+    T = x2.size(0)
+    n = [w.size(0) for w in weights]
+    out = torch.empty((T, sum(n)), dtype=BF16, device=x.device)
+    W = len(weights)
+    wp = (C.c_void_p * W)(*[w.data_ptr() for w in weights])
+    wst = (C.c_int64 * W)(*[w.stride(0) for w in weights])
+    nf = (C.c_int64 * W)(*n)
+    need = abi.load().mllm_linear_workspace_size(T, W, nf, K)
+    ws = _linear_workspace(x.device, need)
+    abi.call("mllm_linear_bf16", _ptr(x2), x2.stride(0), T, K, W, wp, wst, nf, _ptr(out), out.stride(0),
+             _ptr(ws), ws.numel() if ws is not None else 0, abi.stream_handle())
+    return out.view(*lead, sum(n))
+
+
+_LINEAR_WS: dict = {}
+
+
+def _linear_workspace(device, nbytes: int):
+    """The split partials and tile counters of mllm_linear_bf16: one zero-filled buffer per
+    (device, stream), grown on demand; every call leaves its counters at zero."""
+    if nbytes == 0:
+        return None
+    key = (device, torch.cuda.current_stream(device).cuda_stream)
+    ws = _LINEAR_WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _LINEAR_WS[key] = ws
+    return ws
+
+
 def _linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    """Linear::Forward (Linear.h:33-68): x @ w.T in the input dtype (a cuBLAS GEMM)."""
+    """Linear::Forward (Linear.h:33-68): x @ w.T in the input dtype, a cuBLAS GEMM as in the
+    reference (for one weight mllm_linear_bf16 is not faster than cuBLAS beyond a few tokens)."""
     if x.size(-1) != w.size(1):
         raise RuntimeError("Linear: last dim of x must match weight in_features.")
     return torch.nn.functional.linear(x, w)
+
+
+def _project_qkv(h: torch.Tensor, w_q, w_k, w_v, num_heads: int, num_kv_heads: int, head_dim: int):
+    """The three attention projections (TransformerBlock.h:82-96, Attention.h:52-54) as q [B,H,S,D]
+    and k/v [B,Hkv,S,D] views.  Up to 256 tokens: one mllm_linear_bf16 launch writes q | k | v side
+    by side and the views point into it; otherwise three cuBLAS GEMMs as in the reference."""
+    B, S, E = h.shape
+    if linear_supported(h, [w_q, w_k, w_v]):
+        qkv = linear(h, [w_q, w_k, w_v])          # [B, S, (H + 2 Hkv) D]
+        hq, hk = num_heads * head_dim, num_kv_heads * head_dim
+        q = qkv[..., :hq].view(B, S, num_heads, head_dim).transpose(1, 2)
+        k = qkv[..., hq:hq + hk].view(B, S, num_kv_heads, head_dim).transpose(1, 2)
+        v = qkv[..., hq + hk:hq + 2 * hk].view(B, S, num_kv_heads, head_dim).transpose(1, 2)
+        return q, k, v
+    q = _linear(h, w_q).view(B, S, num_heads, head_dim).transpose(1, 2)
+    k = _linear(h, w_k).view(B, S, num_kv_heads, head_dim).transpose(1, 2)
+    v = _linear(h, w_v).view(B, S, num_kv_heads, head_dim).transpose(1, 2)
+    return q, k, v
 
 
 class Attention:
@@ -470,10 +548,7 @@ class Attention:
         """Attention::Forward (Attention.h:29-86): project, view, transpose, then the above."""
         if hidden.dim() != 3:
             raise RuntimeError("Attention: hidden must be [B, S, H].")
-        B, S, _ = hidden.shape
-        q = _linear(hidden, w_q).view(B, S, num_heads, head_dim).transpose(1, 2)
-        k = _linear(hidden, w_k).view(B, S, num_kv_heads, head_dim).transpose(1, 2)
-        v = _linear(hidden, w_v).view(B, S, num_kv_heads, head_dim).transpose(1, 2)
+        q, k, v = _project_qkv(hidden, w_q, w_k, w_v, num_heads, num_kv_heads, head_dim)
         return Attention.forward_projected(q, k, v, w_o, num_heads, num_kv_heads, head_dim,
                                            rope_theta, position_ids, kv_cache)
 
@@ -483,9 +558,6 @@ def attention_block(h, w_q, w_k, w_v, w_o, num_heads: int, num_kv_heads: int, he
                     rms_norm_eps: float = 1e-6):
     """The attention half of TransformerBlock::Forward (TransformerBlock.h:77-195) after the
     input RMSNorm: Qwen3 branch when norm weights are given, Llama branch otherwise."""
-    B, S, _ = h.shape
-    q = _linear(h, w_q).view(B, S, num_heads, head_dim).transpose(1, 2)
-    k = _linear(h, w_k).view(B, S, num_kv_heads, head_dim).transpose(1, 2)
-    v = _linear(h, w_v).view(B, S, num_kv_heads, head_dim).transpose(1, 2)
+    q, k, v = _project_qkv(h, w_q, w_k, w_v, num_heads, num_kv_heads, head_dim)
     return Attention.forward_projected(q, k, v, w_o, num_heads, num_kv_heads, head_dim, rope_theta,
                                        position_ids, kv_cache, w_q_norm, w_k_norm, rms_norm_eps)

@@ -64,6 +64,26 @@ def test_host_side_argument_validation(lib):
     assert step(8, 2, 128, theta=0.0) == 1 and b"positions" in lib.mllm_attn_last_error()
 
 
+def test_linear_argument_validation(lib):
+    """mllm_linear_bf16 rejects unsupported shapes before touching the device."""
+    w = (C.c_void_p * 2)(16, 16)
+    ws = (C.c_int64 * 2)(4096, 4096)
+
+    def call(tokens=32, K=4096, n=(4096, 1024), nw=2):
+        nf = (C.c_int64 * 2)(*n)
+        return lib.mllm_linear_bf16(16, K, tokens, K, nw, w, ws, nf, 16, 8192, None, 0, None)
+    assert call(tokens=257) == 1 and b"tokens" in lib.mllm_attn_last_error()
+    assert call(nw=0) == 1 and call(nw=5) == 1
+    assert call(K=200) == 1 and b"multiple of 64" in lib.mllm_attn_last_error()
+    assert call(n=(4096, 1000)) == 1 and b"multiple of 128" in lib.mllm_attn_last_error()
+    assert call(tokens=0) == 0          # nothing to do, no device needed
+    # workspace: the partials of a split tile plus one counter per tile (148 SMs assumed here)
+    nf = (C.c_int64 * 3)(4096, 1024, 1024)
+    size = lib.mllm_linear_workspace_size(32, 3, nf, 4096)
+    assert size >= 48 * 2 * 32 * 128 * 4 and size % 4 == 0
+    assert lib.mllm_linear_workspace_size(300, 3, nf, 4096) == 0       # invalid -> 0
+
+
 def test_workspace_size(lib):
     ws = lib.mllm_decode_attention_workspace_size(32, 32, 8, 128, 4096)
     assert ws > 0 and ws % 256 == 0

@@ -112,6 +112,8 @@ def _exchange_worker(rank, world, port, q):
                             device_id=dev)
     try:
         from mllm_b200 import abi, tp
+        torch.matmul(torch.ones(8, 8, device=dev), torch.ones(8, 8, device=dev))   # library set-up first
+        torch.cuda.synchronize()
         out = {}
         for rows, hidden, k, sub in ((600, 512, 512, 2), (2, 4096, 2048, 1), (257, 1024, 256, 3)):
             ex = tp.PeerExchange(rows, hidden, sub=sub)
