@@ -637,6 +637,51 @@ def run_gpu(args, rank, world, device):
             "h2d": qkv.numel() * 2, "d2h": out.numel() * 2}
 
 
+def run_serve(args):
+    """Continuous batching (mllm_b200.serving) against one request at a time, the way the
+    reference's batch-1 Generate serves a queue (QwenRunner.cpp:420-545, Scheduler.cpp:45-77).
+    Qwen3-8B geometry (36 layers, hidden 4096, 32/8 heads, SwiGLU 12288, vocab 151936), random
+    bf16 weights; requests with prompt lengths U[64, 512] (seeded) and 32 new tokens each."""
+    import numpy as np
+    import torch
+    from mllm_b200 import build
+    from mllm_b200.serving import ContinuousBatcher, DecoderModel, DecoderShape
+    build.build()
+    shape = DecoderShape(vocab=151936, hidden=4096, layers=36, heads=32, kv_heads=8, head_dim=128,
+                         intermediate=12288)
+    model = DecoderModel(shape, seed=11)
+    rng = np.random.default_rng(12)
+    n_req, new_tok, serial_sample = args.serve_requests, 32, 4
+    prompts = [rng.integers(0, shape.vocab, int(n)).tolist() for n in rng.integers(64, 513, n_req)]
+
+    def serve(batch, reqs):
+        bat = ContinuousBatcher(model, max_batch=batch, num_blocks=batch * 5 + 8, block_size=128)
+        for p in reqs:
+            bat.submit(p, new_tok)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        out = bat.run()
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        del bat
+        torch.cuda.empty_cache()
+        return dt, sum(len(t) for t in out.values()), sum(len(p) for p in reqs)
+
+    serve(4, prompts[:4])     # warm-up: library set-up, cuBLAS handles, allocator
+    dt_b, tok_b, ptok_b = serve(args.serve_batch, prompts)
+    dt_s, tok_s, ptok_s = serve(1, prompts[:serial_sample])
+    line = {"metric": "batched greedy serving through mllm_b200.serving (continuous batching over the paged KV cache)",
+            "workload": f"Qwen3-8B geometry, random bf16 weights; {n_req} requests, prompts U[64, 512] tokens, "
+                        f"{new_tok} new tokens each",
+            "batched": {"max_batch": args.serve_batch, "seconds": dt_b, "new_tokens": tok_b, "prompt_tokens": ptok_b,
+                        "new_tokens_per_s": tok_b / dt_b},
+            "one_at_a_time": {"requests": serial_sample, "seconds": dt_s, "new_tokens": tok_s,
+                              "prompt_tokens": ptok_s, "new_tokens_per_s": tok_s / dt_s},
+            "speedup_new_tokens_per_s": (tok_b / dt_b) / (tok_s / dt_s),
+            "timing": "wall clock around ContinuousBatcher.run (prefills, decode steps, sampling, host reads)"}
+    print(json.dumps(line))
+
+
 def run_generate(args):
     """Full random-init Qwen3-8B (36 layers) through the reference's UNCHANGED QwenRunner, twice:
     built on the reference's own runtime headers and on the drop-in headers.  Batch 8 prompts
@@ -773,8 +818,11 @@ def main():
     ap.add_argument("--skip-prefill", action="store_true")
     ap.add_argument("--skip-ragged", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg (profiling runs)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "qwen3-8b-generate"],
-                    help="decode: the headline line; qwen3-8b-generate: full-model runner parity + speed")
+    ap.add_argument("--workload", default="decode", choices=["decode", "qwen3-8b-generate", "serve"],
+                    help="decode: the headline line; qwen3-8b-generate: full-model runner parity + speed; "
+                         "serve: continuous batching vs one request at a time")
+    ap.add_argument("--serve-requests", type=int, default=64)
+    ap.add_argument("--serve-batch", type=int, default=64)
     ap.add_argument("--gen-steps", type=int, default=128)
     ap.add_argument("--fp32-floor", action="store_true",
                     help="also run the reference runner on fp32 weights as the precision floor")
@@ -783,6 +831,9 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.workload == "qwen3-8b-generate":
         run_generate(args)
+        return
+    if args.workload == "serve":
+        run_serve(args)
         return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -192,6 +192,24 @@ class PagedKVCache:
         self._host_lengths[seq] = 0
         self.lengths[seq] = 0
 
+    def move(self, src: int, dst: int) -> None:
+        """Hand sequence `src`'s blocks and length to the empty row `dst` (its block-table row is
+        copied; no K/V row moves).  A serving loop uses it to keep its live sequences in rows
+        0..n-1 when one in the middle finishes."""
+        if src == dst:
+            return
+        if self._blocks[dst] or self._host_lengths[dst]:
+            raise RuntimeError("PagedKVCache: move target row is not empty")
+        self.block_table[dst].copy_(self.block_table[src])
+        self.lengths[dst] = self.lengths[src]
+        self._blocks[dst], self._blocks[src] = self._blocks[src], []
+        self._host_lengths[dst], self._host_lengths[src] = self._host_lengths[src], 0
+        self.lengths[src] = 0
+
+    def slot(self, seq: int) -> "PagedSlot":
+        """A one-sequence view of row `seq` (prefill of one request while other rows are live)."""
+        return PagedSlot(self, seq)
+
     # -- the KVCache interface the attention functions use --
     def host_lengths(self) -> list[int]:
         return list(self._host_lengths)
@@ -225,6 +243,57 @@ class PagedKVCache:
         k = torch.cat([self.k_pool[b] for b in blocks], dim=1)[:, :rows]
         v = torch.cat([self.v_pool[b] for b in blocks], dim=1)[:, :rows]
         return k, v
+
+
+class PagedSlot(PagedKVCache):
+    """Row `seq` of a PagedKVCache seen as a batch of one: the same pools, the parent's block-table
+    row and length (shared memory), and reserve/advance acting on that row."""
+
+    def __init__(self, parent: PagedKVCache, seq: int):   # no pool allocation: a view
+        self._parent, self._seq = parent, seq
+        self.block_size = parent.block_size
+        self.num_blocks = parent.num_blocks
+        self.max_blocks_per_seq = parent.max_blocks_per_seq
+        self.k_pool, self.v_pool = parent.k_pool, parent.v_pool
+        self.block_table = parent.block_table[seq:seq + 1]
+        self.lengths = parent.lengths[seq:seq + 1]
+
+    @property
+    def free_blocks(self) -> int:
+        return self._parent.free_blocks
+
+    def blocks_of(self, seq: int) -> list[int]:
+        return self._parent.blocks_of(self._seq + seq)
+
+    def reserve(self, seq: int, rows: int) -> None:
+        if seq != 0:
+            raise RuntimeError("PagedSlot: a view holds one sequence")
+        self._parent.reserve(self._seq, rows)
+
+    def release(self, seq: int = 0) -> None:
+        self._parent.release(self._seq)
+
+    def move(self, src: int, dst: int) -> None:
+        raise RuntimeError("PagedSlot: move rows on the parent cache")
+
+    def host_lengths(self) -> list[int]:
+        return [self._parent.host_lengths()[self._seq]]
+
+    def set_lengths(self, lens: list[int]) -> None:
+        if len(lens) != 1:
+            raise RuntimeError("PagedSlot: a view holds one sequence")
+        self._parent.reserve(self._seq, lens[0])
+        self._parent._host_lengths[self._seq] = lens[0]
+        self.lengths.fill_(lens[0])
+
+    def advance(self, n, batch: int | None = None) -> None:
+        self.set_lengths([self.host_lengths()[0] + (n[0] if isinstance(n, list) else n)])
+
+    def length_of(self, batch: int) -> int:
+        return self.host_lengths()[0]
+
+    def gather(self, seq: int, rows: int):
+        return self._parent.gather(self._seq + seq, rows)
 
 
 class DecodeWorkspace:
