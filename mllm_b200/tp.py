@@ -137,8 +137,10 @@ class PeerExchange:
             abi.call("mllm_ipc_open_handle", hh, C.byref(p))
             self.peer.append(p.value)
         self.partial = torch.empty((rows, hidden), dtype=torch.bfloat16, device=self.device)
-        self.s_send = torch.cuda.Stream(device=self.device)
-        self.s_gather = torch.cuda.Stream(device=self.device)
+        # one send and one gather stream per peer, so transfers to different peers run on
+        # different copy engines at the same time
+        self.s_send = {p: torch.cuda.Stream(device=self.device) for p in range(self.N) if p != self.r}
+        self.s_gather = {p: torch.cuda.Stream(device=self.device) for p in range(self.N) if p != self.r}
         self.s_reduce = torch.cuda.Stream(device=self.device)
         self.calls = 0
         dist.barrier(group=group)
@@ -192,10 +194,11 @@ class PeerExchange:
                 ev.record(cur)
                 nbytes = (b - a) * H * 2
                 if o != r:
-                    self.s_send.wait_event(ev)
+                    ss = self.s_send[o]
+                    ss.wait_event(ev)
                     dst = self._recv(o, st, r, a - self.block[o][0])
-                    abi.call("mllm_copy_async", dst, self.partial[a:b].data_ptr(), nbytes, h(self.s_send))
-                    abi.call("mllm_signal_u32", self._recv_flag(o, r), (base + j + 1) & 0xFFFFFFFF, h(self.s_send))
+                    abi.call("mllm_copy_async", dst, self.partial[a:b].data_ptr(), nbytes, h(ss))
+                    abi.call("mllm_signal_u32", self._recv_flag(o, r), (base + j + 1) & 0xFFFFFFFF, h(ss))
                     continue
                 # own piece: wait for the others' partials, sum, send the final rows everywhere
                 self.s_reduce.wait_event(ev)
@@ -210,19 +213,17 @@ class PeerExchange:
                 abi.call("mllm_sum_bf16", self._out(r, st, a), srcs, N, (b - a) * H, h(self.s_reduce))
                 ev2 = torch.cuda.Event()
                 ev2.record(self.s_reduce)
-                self.s_gather.wait_event(ev2)
-                for p in range(N):
-                    if p == r:
-                        continue
-                    abi.call("mllm_copy_async", self._out(p, st, a), self._out(r, st, a), nbytes, h(self.s_gather))
-                    abi.call("mllm_signal_u32", self._out_flag(p, r), (base + j + 1) & 0xFFFFFFFF, h(self.s_gather))
+                for p, sg in self.s_gather.items():
+                    sg.wait_event(ev2)
+                    abi.call("mllm_copy_async", self._out(p, st, a), self._out(r, st, a), nbytes, h(sg))
+                    abi.call("mllm_signal_u32", self._out_flag(p, r), (base + j + 1) & 0xFFFFFFFF, h(sg))
         # the output is complete once every other rank has delivered all its pieces
         cur.wait_stream(self.s_reduce)
         for s in range(N):
             if s != r:
                 abi.call("mllm_wait_u32", self._out_flag(r, s), (base + sub) & 0xFFFFFFFF, h(cur))
-        cur.wait_stream(self.s_send)     # the next call's GEMMs overwrite `partial`
-        cur.wait_stream(self.s_gather)
+        for st_ in list(self.s_send.values()) + list(self.s_gather.values()):
+            cur.wait_stream(st_)         # the next call's GEMMs overwrite `partial`
         return self._tensor(self._out(r, st, 0), self.rows)
 
     def close(self):
