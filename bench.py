@@ -527,8 +527,9 @@ def run_gpu(args, rank, world, device):
         torch.cuda.synchronize()
         barrier()
         overlap_ms = max_over_ranks(p0.elapsed_time(p1)) / ksteps
-        # the exchange over NVLink copy engines: partial rows copied to their owner as each GEMM
-        # piece finishes, summed there, final rows copied back (mllm_b200.tp.PeerExchange)
+        # the exchange over NVLink peer memory: each GEMM piece lands in a buffer the other ranks
+        # can read; its owner pulls it from every rank, sums and pushes the rows to every rank
+        # (mllm_b200.tp.PeerExchange)
         peer_ms = None
         if world > 1:
             from mllm_b200.tp import PeerExchange
@@ -925,8 +926,9 @@ def main():
                             "allreduce_bytes": p["allreduce_bytes"], "allreduce_busbw_gbs": p["allreduce_busbw_gbs"],
                             "note": "column-sharded o_proj GEMM + NCCL all-reduce of the [B*S, hidden] partials; "
                                     "overlapped_ms: GEMM in 4 pieces, each piece's all-reduce overlapping the "
-                                    "next GEMM; peer_exchange_ms: GEMM pieces sent to their owner rank over "
-                                    "NVLink copy engines, summed there and copied back (no NCCL)"},
+                                    "next GEMM; peer_exchange_ms: GEMM pieces written to a buffer every rank "
+                                    "can read; each owner's kernel pulls its rows from all ranks over NVLink, "
+                                    "sums them and stores the result into every rank (no NCCL)"},
             "roofline": {"bound": "tensor", "kernel": "prefill_kernel<128>",
                          "achieved": fl / n / (p["attn_ms"] * 1e-3) / 1e12, "peak": tf_peak, "unit": "TFLOP/s",
                          "frac": fl / n / (p["attn_ms"] * 1e-3) / 1e12 / tf_peak, "peak_source": peak_src,

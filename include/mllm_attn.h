@@ -339,8 +339,9 @@ MLLM_API int mllm_linear_bf16(const void* x, int64_t x_stride, int tokens, int64
 /* ----------------------------------------------------------------------------------------
  * Peer-memory plumbing for the tensor-parallel o_proj exchange (no reference counterpart: the
  * reference runs on one device, QwenRunner.cpp:236,328).  mllm_b200/tp.py's PeerExchange
- * sums the ranks' o_proj partials with these: copies over NVLink on the copy engines, flags
- * raised in the owner's memory, a bounded wait, and the sum.
+ * sums the ranks' o_proj partials with these: flags raised in a peer's memory, a bounded
+ * wait, and a sum kernel that reads every rank's partial rows over NVLink and stores the sum
+ * into every rank's output rows.
  *   mllm_ipc_alloc/free: cudaMalloc'd, zero-filled device memory to share (setup, not per call)
  *   mllm_ipc_get_handle / open_handle / close_handle: CUDA IPC of such an allocation's base;
  *       the handle is MLLM_IPC_HANDLE_BYTES bytes
@@ -349,8 +350,9 @@ MLLM_API int mllm_linear_bf16(const void* x, int64_t x_stride, int tokens, int64
  *       release (flag may be a peer's memory)
  *   mllm_wait_u32: the stream's later work waits until (int32)(*flag - value) >= 0; gives up
  *       after about four seconds and records MLLM_ERR_DEVICE_TIMEOUT (mllm_attn_device_status)
- *   mllm_sum_bf16: out[i] = sum over the n (<= 8) sources in order, fp32, one rounding; count
- *       is even */
+ *   mllm_sum_bf16: dsts[d][i] = sum over s of srcs[s][i] for every d < n_dst, fp32 in the order
+ *       s = 0, 1, ..., one rounding to bf16; 1..8 sources and destinations (either may be a
+ *       peer's opened allocation), 16-byte aligned, count a multiple of 8 */
 #define MLLM_IPC_HANDLE_BYTES 64
 MLLM_API int mllm_ipc_alloc(size_t bytes, void** ptr);
 MLLM_API int mllm_ipc_free(void* ptr);
@@ -360,7 +362,8 @@ MLLM_API int mllm_ipc_close_handle(void* ptr);
 MLLM_API int mllm_copy_async(void* dst, const void* src, size_t bytes, mllm_stream_t stream);
 MLLM_API int mllm_signal_u32(uint32_t* flag, uint32_t value, mllm_stream_t stream);
 MLLM_API int mllm_wait_u32(const uint32_t* flag, uint32_t value, mllm_stream_t stream);
-MLLM_API int mllm_sum_bf16(void* out, const void* const* srcs, int n, int64_t count, mllm_stream_t stream);
+MLLM_API int mllm_sum_bf16(void* const* dsts, int n_dst, const void* const* srcs, int n_src, int64_t count,
+                           mllm_stream_t stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

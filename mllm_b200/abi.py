@@ -81,7 +81,7 @@ SIGNATURES = {
     "mllm_copy_async": (_i, [_p, _p, _sz, _p]),
     "mllm_signal_u32": (_i, [_p, C.c_uint32, _p]),
     "mllm_wait_u32": (_i, [_p, C.c_uint32, _p]),
-    "mllm_sum_bf16": (_i, [_p, C.POINTER(C.c_void_p), _i, _i64, _p]),
+    "mllm_sum_bf16": (_i, [C.POINTER(C.c_void_p), _i, C.POINTER(C.c_void_p), _i, _i64, _p]),
     "mllm_sample_workspace_size": (_sz, [_i, _i]),
     "mllm_sample": (_i, [_p, _i, _i64, _i, _i, _p, _i64, _p, _f, _i, _f, _i, _f, C.c_uint64, C.c_uint64, _p, _p,
                          _sz, _p]),

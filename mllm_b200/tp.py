@@ -79,22 +79,25 @@ def oproj_allreduce(attn, w_o, group=None, chunks: int = 4):
 
 
 class PeerExchange:
-    """The o_proj exchange over NVLink copy engines: each rank's o_proj partial [T, hidden] summed
+    """The o_proj exchange over NVLink peer memory: each rank's o_proj partial [T, hidden] summed
     over the ranks, every rank ending with the full sum, without an NCCL all-reduce.
 
     The rows are split into N owner blocks (block o belongs to rank o) of `sub` pieces each.  A
-    rank computes its partial piece by piece, the pieces it does not own first in each round:
-      * a piece owned by rank o goes to o's receive buffer (cudaMemcpyAsync over NVLink on a copy
-        stream, so it overlaps the GEMM of the next pieces), after which a flag in o's memory is
-        raised to a per-call counter;
-      * once its own piece is computed, the owner waits (bounded) for the other ranks' flags, sums
-        the N partials of the piece in rank order (fp32, one rounding), and copies the final rows
-        to every other rank the same way.
-    The result for rank r's rows is bit-identical on every rank.  Buffers are CUDA IPC
-    allocations shared once at construction (mllm_ipc_*); receive and output buffers alternate
-    between two sets by call parity, and a rank only writes a peer's set after having received
-    that peer's previous output, so no write can overtake a read.  A returned output stays valid
-    until the call after next.  No multicast object or load is used."""
+    rank computes its partial piece by piece into a buffer the other ranks can read, the pieces
+    it does not own first in each round, and after each piece raises a flag in the owner's
+    memory.  Once its own piece is computed, the owner waits (bounded) for the other ranks'
+    flags and runs one kernel (mllm_sum_bf16) that reads the piece from every rank's buffer over
+    NVLink, adds the N partials in rank order (fp32, one rounding) and stores the result into
+    every rank's output buffer; then it raises a flag in each rank's memory.  So the SMs move
+    the data, the transfers of one piece overlap the GEMM of the next, and NVLink carries
+    partials in and final rows out at the same time.
+
+    Buffers are CUDA IPC allocations shared once at construction (mllm_ipc_*).  Output buffers
+    alternate between two sets by call parity (a returned output stays valid until the call after
+    next); the partial buffer needs one copy, because a call ends only after every owner has
+    stored its rows, i.e. after every read of this rank's partial.  Flags count up monotonically.
+    No multicast object or load is used, and no library kernel touches a peer's memory (the GEMM
+    writes this rank's own buffer)."""
 
     def __init__(self, rows: int, hidden: int, group=None, sub: int = 2, device=None):
         import ctypes as C
@@ -107,6 +110,10 @@ class PeerExchange:
         self.group = group
         self.N = dist.get_world_size(group)
         self.r = dist.get_rank(group)
+        if self.N > 8:
+            raise ValueError("PeerExchange: at most 8 ranks")
+        if hidden % 8 != 0:
+            raise ValueError("PeerExchange: hidden must be a multiple of 8")
         self.rows, self.hidden, self.sub = rows, hidden, sub
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         N = self.N
@@ -114,12 +121,10 @@ class PeerExchange:
         self.pieces = {}
         for o, (a, b) in enumerate(self.block):
             self.pieces[o] = [(a + j * (b - a) // sub, a + (j + 1) * (b - a) // sub) for j in range(sub)]
-        self.max_block = max(b - a for a, b in self.block)
-        es = 2
-        self.recv_bytes = N * self.max_block * hidden * es     # per set: [sender][block row][hidden]
-        self.out_bytes = rows * hidden * es                   # per set
-        self.flag_bytes = 4096                                 # recv flags [N], out flags [N]
-        total = self.flag_bytes + 2 * (self.recv_bytes + self.out_bytes)
+        self.flag_bytes = 4096                         # ready flags [N], arrived flags [N]
+        self.part_bytes = (rows * hidden * 2 + 255) // 256 * 256
+        self.out_bytes = (rows * hidden * 2 + 255) // 256 * 256   # per set
+        total = self.flag_bytes + self.part_bytes + 2 * self.out_bytes
         base = C.c_void_p()
         abi.call("mllm_ipc_alloc", total, C.byref(base))
         self.base = base.value
@@ -136,29 +141,24 @@ class PeerExchange:
             hh = (C.c_ubyte * 64).from_buffer_copy(handles[s])
             abi.call("mllm_ipc_open_handle", hh, C.byref(p))
             self.peer.append(p.value)
-        self.partial = torch.empty((rows, hidden), dtype=torch.bfloat16, device=self.device)
-        # one send and one gather stream per peer, so transfers to different peers run on
-        # different copy engines at the same time
-        self.s_send = {p: torch.cuda.Stream(device=self.device) for p in range(self.N) if p != self.r}
-        self.s_gather = {p: torch.cuda.Stream(device=self.device) for p in range(self.N) if p != self.r}
+        self.partial = self._tensor(self._part(self.r, 0), rows)
+        self.s_sig = {o: torch.cuda.Stream(device=self.device) for o in range(N) if o != self.r}
         self.s_reduce = torch.cuda.Stream(device=self.device)
         self.calls = 0
         dist.barrier(group=group)
 
     # addresses inside rank s's shared allocation
-    def _recv_flag(self, s, sender):
+    def _ready_flag(self, s, sender):
         return self.peer[s] + 4 * sender
 
-    def _out_flag(self, s, sender):
+    def _arrived_flag(self, s, sender):
         return self.peer[s] + 4 * (self.N + sender)
 
-    def _recv(self, s, st, sender, row_in_block):
-        return (self.peer[s] + self.flag_bytes + st * (self.recv_bytes + self.out_bytes)
-                + ((sender * self.max_block + row_in_block) * self.hidden) * 2)
+    def _part(self, s, row):
+        return self.peer[s] + self.flag_bytes + row * self.hidden * 2
 
     def _out(self, s, st, row):
-        return self.peer[s] + self.flag_bytes + st * (self.recv_bytes + self.out_bytes) + self.recv_bytes + \
-            row * self.hidden * 2
+        return self.peer[s] + self.flag_bytes + self.part_bytes + st * self.out_bytes + row * self.hidden * 2
 
     def _tensor(self, ptr, rows):
         import torch
@@ -186,44 +186,38 @@ class PeerExchange:
         cur = torch.cuda.current_stream(self.device)
         h = lambda s: s.cuda_stream
         for j in range(sub):
+            flag = (base + j + 1) & 0xFFFFFFFF
             for k in range(1, N + 1):
                 o = (r + k) % N
                 a, b = self.pieces[o][j]
                 torch.matmul(attn[a:b], w_o.t(), out=self.partial[a:b])
                 ev = torch.cuda.Event()
                 ev.record(cur)
-                nbytes = (b - a) * H * 2
                 if o != r:
-                    ss = self.s_send[o]
+                    ss = self.s_sig[o]
                     ss.wait_event(ev)
-                    dst = self._recv(o, st, r, a - self.block[o][0])
-                    abi.call("mllm_copy_async", dst, self.partial[a:b].data_ptr(), nbytes, h(ss))
-                    abi.call("mllm_signal_u32", self._recv_flag(o, r), (base + j + 1) & 0xFFFFFFFF, h(ss))
+                    abi.call("mllm_signal_u32", self._ready_flag(o, r), flag, h(ss))
                     continue
-                # own piece: wait for the others' partials, sum, send the final rows everywhere
-                self.s_reduce.wait_event(ev)
-                srcs = (C.c_void_p * N)()
+                # own piece: once every rank's piece is ready, pull, sum and push to every rank
+                sr = self.s_reduce
+                sr.wait_event(ev)
                 for s in range(N):
-                    if s == r:
-                        srcs[s] = self.partial[a:b].data_ptr()
-                    else:
-                        abi.call("mllm_wait_u32", self._recv_flag(r, s), (base + j + 1) & 0xFFFFFFFF,
-                                 h(self.s_reduce))
-                        srcs[s] = self._recv(r, st, s, a - self.block[r][0])
-                abi.call("mllm_sum_bf16", self._out(r, st, a), srcs, N, (b - a) * H, h(self.s_reduce))
-                ev2 = torch.cuda.Event()
-                ev2.record(self.s_reduce)
-                for p, sg in self.s_gather.items():
-                    sg.wait_event(ev2)
-                    abi.call("mllm_copy_async", self._out(p, st, a), self._out(r, st, a), nbytes, h(sg))
-                    abi.call("mllm_signal_u32", self._out_flag(p, r), (base + j + 1) & 0xFFFFFFFF, h(sg))
-        # the output is complete once every other rank has delivered all its pieces
+                    if s != r:
+                        abi.call("mllm_wait_u32", self._ready_flag(r, s), flag, h(sr))
+                srcs = (C.c_void_p * N)(*[self._part(s, a) for s in range(N)])
+                dsts = (C.c_void_p * N)(*[self._out(p, st, a) for p in range(N)])
+                abi.call("mllm_sum_bf16", dsts, N, srcs, N, (b - a) * H, h(sr))
+                for p in range(N):
+                    if p != r:
+                        abi.call("mllm_signal_u32", self._arrived_flag(p, r), flag, h(sr))
+        # the output is complete once every owner has stored its rows here; that is also the
+        # point after which no rank reads this rank's partial any more
         cur.wait_stream(self.s_reduce)
         for s in range(N):
             if s != r:
-                abi.call("mllm_wait_u32", self._out_flag(r, s), (base + sub) & 0xFFFFFFFF, h(cur))
-        for st_ in list(self.s_send.values()) + list(self.s_gather.values()):
-            cur.wait_stream(st_)         # the next call's GEMMs overwrite `partial`
+                abi.call("mllm_wait_u32", self._arrived_flag(r, s), (base + sub) & 0xFFFFFFFF, h(cur))
+        for ss in self.s_sig.values():
+            cur.wait_stream(ss)
         return self._tensor(self._out(r, st, 0), self.rows)
 
     def close(self):

@@ -163,3 +163,68 @@ def test_peer_exchange_matches_nccl_allreduce():
         got1, _ = res[1][key]
         np.testing.assert_array_equal(got0, got1, err_msg=f"{key}: ranks disagree")
         np.testing.assert_array_equal(got0, want0, err_msg=f"{key}: differs from NCCL all-reduce")
+
+
+def _exchange_worker_n(rank, world, port, q):
+    """PeerExchange at `world` ranks: every rank holds the same result, equal to the fp32 sum of
+    the ranks' bf16 partials (in rank order) rounded once."""
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from mllm_b200 import abi, tp
+        torch.matmul(torch.ones(8, 8, device=dev), torch.ones(8, 8, device=dev))
+        torch.cuda.synchronize()
+        rows, hidden, k = 1000, 1024, 256
+        ex = tp.PeerExchange(rows, hidden, sub=2)
+        got = []
+        parts = []
+        for call in range(4):
+            g = torch.Generator(device=dev).manual_seed(1000 * call + rank)
+            attn = torch.randn(rows, k, device=dev, generator=g).bfloat16()
+            w_o = (0.05 * torch.randn(hidden, k, device=dev, generator=g)).bfloat16()
+            part = torch.empty(rows, hidden, device=dev, dtype=torch.bfloat16)
+            for o in range(world):
+                for a, b in ex.pieces[o]:
+                    torch.matmul(attn[a:b], w_o.t(), out=part[a:b])
+            y = ex(attn, w_o)
+            got.append(y.clone().cpu())
+            parts.append(part.cpu())
+        torch.cuda.synchronize()
+        assert abi.load().mllm_attn_device_status(None) == 0
+        ex.close()
+        q.put((rank, torch.stack(got).view(torch.int16).numpy(), torch.stack(parts).float().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 3, reason="needs 3+ GPUs")
+def test_peer_exchange_on_all_gpus():
+    import torch.multiprocessing as mp
+    world = min(torch.cuda.device_count(), 8)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_worker_n, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, got, part = q.get(timeout=300)
+        res[r] = (got, part)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(1, world):
+        np.testing.assert_array_equal(res[r][0], res[0][0], err_msg=f"rank {r} differs from rank 0")
+    acc = np.zeros_like(res[0][1])
+    for r in range(world):
+        acc = acc + res[r][1]          # fp32, rank order
+    want = torch.from_numpy(acc).bfloat16().view(torch.int16).numpy()
+    np.testing.assert_array_equal(res[0][0], want)
