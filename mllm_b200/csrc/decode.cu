@@ -515,11 +515,14 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 2)
 }
 
 // Merges the per-chunk partials of every (sequence, query head) whose cache spans more
-// than one chunk.  One CTA per (kv head, sequence).  The (m, l) pairs of all its chunks are
-// staged in shared memory with one parallel load; thread r < n_rep turns its head's pairs into
-// per-chunk weights exp2(m_c - M) and 1/L; then thread d sums the partial column d over the
-// chunks with independent loads.
+// than one chunk.  One CTA per (kv head, sequence); thread d owns column d of every head.
+// By the time this runs the partials have usually left L2 (the split kernel streamed the
+// whole cache through it after writing them), so every load of a CTA goes out in one round:
+// thread d first issues its column's loads for all heads and chunks, then the (m, l) pairs are
+// staged and turned into chunk weights exp2(m_c - M) and 1/L while those loads are in flight,
+// and only then are the columns summed, in chunk order.
 constexpr int kMaxChunks = 128;
+constexpr int kCombineBatch = 8;   // chunks per batch of loads in flight (all heads at once)
 
 template <int D>
 __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeArgs a) {
@@ -533,6 +536,17 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeArgs a) {
     const int nch_b = (L + a.chunk - 1) / a.chunk;
     if (nch_b <= 1) return;  // written directly by the split kernel
     const int64_t item0 = ((int64_t)b * a.Hkv + g) * a.nch;
+    const int d = threadIdx.x;
+    const int64_t step = (int64_t)a.n_rep * D;   // next chunk, same head
+    const float* col = a.part_o + (item0 * a.n_rep) * D + d;
+    // the first batch of this thread's column loads, all heads, before anything else
+    float v[kMaxGroup][kCombineBatch];
+    const int nb0 = nch_b < kCombineBatch ? nch_b : kCombineBatch;
+#pragma unroll
+    for (int r = 0; r < kMaxGroup; ++r)
+#pragma unroll
+        for (int c = 0; c < kCombineBatch; ++c)
+            v[r][c] = (d < D && r < a.n_rep && c < nb0) ? col[r * D + c * step] : 0.f;
     const int n = a.n_rep * nch_b;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int r = i / nch_b, c = i - r * nch_b;
@@ -555,16 +569,28 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeArgs a) {
         s_inv[r] = (Lt > 0.f) ? 1.f / Lt : 0.f;
     }
     __syncthreads();
-    const int d = threadIdx.x;
     if (d >= D) return;
-    for (int r = 0; r < a.n_rep; ++r) {
-        const float* col = a.part_o + ((item0 * a.n_rep) + r) * D + d;
-        const int64_t step = (int64_t)a.n_rep * D;   // next chunk, same head
-        float acc = 0.f;
-#pragma unroll 8
-        for (int c = 0; c < nch_b; ++c) acc += col[c * step] * s_m[r * nch_b + c];
-        a.out[((int64_t)b * a.H + (int64_t)g * a.n_rep + r) * D + d] = __float2bfloat16_rn(acc * s_inv[r]);
+    float acc[kMaxGroup];
+#pragma unroll
+    for (int r = 0; r < kMaxGroup; ++r) acc[r] = 0.f;
+    for (int c0 = 0; c0 < nch_b; c0 += kCombineBatch) {
+        if (c0 > 0) {   // the next batch (sequences of more than kCombineBatch chunks)
+#pragma unroll
+            for (int r = 0; r < kMaxGroup; ++r)
+#pragma unroll
+                for (int c = 0; c < kCombineBatch; ++c)
+                    v[r][c] = (r < a.n_rep && c0 + c < nch_b) ? col[r * D + (c0 + c) * step] : 0.f;
+        }
+#pragma unroll
+        for (int r = 0; r < kMaxGroup; ++r)
+#pragma unroll
+            for (int c = 0; c < kCombineBatch; ++c)
+                if (r < a.n_rep && c0 + c < nch_b) acc[r] += v[r][c] * s_m[r * nch_b + c0 + c];
     }
+#pragma unroll
+    for (int r = 0; r < kMaxGroup; ++r)
+        if (r < a.n_rep)
+            a.out[((int64_t)b * a.H + (int64_t)g * a.n_rep + r) * D + d] = __float2bfloat16_rn(acc[r] * s_inv[r]);
 }
 
 // Chunking of the cache rows into work items: aim for ~16 items per SM so the persistent
