@@ -237,7 +237,7 @@ def run_gpu(args, rank, world, device):
     q_rot = torch.empty(B, H, D, dtype=torch.bfloat16, device=device)
     out = torch.empty(B, H * D, dtype=torch.bfloat16, device=device)
     ws_bytes = lib.mllm_decode_attention_workspace_size(B, H, HKV, D, L)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)   # the header starts at zero
     csb, csh, cst = kbuf.stride()[:3]
     row = (H + 2 * HKV) * D
     scale = 1.0 / math.sqrt(D)
@@ -567,7 +567,7 @@ def run_gpu(args, rank, world, device):
         orr = torch.empty(RAG_B, Hr * D, dtype=torch.bfloat16, device=device)
         lens_r = torch.from_numpy(lens_np.astype("int32")).to(device)
         ws_r_bytes = lib.mllm_decode_attention_workspace_size(RAG_B, Hr, Hkvr, D, Lmax)
-        ws_r = torch.empty(ws_r_bytes, dtype=torch.uint8, device=device)
+        ws_r = torch.zeros(ws_r_bytes, dtype=torch.uint8, device=device)
         rsb, rsh, rst = kr.stride()[:3]
 
         def decode_r():

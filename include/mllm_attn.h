@@ -150,7 +150,10 @@ MLLM_API int mllm_prefill_attention_bf16(const void* q, const void* k_cache, con
  *            max_kv_len rows (the batch-uniform cache of the reference runners).
  *   out:    bf16 [batch, num_heads*head_dim]
  *   workspace: device scratch of at least mllm_decode_attention_workspace_size() bytes,
- *            256-byte aligned; contents need not be initialised. */
+ *            256-byte aligned.  Its first 256 bytes hold the counter from which the persistent
+ *            CTAs take work items: they must be zero before the first call, and every call
+ *            leaves them zero, so one workspace serves any number of calls of any shape in one
+ *            stream (not concurrent calls).  The rest needs no initialisation. */
 MLLM_API size_t mllm_decode_attention_workspace_size(int batch, int num_heads, int num_kv_heads, int head_dim,
                                             int max_kv_len);
 

@@ -4,8 +4,11 @@
 // cache, repeat_interleave-ing it n_rep times and upcasting it to fp32, each KV-head row is
 // streamed from HBM exactly once and shared by its whole GQA group of query heads.
 //
-// Structure (per CTA, persistent over a static, strided list of work items):
-//   work item  = (sequence b, kv head g, chunk c of CH cache rows)
+// Structure (per CTA, persistent over a list of work items):
+//   work item  = (sequence b, kv head g, chunk c of CH cache rows); a CTA's first item is its
+//                block index, later ones come from a counter in the workspace (the CTAs that
+//                run fastest take more items, so they all finish together); the producer lane
+//                claims them one item ahead and publishes the CTA's sequence in shared memory
 //   warp 4     = producer: one elected lane issues TMA tile loads (64 rows x head_dim of K
 //                and of V, 128-byte swizzled) into an NSTAGE ring guarded by mbarriers
 //   warps 0-3  = consumers: each owns 16 of the 64 rows of every tile.
@@ -53,6 +56,7 @@ constexpr int kThreads = (kConsumerWarps + 1) * 32;   // consumers + TMA produce
 constexpr int kThreadsFused = kThreads + 32;          // + the fused step's epilogue warp
 constexpr int kMaxGroup = 8;      // query heads per kv head handled as MMA rows
 constexpr int kBoxBytes = kTile * 128;  // one 64-row x 64-column bf16 TMA box
+constexpr int kRing = 8;          // entries of a CTA's published item sequence
 
 template <int D>
 struct DecodeCfg {
@@ -76,6 +80,8 @@ struct DecodeArgs {
     __nv_bfloat16* out;         // [B, H*D]
     float* part_o;              // [B*Hkv*nch, n_rep, D]
     float* part_ml;             // [B*Hkv*nch, n_rep, 2]
+    unsigned* item_counter;     // items handed out past the first grid-size ones (zero between calls),
+                                // or NULL: the static strided schedule
     int B, H, Hkv, n_rep, max_len, chunk, nch, items;
     float scale_log2;
     KvLayout lay;                // contiguous, or the paged cache's block table
@@ -121,8 +127,17 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 2)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // The CTA's item sequence: entry k at slot k % kRing, valid once s_pub[slot] == k.  The
+    // producer lane writes it; the consumers report the entry they work on in s_cons.
+    __shared__ int s_items[kRing];
+    __shared__ int s_pub[kRing];
+    __shared__ int s_cons;
 
     if (threadIdx.x == 0) {
+        for (int i = 0; i < kRing; ++i) s_pub[i] = -1;
+        s_items[0] = blockIdx.x;
+        s_pub[0] = 0;
+        s_cons = 0;
         for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
@@ -154,6 +169,19 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 2)
         // the fused step's new row L-1 is not loaded: its item takes it from shared memory
         t1 = min(t0 + a.chunk, kFused ? L - 1 : L);
     };
+    // Entry k of the CTA's item sequence, once the producer lane has published it (bounded).
+    auto item_at = [&](int k) -> int {
+        const int slot = k & (kRing - 1);
+        for (uint32_t i = 0; i < kSpinLimit; ++i) {
+            if (*reinterpret_cast<volatile int*>(&s_pub[slot]) == k) {
+                __threadfence_block();
+                return *reinterpret_cast<volatile int*>(&s_items[slot]);
+            }
+            if (i > 64) __nanosleep(64);
+        }
+        record_error(kErrTimeout);
+        return INT_MAX;   // ends the caller's loop
+    };
 
     if (kFused && warp == kConsumerWarps + 1) {
         // --------------------- the new token's epilogue (whole warp) ---------------------
@@ -166,7 +194,9 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 2)
             gk[i] = norm ? __bfloat162float(a.k_gamma[lane + 32 * i]) : 0.f;
         }
         int n_act = 0;   // active items so far (items with tiles or with the new row)
-        for (int item = blockIdx.x; item < a.items; item += gridDim.x) {
+        for (int k = 0;; ++k) {
+            const int item = item_at(k);
+            if (item >= a.items) break;
             int b, g, c, t0, t1, L;
             item_range(item, b, g, c, t0, t1, L);
             const int nch_b = (L + a.chunk - 1) / a.chunk;
@@ -256,7 +286,21 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 2)
             int stage = 0;
             uint32_t phase = 0;
             bool alive = true;
-            for (int item = blockIdx.x; item < a.items && alive; item += gridDim.x) {
+            for (int k = 0; alive; ++k) {
+                const int item = *reinterpret_cast<volatile int*>(&s_items[k & (kRing - 1)]);   // published by this lane
+                if (item >= a.items) break;
+                // claim and publish entry k + 1 now, one item ahead of the other warps; never
+                // more than kRing - 2 entries ahead of the consumers, whose entry's slot is live
+                for (uint32_t i = 0; k + 1 - *reinterpret_cast<volatile int*>(&s_cons) > kRing - 2; ++i) {
+                    if (i >= kSpinLimit) { record_error(kErrTimeout); alive = false; break; }
+                    if (i > 64) __nanosleep(64);
+                }
+                if (!alive) break;
+                const int nxt = a.item_counter ? (int)gridDim.x + (int)atomicAdd(a.item_counter, 1u)
+                                               : item + (int)gridDim.x;
+                s_items[(k + 1) & (kRing - 1)] = nxt < a.items ? nxt : a.items;
+                __threadfence_block();
+                *reinterpret_cast<volatile int*>(&s_pub[(k + 1) & (kRing - 1)]) = k + 1;
                 int b, g, c, t0, t1, L;
                 item_range(item, b, g, c, t0, t1, L);
                 for (int t = t0; t < t1; t += kTile) {
@@ -288,7 +332,10 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 2)
     bool alive = true;
     int n_act = 0;               // fused: active items so far (matches the producer's count)
 
-    for (int item = blockIdx.x; item < a.items && alive; item += gridDim.x) {
+    for (int k = 0; alive; ++k) {
+        if (threadIdx.x == 0) *reinterpret_cast<volatile int*>(&s_cons) = k;
+        const int item = item_at(k);
+        if (item >= a.items) break;
         int b, g, c, t0, t1, L;
         item_range(item, b, g, c, t0, t1, L);
         const int nch_b = (L + a.chunk - 1) / a.chunk;
@@ -531,6 +578,8 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeArgs a) {
     __shared__ float s_inv[kMaxGroup];
     pdl_wait();      // partials come from the split kernel launched just before
     const int g = blockIdx.x, b = blockIdx.y;
+    // the split grid has finished handing out items: ready the counter for the next call
+    if (g == 0 && b == 0 && threadIdx.x == 0 && a.item_counter != nullptr) *a.item_counter = 0u;
     int L = a.kv_lens ? a.kv_lens[b] : a.max_len;
     L = L < 0 ? 0 : (L > a.max_len ? a.max_len : L);
     const int nch_b = (L + a.chunk - 1) / a.chunk;
@@ -625,10 +674,13 @@ void plan_chunks(int B, int Hkv, int max_len, int grid, int& chunk, int& nch) {
     nch = (max_len + chunk - 1) / chunk;
 }
 
+// The workspace starts with a 256-byte header holding the item counter, then the partials.
+constexpr size_t kHeaderBytes = 256;
+
 size_t workspace_bytes_for(int B, int H, int Hkv, int D, int max_len) {
     const int n_rep = H / Hkv;
     const size_t parts = (size_t)B * Hkv * max_chunks(max_len) * n_rep;
-    const size_t bytes = parts * D * 4 + parts * 2 * 4;
+    const size_t bytes = kHeaderBytes + parts * D * 4 + parts * 2 * 4;
     return (bytes + 255) & ~size_t(255);
 }
 
@@ -640,7 +692,10 @@ int launch_decode_d(DecodeArgs& a, const CUtensorMap& tmK, const CUtensorMap& tm
                     cudaStream_t s) {
     plan_chunks(a.B, a.Hkv, a.max_len, 2 * num_sms, a.chunk, a.nch);
     const size_t parts = (size_t)a.B * a.Hkv * a.nch * a.n_rep;
-    a.part_o = reinterpret_cast<float*>(workspace);
+    // items past the first grid-size ones come from the counter when the combine kernel runs
+    // after this launch (it resets the counter); a single-chunk call keeps the static schedule
+    a.item_counter = a.nch > 1 ? reinterpret_cast<unsigned*>(workspace) : nullptr;
+    a.part_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kHeaderBytes);
     a.part_ml = a.part_o + parts * D;
     a.items = a.B * a.Hkv * a.nch;
     const int grid = std::min(a.items, 2 * num_sms);

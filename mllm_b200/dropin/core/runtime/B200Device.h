@@ -108,13 +108,14 @@ namespace mllm
             return true;
         }
 
-        // Grow-only scratch for the split-K decode partials (the C ABI never allocates).
+        // Grow-only, zero-filled scratch for the split-K decode partials (the C ABI never
+        // allocates); its 256-byte header starts at zero and every call leaves it zero.
         inline torch::Tensor DecodeWorkspace(size_t bytes, const torch::Device& dev)
         {
             thread_local torch::Tensor ws;
             if (!ws.defined() || (size_t)ws.numel() < bytes || ws.device() != dev)
             {
-                ws = torch::empty({(int64_t)std::max<size_t>(bytes, 256)},
+                ws = torch::zeros({(int64_t)std::max<size_t>(bytes, 256)},
                                   torch::TensorOptions().dtype(torch::kUInt8).device(dev));
             }
             return ws;

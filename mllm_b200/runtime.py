@@ -297,14 +297,15 @@ class PagedSlot(PagedKVCache):
 
 
 class DecodeWorkspace:
-    """Grow-only device scratch for the split-K decode partials (the C ABI never allocates)."""
+    """Grow-only, zero-filled device scratch for the split-K decode partials (the C ABI never
+    allocates).  Its 256-byte header must start at zero; every call leaves it zero."""
 
     def __init__(self):
         self.buf = None
 
     def get(self, nbytes: int, device) -> torch.Tensor:
         if self.buf is None or self.buf.numel() < nbytes or self.buf.device != torch.device(device):
-            self.buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+            self.buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
         return self.buf
 
 

@@ -202,6 +202,47 @@ def test_decode_vs_oracle(rt, B, H, Hkv, D, lens):
     np.testing.assert_allclose(got, ref, rtol=RTOL, atol=ATOL)
 
 
+def test_decode_large_ragged_batch(rt):
+    """A ragged batch large enough that every persistent CTA takes several items from the
+    workspace counter, with many empty chunks (short sequences in a long-plan batch): every
+    sequence against a torch fp32 reference, paged bit-identical to contiguous, repeated calls
+    bit-identical (items may land on other CTAs; each is computed and merged the same way)."""
+    import random
+    B, H, Hkv, D = 64, 40, 8, 128
+    rng = np.random.default_rng(2024)
+    lens = rng.integers(1, 6000, B).tolist()
+    lens[0], lens[1], lens[2] = 6144, 1, 4096        # the longest plans the chunks; tile and chunk edges
+    Lmax = max(lens)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    cont = rt.KVCache(B, Hkv, D, Lmax, zero=False)
+    cont.key_buf.copy_(torch.randn(cont.key_buf.shape, device="cuda", generator=g))
+    cont.value_buf.copy_(torch.randn(cont.value_buf.shape, device="cuda", generator=g))
+    cont.set_lengths(lens)
+    q = torch.randn(B, H, D, device="cuda", generator=g).bfloat16()
+    out = rt.decode_attention(q, cont, Hkv).view(B, H, D).float()
+    n_rep = H // Hkv
+    for b, L in enumerate(lens):
+        k = cont.key_buf[b, :, :L].float().repeat_interleave(n_rep, 0)      # [H, L, D]
+        v = cont.value_buf[b, :, :L].float().repeat_interleave(n_rep, 0)
+        p = torch.softmax((q[b].float().unsqueeze(1) @ k.transpose(1, 2)) / math.sqrt(D), -1)
+        ref = (p @ v).squeeze(1)
+        torch.testing.assert_close(out[b], ref, rtol=2e-2, atol=2e-2, msg=f"sequence {b} (L={L})")
+    bits = lambda t: t.contiguous().view(torch.int16)
+    again = rt.decode_attention(q, cont, Hkv).view(B, H, D)
+    assert torch.equal(bits(again), bits(out.bfloat16()))
+    block = 256
+    paged = rt.PagedKVCache(num_blocks=sum(-(-L // block) for L in lens) + 2, num_kv_heads=Hkv, head_dim=D,
+                            block_size=block, max_seqs=B)
+    random.Random(5).shuffle(paged._free)
+    paged.set_lengths(lens)
+    for b, L in enumerate(lens):
+        for i, blk in enumerate(paged.blocks_of(b)):
+            r0, r1 = i * block, min(L, (i + 1) * block)
+            paged.k_pool[blk, :, : r1 - r0] = cont.key_buf[b, :, r0:r1]
+            paged.v_pool[blk, :, : r1 - r0] = cont.value_buf[b, :, r0:r1]
+    assert torch.equal(bits(rt.decode_attention(q, paged, Hkv).view(B, H, D)), bits(again))
+
+
 # ---------------------------------------------------------------------------------------
 # Fused decode step (epilogue of the new token + decode in one launch)
 # ---------------------------------------------------------------------------------------

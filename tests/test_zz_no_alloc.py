@@ -41,7 +41,7 @@ def _with_workspace(lib, q, k, v, kv_lens, H, Hkv, D, L):
     B = q.shape[0]
     out = torch.empty(B, H * D, dtype=torch.bfloat16, device="cuda")
     nbytes = lib.mllm_decode_attention_workspace_size(B, H, Hkv, D, L)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
     st = lib.mllm_decode_attention_bf16(q.data_ptr(), k.data_ptr(), v.data_ptr(), *k.stride()[:3],
                                         kv_lens.data_ptr(), B, H, Hkv, D, L, 1.0 / math.sqrt(D), out.data_ptr(),
                                         ws.data_ptr(), nbytes, None)
