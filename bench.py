@@ -31,6 +31,7 @@ reference sources) on this host's cores on bounded samples of the same decode wo
 from __future__ import annotations
 
 import argparse
+import ctypes as C
 import json
 import math
 import os
@@ -268,7 +269,12 @@ def run_gpu(args, rank, world, device):
             dst.data_ptr(), ws.data_ptr(), ws_bytes, sh)
         assert st == 0, lib.mllm_attn_last_error()
 
-    launches_per_step = 2  # split + combine (the cache is split into several chunks here)
+    # our kernel launches per fused step: the split kernel, plus the combine when the plan
+    # splits each sequence's cache into several chunks
+    plan_rows, plan_chunks, plan_launches = C.c_int(), C.c_int(), C.c_int()
+    assert lib.mllm_decode_attention_plan(B, H, HKV, D, L, C.byref(plan_rows), C.byref(plan_chunks),
+                                          C.byref(plan_launches)) == 0, lib.mllm_attn_last_error()
+    launches_per_step = plan_launches.value
 
     def barrier():
         if world > 1:
@@ -634,7 +640,7 @@ def run_gpu(args, rank, world, device):
     return {"elapsed_ms": elapsed_ms, "dec_ms": dec_ms, "unfused_ms": unfused_ms, "e2e_ms": e2e_ms, "pre": pre,
             "proj": proj,
             "rag": rag, "clocks": clocks,
-            "launches_per_step": launches_per_step,
+            "launches_per_step": launches_per_step, "plan": (plan_rows.value, plan_chunks.value),
             "h2d": qkv.numel() * 2, "d2h": out.numel() * 2}
 
 
@@ -893,6 +899,8 @@ def main():
                     "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"],
                     "ms_per_step": e2e_ms},
             "gpu_launches": res["launches_per_step"] * args.steps,
+            "decode_plan": {"chunk_rows": res["plan"][0], "chunks_per_sequence": res["plan"][1],
+                            "launches_per_step": res["launches_per_step"]},
             "unfused": {"ms_per_step": res["unfused_ms"], "decode_only_ms": res["dec_ms"],
                         "value": kv_bytes * n / (res["unfused_ms"] * 1e-3) / 1e9, "unit": "GB/s",
                         "note": "the same step as mllm_qkv_epilogue_bf16 + mllm_decode_attention_bf16"},

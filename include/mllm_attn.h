@@ -157,6 +157,13 @@ MLLM_API int mllm_prefill_attention_bf16(const void* q, const void* k_cache, con
 MLLM_API size_t mllm_decode_attention_workspace_size(int batch, int num_heads, int num_kv_heads, int head_dim,
                                             int max_kv_len);
 
+/* How a decode call of this shape on the current device is split: rows per chunk, chunks per
+ * (sequence, kv head) and kernel launches per call (1: one chunk each, no combine; 2: the split
+ * kernel and the combine).  Any output pointer may be NULL.  Applies to every decode entry point
+ * (plain, paged, fused step, no-alloc). */
+MLLM_API int mllm_decode_attention_plan(int batch, int num_heads, int num_kv_heads, int head_dim, int max_kv_len,
+                                        int* chunk_rows, int* chunks, int* launches);
+
 MLLM_API int mllm_decode_attention_bf16(const void* q, const void* k_cache, const void* v_cache,
                                int64_t cache_sb, int64_t cache_sh, int64_t cache_st,
                                const int32_t* kv_lens, int batch, int num_heads, int num_kv_heads,

@@ -56,6 +56,8 @@ SIGNATURES = {
                                     _p, _p, _d, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i64, _p]),
     "mllm_prefill_attention_bf16": (_i, [_p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _i, _f, _p, _p]),
     "mllm_decode_attention_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
+    "mllm_decode_attention_plan": (_i, [_i, _i, _i, _i, _i, C.POINTER(C.c_int), C.POINTER(C.c_int),
+                                        C.POINTER(C.c_int)]),
     "mllm_decode_attention_bf16": (_i, [_p, _p, _p, _i64, _i64, _i64, _p, _i, _i, _i, _i, _i, _f, _p,
                                         _p, _sz, _p]),
     "mllm_decode_attention_noalloc_bf16": (_i, [_p, _p, _p, _i64, _i64, _i64, _p, _i, _i, _i, _i, _i, _f,

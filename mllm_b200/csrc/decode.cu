@@ -642,16 +642,19 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeArgs a) {
             a.out[((int64_t)b * a.H + (int64_t)g * a.n_rep + r) * D + d] = __float2bfloat16_rn(acc[r] * s_inv[r]);
 }
 
-// Chunking of the cache rows into work items: aim for ~16 items per SM so the persistent
-// grid stays balanced, with chunks of at least 256 rows (amortises the per-item merge).
+// Chunking of the cache rows into work items, with chunks of at least 256 rows (amortises the
+// per-item merge).
 constexpr int kMinChunk = 256;
+constexpr double kCombineTiles = 4.0;   // the combine launch after a split grid, in tile-times
 
 int max_chunks(int max_len) { return std::min(kMaxChunks, std::max(1, (max_len + kMinChunk - 1) / kMinChunk)); }
 
-// Picks the chunk count per sequence for the static, strided item list of a grid of
-// `grid` persistent CTAs: the slowest CTA processes ceil(items / grid) items of
-// ceil(tiles / nch) tiles each, plus a merge cost of about half a tile per item.  Equal-sized
-// chunks that divide the work evenly over the CTAs win.
+// Picks the chunk count per sequence for a grid of `grid` persistent CTAs, in units of one
+// CTA's time per 64-row tile.  One chunk per (sequence, kv head): every CTA takes at most
+// ceil(items / grid) items under the static schedule, no partials, no combine.  Several: the
+// CTAs take items from the counter, so the work (tiles plus about half a tile of merge per item)
+// spreads evenly over the grid, and the step ends about one item after the average CTA, plus
+// the combine launch (about four tile-times, measured).
 void plan_chunks(int B, int Hkv, int max_len, int grid, int& chunk, int& nch) {
     const int64_t pairs = (int64_t)B * Hkv;
     const int64_t tiles = (max_len + kTile - 1) / kTile;
@@ -662,8 +665,9 @@ void plan_chunks(int B, int Hkv, int max_len, int grid, int& chunk, int& nch) {
         const int64_t chunk_tiles = (tiles + n - 1) / n;
         const int64_t n_eff = (tiles + chunk_tiles - 1) / chunk_tiles;   // chunks actually used
         const int64_t items = pairs * n_eff;
-        const int64_t per_cta = (items + grid - 1) / grid;
-        const double cost = (double)per_cta * ((double)chunk_tiles + 0.5);
+        const double cost = n_eff == 1
+            ? (double)((items + grid - 1) / grid) * ((double)chunk_tiles + 0.5)
+            : (double)items * ((double)chunk_tiles + 0.5) / grid + (double)chunk_tiles + kCombineTiles;
         if (cost < best - 1e-9) {
             best = cost;
             best_n = (int)n_eff;
@@ -736,6 +740,21 @@ extern "C" size_t mllm_decode_attention_workspace_size(int batch, int num_heads,
         head_dim <= 0)
         return 0;
     return workspace_bytes_for(batch, num_heads, num_kv_heads, head_dim, max_kv_len);
+}
+
+extern "C" int mllm_decode_attention_plan(int batch, int num_heads, int num_kv_heads, int head_dim, int max_kv_len,
+                                          int* chunk_rows, int* chunks, int* launches) {
+    if (batch <= 0 || num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads || max_kv_len <= 0 ||
+        (head_dim != 64 && head_dim != 128))
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention_plan: bad sizes");
+    int num_sms = 0;
+    if (int st = require_sm100(&num_sms)) return st;
+    int chunk = 0, nch = 0;
+    plan_chunks(batch, num_kv_heads, max_kv_len, 2 * num_sms, chunk, nch);
+    if (chunk_rows) *chunk_rows = chunk;
+    if (chunks) *chunks = nch;
+    if (launches) *launches = nch > 1 ? 2 : 1;
+    return ok();
 }
 
 extern "C" int mllm_decode_attention_bf16(const void* q, const void* k_cache, const void* v_cache,

@@ -84,6 +84,13 @@ def test_linear_argument_validation(lib):
     assert lib.mllm_linear_workspace_size(300, 3, nf, 4096) == 0       # invalid -> 0
 
 
+def test_decode_plan_argument_validation(lib):
+    r, c, n = C.c_int(), C.c_int(), C.c_int()
+    assert lib.mllm_decode_attention_plan(0, 32, 8, 128, 4096, C.byref(r), C.byref(c), C.byref(n)) == 1
+    assert lib.mllm_decode_attention_plan(32, 30, 8, 128, 4096, None, None, None) == 1
+    assert lib.mllm_decode_attention_plan(32, 32, 8, 96, 4096, None, None, None) == 1
+
+
 def test_workspace_size(lib):
     ws = lib.mllm_decode_attention_workspace_size(32, 32, 8, 128, 4096)
     assert ws > 0 and ws % 256 == 0

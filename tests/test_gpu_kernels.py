@@ -202,6 +202,24 @@ def test_decode_vs_oracle(rt, B, H, Hkv, D, lens):
     np.testing.assert_allclose(got, ref, rtol=RTOL, atol=ATOL)
 
 
+def test_decode_plan(rt):
+    """The chunk plan: one chunk per (sequence, kv head) when the pairs alone fill the grid for
+    long enough (Qwen3-8B batch 32, 4096 rows: no partials, no combine launch); several, taken
+    from the workspace counter, for few pairs or long ragged caches."""
+    import ctypes as C
+    lib = rt.abi.load()
+
+    def plan(*shape):
+        r, c, n = C.c_int(), C.c_int(), C.c_int()
+        assert lib.mllm_decode_attention_plan(*shape, C.byref(r), C.byref(c), C.byref(n)) == 0
+        return r.value, c.value, n.value
+    assert plan(32, 32, 8, 128, 4096) == (4096, 1, 1)
+    rows, chunks, launches = plan(8, 32, 8, 128, 2048)
+    assert chunks > 1 and launches == 2 and rows * chunks >= 2048 and rows % 64 == 0
+    rows, chunks, launches = plan(64, 40, 8, 128, 32069)
+    assert chunks > 1 and launches == 2 and rows * chunks >= 32069
+
+
 def test_decode_large_ragged_batch(rt):
     """A ragged batch large enough that every persistent CTA takes several items from the
     workspace counter, with many empty chunks (short sequences in a long-plan batch): every
