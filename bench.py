@@ -613,7 +613,6 @@ def run_gpu(args, rank, world, device):
         pk.k_pool.normal_(generator=gen)
         pk.v_pool.normal_(generator=gen)
         kvd = pk.descriptor()
-        import ctypes as C
 
         def decode_p():
             st = lib.mllm_decode_attention_paged_bf16(qr.data_ptr(), C.byref(kvd), pk.lengths.data_ptr(), RAG_B, Hr,
@@ -904,7 +903,9 @@ def main():
             "unfused": {"ms_per_step": res["unfused_ms"], "decode_only_ms": res["dec_ms"],
                         "value": kv_bytes * n / (res["unfused_ms"] * 1e-3) / 1e9, "unit": "GB/s",
                         "note": "the same step as mllm_qkv_epilogue_bf16 + mllm_decode_attention_bf16"},
-            "roofline": {"bound": "hbm", "kernel": "decode_split_kernel<128, fused> + decode_combine_kernel",
+            "roofline": {"bound": "hbm",
+                         "kernel": "decode_split_kernel<128, fused>" +
+                                   (" + decode_combine_kernel" if res["launches_per_step"] > 1 else ""),
                          "timing": "K back-to-back fused decode steps between two CUDA events",
                          "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                          "peak_source": peak_src, "traffic": profile_traffic("decode_qwen3_8b_b32_l4096")},
