@@ -8,7 +8,8 @@ against a bf16 KV cache of 4096 rows per sequence (hidden 4096, 32 q heads, 8 kv
 head_dim 128, per-head QK-RMSNorm eps 1e-6, RoPE theta 1e6).  One step = the QKV epilogue of
 the new token (QK-norm + RoPE + KV append) + split-K flash-decode over 4096 rows, i.e. the
 attention step between the q/k/v projections and o_proj, run as the fused decode step
-(mllm_decode_step_bf16: one split-kernel launch plus the chunk combine).  Metric = algorithmic
+(mllm_decode_step_bf16: one split-kernel launch, plus the chunk combine when the plan splits the
+cache; at this shape it does not).  Metric = algorithmic
 KV bytes read (2 * B * Hkv * L * D * 2 B = 536,870,912 B per step) / step time.  The cache
 (537 MB) is larger than L2 (126 MB), so every step streams it from HBM.  `unfused` reports the
 same step as two calls (mllm_qkv_epilogue_bf16, then mllm_decode_attention_bf16).
