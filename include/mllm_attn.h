@@ -184,8 +184,10 @@ MLLM_API int mllm_decode_attention_bf16(const void* q, const void* k_cache, cons
  *   head_dim 128 -- needs about 8.1 MiB).
  *   The first call on each device looks up the array's device address (cudaGetSymbolAddress);
  *   make that first call before any CUDA stream capture begins.
- *   All calls on a device share the array, which keeps the previous call's partials (every
- *   value read within a call is written earlier in that call, so nothing is cleared).  Calls
+ *   All calls on a device share the array, which keeps the previous call's contents.  Its
+ *   first 256 bytes are the work-item counter of the decode workspace: zero from the start
+ *   (static storage) and set back to zero by every call that uses it; the partials after it
+ *   are always written earlier in a call than they are read, so nothing needs clearing.  Calls
  *   that overlap on the GPU -- concurrent streams, or several host threads -- race on it:
  *   serialise them. */
 MLLM_API int mllm_decode_attention_noalloc_bf16(const void* q, const void* k_cache, const void* v_cache,

@@ -942,8 +942,9 @@ extern "C" int mllm_decode_attention_noalloc_bf16(const void* q, const void* k_c
                                64, kTile))
         return st;
 
-    // Every partial the combine step reads is written earlier in the same call, so the scratch
-    // needs no clearing between calls.
+    // The scratch begins with the work-item counter: zero from the start (static storage) and
+    // reset by the combine kernel of every call that takes items from it.  Every partial the
+    // combine reads is written earlier in the same call.  So nothing needs clearing between calls.
     DecodeArgs a = {};
     a.q = (const __nv_bfloat16*)q;
     a.kv_lens = kv_lens;
