@@ -221,14 +221,19 @@ class PeerExchange:
         return self._tensor(self._out(r, st, 0), self.rows)
 
     def close(self):
+        """Collective: every rank calls it.  Each rank unmaps the other ranks' buffers, and frees
+        its own only after all ranks have unmapped it (an exported allocation must outlive every
+        mapping of it)."""
         from . import abi
         if getattr(self, "base", None) is None:
             return
         import torch
+        import torch.distributed as dist
         torch.cuda.synchronize(self.device)
         for s, p in enumerate(self.peer):
             if s != self.r:
                 abi.call("mllm_ipc_close_handle", p)
+        dist.barrier(group=self.group)
         abi.call("mllm_ipc_free", self.base)
         self.base = None
 
