@@ -77,6 +77,46 @@ struct LinearArgs {
     float* partial;                    // [tiles][splits][tokens][128]
 };
 
+// The last CTA of a tile sums its split partials: out = ((p0 + p1) + p2) + ... in fp32, one
+// rounding.  Lane l owns rows 4l..4l+3 (one float4 per partial); warp w takes tokens w, w+4, ...
+// in batches of BATCH tokens whose loads (BATCH x MS float4 per thread) all go out before any
+// add, so a batch costs one round trip to L2.
+template <int BATCH, int MS>
+__device__ __forceinline__ void reduce_partials(const float* base, __nv_bfloat16* orow, int64_t ostride, int T,
+                                                int splits, int warp) {
+    for (int t0 = warp; t0 < T; t0 += 4 * BATCH) {
+        float4 v[BATCH][MS];
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b) {
+            const int t = t0 + 4 * b;
+#pragma unroll
+            for (int sp = 0; sp < MS; ++sp)
+                if (t < T && sp < splits)
+                    v[b][sp] = __ldcg(reinterpret_cast<const float4*>(base + ((size_t)sp * T + t) * kTileRows));
+        }
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b) {
+            const int t = t0 + 4 * b;
+            if (t >= T) break;
+            float4 acc = v[b][0];
+#pragma unroll
+            for (int sp = 1; sp < MS; ++sp)
+                if (sp < splits) {
+                    acc.x = __fadd_rn(acc.x, v[b][sp].x);
+                    acc.y = __fadd_rn(acc.y, v[b][sp].y);
+                    acc.z = __fadd_rn(acc.z, v[b][sp].z);
+                    acc.w = __fadd_rn(acc.w, v[b][sp].w);
+                }
+            __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+            __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+            uint2 pk;
+            pk.x = *reinterpret_cast<uint32_t*>(&lo);
+            pk.y = *reinterpret_cast<uint32_t*>(&hi);
+            *reinterpret_cast<uint2*>(orow + (int64_t)t * ostride) = pk;
+        }
+    }
+}
+
 template <int NT>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_kernel(const __grid_constant__ LinearMaps maps, const LinearArgs a) {
@@ -211,41 +251,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[tile], 1u) == (unsigned)(splits - 1);
         __syncthreads();
         if (s_last) {
-            // the last CTA of the tile: out = ((p0 + p1) + p2) + ... in fp32, one rounding.
-            // Lane l owns rows 4l..4l+3 (one float4 per partial), warp w tokens w, w+4, ...
+            // the last CTA of the tile adds the partials (reduce_partials)
             __threadfence();
             const float* base = a.partial + (size_t)tile * splits * T * kTileRows + 4 * lane;
-            for (int t0 = warp; t0 < T; t0 += 4 * kRedBatch) {
-                float4 v[kRedBatch][kMaxSplits];
-#pragma unroll
-                for (int b = 0; b < kRedBatch; ++b) {
-                    const int t = t0 + 4 * b;
-#pragma unroll
-                    for (int sp = 0; sp < kMaxSplits; ++sp)
-                        if (t < T && sp < splits)
-                            v[b][sp] = __ldcg(reinterpret_cast<const float4*>(base + ((size_t)sp * T + t) * kTileRows));
-                }
-#pragma unroll
-                for (int b = 0; b < kRedBatch; ++b) {
-                    const int t = t0 + 4 * b;
-                    if (t >= T) break;
-                    float4 acc = v[b][0];
-#pragma unroll
-                    for (int sp = 1; sp < kMaxSplits; ++sp)
-                        if (sp < splits) {
-                            acc.x = __fadd_rn(acc.x, v[b][sp].x);
-                            acc.y = __fadd_rn(acc.y, v[b][sp].y);
-                            acc.z = __fadd_rn(acc.z, v[b][sp].z);
-                            acc.w = __fadd_rn(acc.w, v[b][sp].w);
-                        }
-                    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
-                    __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
-                    uint2 pk;
-                    pk.x = *reinterpret_cast<uint32_t*>(&lo);
-                    pk.y = *reinterpret_cast<uint32_t*>(&hi);
-                    *reinterpret_cast<uint2*>(outp + (int64_t)t * ostride + 4 * lane) = pk;
-                }
-            }
+            __nv_bfloat16* orow = outp + 4 * lane;
+            // the same registers hold 8 tokens' partials when a tile has at most 4 splits (one
+            // round of loads for 32 tokens), else 4 tokens' of up to 8 splits
+            if (splits <= kMaxSplits / 2)
+                reduce_partials<2 * kRedBatch, kMaxSplits / 2>(base, orow, ostride, T, splits, warp);
+            else
+                reduce_partials<kRedBatch, kMaxSplits>(base, orow, ostride, T, splits, warp);
             if (threadIdx.x == 0) a.counters[tile] = 0u;   // ready for the next call in the stream
         }
     }
