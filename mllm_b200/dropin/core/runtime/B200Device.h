@@ -120,5 +120,19 @@ namespace mllm
             }
             return ws;
         }
+
+        // Grow-only scratch for the device sampler (token counts, sort buffers). Kept apart from
+        // the decode workspace so that nothing the sampler leaves behind can reach the decode
+        // work-item counter.
+        inline torch::Tensor SamplerWorkspace(size_t bytes, const torch::Device& dev)
+        {
+            thread_local torch::Tensor ws;
+            if (!ws.defined() || (size_t)ws.numel() < bytes || ws.device() != dev)
+            {
+                ws = torch::zeros({(int64_t)std::max<size_t>(bytes, 256)},
+                                  torch::TensorOptions().dtype(torch::kUInt8).device(dev));
+            }
+            return ws;
+        }
     }
 }

@@ -74,7 +74,7 @@ namespace mllm
             const uint64_t seed = (uint64_t)torch::randint(INT64_MAX, {1}, torch::kInt64).item<int64_t>();
             auto out = torch::empty({1}, torch::TensorOptions().dtype(torch::kInt64).device(dev));
             const size_t bytes = mllm_sample_workspace_size(1, (int)V);
-            auto ws = b200::DecodeWorkspace(bytes, dev);
+            auto ws = b200::SamplerWorkspace(bytes, dev);
             b200::Check(mllm_sample(logits.data_ptr(), logits.scalar_type() == torch::kBFloat16, V, 1, (int)V,
                                     prev.defined() ? prev.data_ptr<int64_t>() : nullptr, 0,
                                     counts.defined() ? counts.data_ptr<int32_t>() : nullptr, temperature, top_k,
