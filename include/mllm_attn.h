@@ -10,6 +10,8 @@
  *   mllm_decode_attention_bf16  split-K flash-decode over the cache (HBM-bound)
  *   mllm_decode_step_bf16       the epilogue of one new token per sequence fused into decode
  *   mllm_*_paged_bf16           the same four over a paged KV cache (block tables)
+ *   mllm_*_varlen_*             epilogue and prefill over packed sequences of different
+ *                               lengths (several prompts in one launch each)
  *   mllm_sample                 Sampler::Sample on the device (penalty, greedy / top-k / top-p)
  *
  * plus the RoPE table builder and RoPE apply that back the `mllm::RoPE` facade.
@@ -290,6 +292,69 @@ MLLM_API int mllm_decode_step_paged_bf16(const void* q, int64_t q_sb, int64_t q_
                                          int num_heads, int num_kv_heads, int head_dim, int max_kv_len,
                                          float softmax_scale, void* out, void* workspace, size_t workspace_bytes,
                                          mllm_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------
+ * Packed sequences of different lengths (variable-length prefill).  Several prompts, or
+ * prompt chunks, go through the epilogue and the attention in one launch each, instead of one
+ * call per sequence: the runners' Forward takes one [B, S] batch, so the reference prefills
+ * prompts of different lengths one Generate call at a time (QwenRunner.cpp:420-545).
+ * Sequence b owns the packed token rows cu_seqlens[b] .. cu_seqlens[b+1]-1 (int32 device
+ * [batch + 1], non-decreasing, cu_seqlens[0] = 0, cu_seqlens[batch] = total tokens); empty
+ * sequences are allowed.  Cache sequence b of a contiguous cache, or block-table row b of a
+ * paged one, receives sequence b's rows.
+ *
+ * Epilogue (mllm_qkv_epilogue_bf16 / _paged_bf16 for packed tokens):
+ *   q/k/v: token t's head h at q + t*q_st + h*q_sh (likewise k, v); bf16, head_dim contiguous.
+ *   positions: int64 device [total_tokens], each token's RoPE position (required).
+ *   cache_start: int32 device [batch] (NULL: 0), the cache row of sequence b's first new token.
+ *   q_out: bf16 [num_heads, total_tokens, head_dim] -- the layout the varlen prefill reads.
+ *   A token outside the ranges cu_seqlens describes, or a row past the cache, records
+ *   MLLM_ERR_DEVICE_LENGTH and its K/V row is not written.
+ *
+ * Attention (mllm_prefill_attention_bf16 / _paged_bf16 for packed sequences):
+ *   q: bf16 [num_heads, total_q, head_dim] (the varlen epilogue's q_out).
+ *   cu_q_lens: as cu_seqlens above, over total_q rows.
+ *   kv_lens: int32 device [batch], the cache rows of sequence b after its new rows were
+ *       appended (kv_lens[b] >= its q_len); query row s of sequence b sits at position
+ *       kv_lens[b] - q_len + s and sees cache rows 0 .. that position.
+ *   max_q_len: the longest sequence's q_len, or more (it sizes the grid; a longer one is an
+ *       error).
+ *   out: bf16 [total_q, num_heads * head_dim].
+ *   Cache rows past kv_lens[b] that share a 128-row tile with the last visible row are read
+ *   and masked: they must hold finite values (a freshly allocated cache or block should be
+ *   zero-filled).  A sequence whose range, q_len or kv_len is inconsistent (or kv_len beyond
+ *   cache_capacity, or beyond max_blocks_per_seq * block_size) records MLLM_ERR_DEVICE_LENGTH
+ *   and its output rows are not written. */
+MLLM_API int mllm_qkv_epilogue_varlen_bf16(const void* q, int64_t q_st, int64_t q_sh, const void* k, int64_t k_st,
+                                           int64_t k_sh, const void* v, int64_t v_st, int64_t v_sh, int total_tokens,
+                                           int num_heads, int num_kv_heads, int head_dim, const int64_t* positions,
+                                           double rope_theta, const void* q_norm_weight, const void* k_norm_weight,
+                                           double rms_norm_eps, void* q_out, void* k_cache, void* v_cache,
+                                           int64_t cache_sb, int64_t cache_sh, int64_t cache_st,
+                                           int64_t cache_capacity, const int32_t* cu_seqlens, int batch,
+                                           const int32_t* cache_start, mllm_stream_t stream);
+
+MLLM_API int mllm_qkv_epilogue_varlen_paged_bf16(const void* q, int64_t q_st, int64_t q_sh, const void* k,
+                                                 int64_t k_st, int64_t k_sh, const void* v, int64_t v_st,
+                                                 int64_t v_sh, int total_tokens, int num_heads, int num_kv_heads,
+                                                 int head_dim, const int64_t* positions, double rope_theta,
+                                                 const void* q_norm_weight, const void* k_norm_weight,
+                                                 double rms_norm_eps, void* q_out, const mllm_paged_kv* kv,
+                                                 const int32_t* cu_seqlens, int batch, const int32_t* cache_start,
+                                                 mllm_stream_t stream);
+
+MLLM_API int mllm_prefill_attention_varlen_bf16(const void* q, const void* k_cache, const void* v_cache,
+                                                int64_t cache_sb, int64_t cache_sh, int64_t cache_st,
+                                                int64_t cache_capacity, const int32_t* cu_q_lens,
+                                                const int32_t* kv_lens, int batch, int num_heads, int num_kv_heads,
+                                                int head_dim, int total_q, int max_q_len, float softmax_scale,
+                                                void* out, mllm_stream_t stream);
+
+MLLM_API int mllm_prefill_attention_varlen_paged_bf16(const void* q, const mllm_paged_kv* kv,
+                                                      const int32_t* cu_q_lens, const int32_t* kv_lens, int batch,
+                                                      int num_heads, int num_kv_heads, int head_dim, int total_q,
+                                                      int max_q_len, float softmax_scale, void* out,
+                                                      mllm_stream_t stream);
 
 /* ----------------------------------------------------------------------------------------
  * Token sampling on the device.  Replaces src/core/runtime/Sampler.cpp:49-232

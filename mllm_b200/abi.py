@@ -72,6 +72,13 @@ SIGNATURES = {
     "mllm_decode_attention_paged_bf16": (_i, [_p, _kv, _p, _i, _i, _i, _i, _i, _f, _p, _p, _sz, _p]),
     "mllm_decode_step_paged_bf16": (_i, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _d, _p, _p,
                                          _i64, _p, _p, _d, _kv, _p, _i, _i, _i, _i, _i, _f, _p, _p, _sz, _p]),
+    "mllm_qkv_epilogue_varlen_bf16": (_i, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i, _i, _i, _i, _p, _d,
+                                           _p, _p, _d, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i, _p, _p]),
+    "mllm_qkv_epilogue_varlen_paged_bf16": (_i, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i, _i, _i, _i,
+                                                 _p, _d, _p, _p, _d, _p, _kv, _p, _i, _p, _p]),
+    "mllm_prefill_attention_varlen_bf16": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _i, _i, _i, _i, _i,
+                                                _i, _f, _p, _p]),
+    "mllm_prefill_attention_varlen_paged_bf16": (_i, [_p, _kv, _p, _p, _i, _i, _i, _i, _i, _i, _f, _p, _p]),
     "mllm_linear_workspace_size": (_sz, [_i, _i, C.POINTER(C.c_int64), _i64]),
     "mllm_linear_bf16": (_i, [_p, _i64, _i, _i64, _i, C.POINTER(C.c_void_p), C.POINTER(C.c_int64),
                               C.POINTER(C.c_int64), _p, _i64, _p, _sz, _p]),

@@ -103,7 +103,7 @@ int encode_kv_map(CUtensorMap* map, const void* base, int64_t d, int64_t rows, i
 
 using namespace mllm_b200;
 
-extern "C" int mllm_attn_abi_version(void) { return 4; }
+extern "C" int mllm_attn_abi_version(void) { return 5; }
 
 extern "C" const char* mllm_attn_status_string(int status) {
     switch (status) {

@@ -76,10 +76,17 @@ struct PrefillCfg {
 };
 
 struct PrefillArgs {
-    __nv_bfloat16* out;   // [B, q_len, H*D]
+    __nv_bfloat16* out;   // [B, q_len, H*D]; packed: [total_q, H*D]
     int B, H, Hkv, n_rep, q_len, kv_len, n_mblocks;
     float scale_log2;
     KvLayout lay;         // contiguous, or the paged cache's block table
+    // Packed sequences of different lengths (null: every sequence has q_len / kv_len).  Query
+    // rows of sequence b are rows cu_q[b] .. cu_q[b+1]-1 of Q [H, total_q, D] and of out;
+    // q_len is then the largest length the grid covers.
+    const int32_t* cu_q;
+    const int32_t* kv_lens;
+    int total_q;
+    int64_t max_rows;     // cache rows a sequence may address
 };
 
 __device__ __forceinline__ uint32_t col_s(int i) { return (uint32_t)(i * kBN); }
@@ -113,12 +120,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int b = blockIdx.z;
     const int g = h / a.n_rep;
     const int m0 = mb * (kQTiles * kBM);
-    const int pos_offset = a.kv_len - a.q_len;          // absolute position of query row 0
+    int q_len = a.q_len, kv_len = a.kv_len;
+    if (a.cu_q != nullptr) {
+        // CTA-uniform values: the whole block leaves before any barrier or TMEM allocation.
+        const int r0 = a.cu_q[b], r1 = a.cu_q[b + 1];
+        q_len = r1 - r0;
+        kv_len = a.kv_lens[b];
+        if (r0 < 0 || r1 > a.total_q || q_len < 0 || q_len > a.q_len || kv_len < q_len || kv_len > a.max_rows) {
+            if (threadIdx.x == 0) record_error(kErrBadLength);
+            return;
+        }
+        if (m0 >= q_len) return;                         // shorter than the longest sequence
+    }
+    const int pos_offset = kv_len - q_len;               // absolute position of query row 0
     int n_tiles[kQTiles];                                // cache tiles each query tile can see
 #pragma unroll
     for (int i = 0; i < kQTiles; ++i) {
         const int r0 = m0 + i * kBM;
-        n_tiles[i] = (r0 < a.q_len) ? (pos_offset + min(r0 + kBM - 1, a.q_len - 1)) / kBN + 1 : 0;
+        n_tiles[i] = (r0 < q_len) ? (pos_offset + min(r0 + kBM - 1, q_len - 1)) / kBN + 1 : 0;
     }
     const int n_max = max(n_tiles[0], n_tiles[1]);
 
@@ -156,11 +175,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_desc(&tmK);
             tma_prefetch_desc(&tmV);
             mbar_arrive_expect_tx(q_full, kQTiles * Cfg::kQBytes);
-#pragma unroll
+            // packed sequences: one map over all rows, this sequence's rows from cu_q[b].  The
+            // tile loop stays rolled: unrolled, its two row coordinates spill at 72 registers.
+            const int q_first = a.cu_q ? a.cu_q[b] : 0;
+            const int q_bcoord = a.cu_q ? 0 : b;
+#pragma unroll 1
             for (int i = 0; i < kQTiles; ++i)
 #pragma unroll
                 for (int bx = 0; bx < Cfg::kBoxes; ++bx)
-                    tma_load_4d(sQ + i * Cfg::kQBytes + bx * kBox, &tmQ, q_full, bx * 64, m0 + i * kBM, h, b);
+                    tma_load_4d(sQ + i * Cfg::kQBytes + bx * kBox, &tmQ, q_full, bx * 64, q_first + m0 + i * kBM, h,
+                                q_bcoord);
             for (int j = 0; j < n_max; ++j) {
                 const int stage = j % ST;
                 const uint32_t phase = ((j / ST) & 1) ^ 1;
@@ -330,8 +354,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (n > 0 && alive && mbar_wait(&o_done[qt], 0)) {
             tc_fence_after();
             const float inv_l = 1.f / l_run;
-            const bool valid = q_row < a.q_len;
-            __nv_bfloat16* orow = a.out + (((int64_t)b * a.q_len + q_row) * a.H + h) * (int64_t)D;
+            const bool valid = q_row < q_len;
+            const int64_t out_first = a.cu_q ? (int64_t)a.cu_q[b] : (int64_t)b * a.q_len;
+            __nv_bfloat16* orow = a.out + ((out_first + q_row) * a.H + h) * (int64_t)D;
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
                 float o[32];
@@ -370,14 +395,30 @@ using namespace mllm_b200;
 
 namespace {
 
-// Shared by the contiguous and the paged entry point: the K/V maps cover map_rows rows of
-// map_batch sequences (contiguous) or blocks (paged), and `lay` says which.
+// Packed sequences of different lengths (the varlen entry points): per-sequence query row
+// ranges and cache lengths in device memory, `max_rows` the cache rows one sequence may address.
+struct PackedSeqs {
+    const int32_t* cu_q = nullptr;
+    const int32_t* kv_lens = nullptr;
+    int total_q = 0;
+    int64_t max_rows = 0;
+};
+
+// Shared by the contiguous and the paged entry points: the K/V maps cover map_rows rows of
+// map_batch sequences (contiguous) or blocks (paged), and `lay` says which.  With `packed`,
+// q_len is the longest sequence's length and kv_len is unused.
 int prefill_entry(const void* q, const void* k_cache, const void* v_cache, int64_t cache_sb, int64_t cache_sh,
                   int64_t cache_st, int64_t map_rows, int64_t map_batch, const KvLayout& lay, int batch,
                   int num_heads, int num_kv_heads, int head_dim, int q_len, int kv_len, float softmax_scale,
-                  void* out, mllm_stream_t stream) {
+                  void* out, mllm_stream_t stream, const PackedSeqs& packed = PackedSeqs{}) {
+    const bool varlen = packed.cu_q != nullptr;
+    if (varlen) kv_len = q_len;   // host-side checks below; the device checks each sequence
     if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || q_len < 0 || kv_len < 0)
         return fail(MLLM_ERR_INVALID_ARGUMENT, "prefill_attention: bad sizes");
+    if (varlen && (packed.total_q < 0 || packed.kv_lens == nullptr))
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "prefill_attention_varlen: bad total_q or null kv_lens");
+    if (varlen && packed.total_q > (int64_t)batch * q_len)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "prefill_attention_varlen: total_q exceeds batch * max_q_len");
     if (num_heads % num_kv_heads != 0)
         return fail(MLLM_ERR_INVALID_ARGUMENT, "Attention: num_heads must be divisible by num_kv_heads.");
     if (head_dim != 64 && head_dim != 128)
@@ -385,7 +426,7 @@ int prefill_entry(const void* q, const void* k_cache, const void* v_cache, int64
     if (kv_len < q_len) return fail(MLLM_ERR_INVALID_ARGUMENT, "prefill_attention: kv_len < q_len");
     if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale))
         return fail(MLLM_ERR_INVALID_ARGUMENT, "prefill_attention: softmax_scale must be positive");
-    if (batch == 0 || q_len == 0) return ok();
+    if (batch == 0 || q_len == 0 || (varlen && packed.total_q == 0)) return ok();
     if (!q || !k_cache || !v_cache || !out) return fail(MLLM_ERR_INVALID_ARGUMENT, "prefill_attention: null pointer");
     if (!aligned(q, 16) || !aligned(out, 16))
         return fail(MLLM_ERR_INVALID_ARGUMENT, "prefill_attention: q/out must be 16-byte aligned");
@@ -394,8 +435,11 @@ int prefill_entry(const void* q, const void* k_cache, const void* v_cache, int64
 
     const int64_t D = head_dim;
     CUtensorMap tmQ, tmK, tmV;
-    if (int st = encode_kv_map(&tmQ, q, D, q_len, num_heads, batch, D, (int64_t)q_len * D,
-                               (int64_t)num_heads * q_len * D, 64, kBM))
+    // Q [batch, H, q_len, D], or packed Q [H, total_q, D] as one sequence of total_q rows
+    const int64_t q_rows = varlen ? packed.total_q : q_len;
+    const int64_t q_batch = varlen ? 1 : batch;
+    if (int st = encode_kv_map(&tmQ, q, D, q_rows, num_heads, q_batch, D, q_rows * D, (int64_t)num_heads * q_rows * D,
+                               64, kBM))
         return st;
     if (int st = encode_kv_map(&tmK, k_cache, D, map_rows, num_kv_heads, map_batch, cache_st, cache_sh, cache_sb, 64,
                                kBN))
@@ -415,6 +459,10 @@ int prefill_entry(const void* q, const void* k_cache, const void* v_cache, int64
     a.kv_len = kv_len;
     a.n_mblocks = (q_len + kQTiles * kBM - 1) / (kQTiles * kBM);
     a.scale_log2 = (float)((double)softmax_scale * 1.4426950408889634);
+    a.cu_q = packed.cu_q;
+    a.kv_lens = packed.kv_lens;
+    a.total_q = packed.total_q;
+    a.max_rows = packed.max_rows;
     dim3 grid(a.n_mblocks, num_heads, batch);
     cudaStream_t s = (cudaStream_t)stream;
     // The kernel moves registers between warpgroups with setmaxnreg; that is only safe if the
@@ -473,4 +521,40 @@ extern "C" int mllm_prefill_attention_paged_bf16(const void* q, const mllm_paged
     return prefill_entry(q, kv->k_pool, kv->v_pool, kv->block_stride, kv->head_stride, kv->row_stride,
                          kv->block_size, kv->num_blocks, lay, batch, num_heads, num_kv_heads, head_dim, q_len,
                          kv_len, softmax_scale, out, stream);
+}
+
+extern "C" int mllm_prefill_attention_varlen_bf16(const void* q, const void* k_cache, const void* v_cache,
+                                                  int64_t cache_sb, int64_t cache_sh, int64_t cache_st,
+                                                  int64_t cache_capacity, const int32_t* cu_q_lens,
+                                                  const int32_t* kv_lens, int batch, int num_heads, int num_kv_heads,
+                                                  int head_dim, int total_q, int max_q_len, float softmax_scale,
+                                                  void* out, mllm_stream_t stream) {
+    if (cu_q_lens == nullptr) return fail(MLLM_ERR_INVALID_ARGUMENT, "prefill_attention_varlen: cu_q_lens is NULL");
+    if (cache_capacity <= 0 || cache_capacity > 0x7fffffffLL)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "prefill_attention_varlen: bad cache_capacity");
+    PackedSeqs p;
+    p.cu_q = cu_q_lens;
+    p.kv_lens = kv_lens;
+    p.total_q = total_q;
+    p.max_rows = cache_capacity;
+    return prefill_entry(q, k_cache, v_cache, cache_sb, cache_sh, cache_st, cache_capacity, batch, KvLayout{}, batch,
+                         num_heads, num_kv_heads, head_dim, max_q_len, 0, softmax_scale, out, stream, p);
+}
+
+extern "C" int mllm_prefill_attention_varlen_paged_bf16(const void* q, const mllm_paged_kv* kv,
+                                                        const int32_t* cu_q_lens, const int32_t* kv_lens, int batch,
+                                                        int num_heads, int num_kv_heads, int head_dim, int total_q,
+                                                        int max_q_len, float softmax_scale, void* out,
+                                                        mllm_stream_t stream) {
+    if (cu_q_lens == nullptr) return fail(MLLM_ERR_INVALID_ARGUMENT, "prefill_attention_varlen: cu_q_lens is NULL");
+    KvLayout lay;
+    if (int st = paged_layout(kv, 0, head_dim, "prefill_attention_varlen_paged", &lay)) return st;
+    PackedSeqs p;
+    p.cu_q = cu_q_lens;
+    p.kv_lens = kv_lens;
+    p.total_q = total_q;
+    p.max_rows = (int64_t)kv->max_blocks_per_seq * kv->block_size;
+    return prefill_entry(q, kv->k_pool, kv->v_pool, kv->block_stride, kv->head_stride, kv->row_stride,
+                         kv->block_size, kv->num_blocks, lay, batch, num_heads, num_kv_heads, head_dim, max_q_len, 0,
+                         softmax_scale, out, stream, p);
 }

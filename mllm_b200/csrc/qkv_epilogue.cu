@@ -40,7 +40,30 @@ struct EpilogueArgs {
     KvLayout lay;                          // contiguous, or the paged cache's block table
     const int32_t* cache_start;   // NULL: uniform_start for every sequence
     int64_t uniform_start;
+    // Packed sequences (null: B x S tokens): the call runs as one sequence of all tokens, and
+    // cache sequence i takes tokens cu_seqlens[i] .. cu_seqlens[i+1]-1 (n_seqs sequences).
+    const int32_t* cu_seqlens;
+    int n_seqs;
 };
+
+// Cache sequence and row of token (b, s).  Packed: s is the token's packed index; a token outside
+// the ranges cu_seqlens describes gets row -1 (recorded as a bad length, its K/V not written).
+__device__ __forceinline__ int64_t cache_slot(const EpilogueArgs& a, int b, int s, int& seq) {
+    if (a.cu_seqlens == nullptr) {
+        seq = b;
+        return (a.cache_start ? (int64_t)a.cache_start[b] : a.uniform_start) + s;
+    }
+    int lo = 0, hi = a.n_seqs - 1;   // the last sequence that starts at or before s
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (a.cu_seqlens[mid] <= s) lo = mid;
+        else hi = mid - 1;
+    }
+    const int first = a.cu_seqlens[lo];
+    seq = lo;
+    if (first > s || s >= a.cu_seqlens[lo + 1]) return -1;
+    return (a.cache_start ? (int64_t)a.cache_start[lo] : a.uniform_start) + (s - first);
+}
 
 constexpr int kWarps = 8;
 
@@ -83,6 +106,7 @@ __global__ void __launch_bounds__(kWarps * 32, 6) qkv_epilogue_kernel(EpilogueAr
     __shared__ float s_sin[D];
     __shared__ float s_gamma[2][D];   // q / k per-head norm weights (fp32 copies of the bf16 values)
     __shared__ int64_t s_slot;
+    __shared__ int s_seq;
 
     pdl_trigger();   // a decode launched next may start its set-up (it waits for this grid)
     const int token = blockIdx.x;
@@ -111,7 +135,11 @@ __global__ void __launch_bounds__(kWarps * 32, 6) qkv_epilogue_kernel(EpilogueAr
             s_gamma[1][d] = __bfloat162float(a.k_gamma[d]);
         }
     }
-    if (tid == 0) s_slot = (a.cache_start ? (int64_t)a.cache_start[b] : a.uniform_start) + s;
+    if (tid == 0) {
+        int seq;
+        s_slot = cache_slot(a, b, s, seq);
+        s_seq = seq;
+    }
     // Angles for this token: from the caller's table, or computed (bit-identical to the
     // table that mllm_rope_build_cos_sin would produce for the same position).
     if (a.rope_cos != nullptr) {
@@ -127,6 +155,7 @@ __global__ void __launch_bounds__(kWarps * 32, 6) qkv_epilogue_kernel(EpilogueAr
     __syncthreads();
 
     const int64_t slot = s_slot;
+    const int cseq = s_seq;
 #pragma unroll
     for (int t = 0; t < HPW; ++t) {
         if (head0 + t >= total_heads) break;
@@ -153,7 +182,7 @@ __global__ void __launch_bounds__(kWarps * 32, 6) qkv_epilogue_kernel(EpilogueAr
             dst = a.q_out + (((int64_t)b * a.H + r.h) * a.S + s) * D;
         } else {
             int blk, row;
-            if (slot < 0 || slot >= a.capacity || !kv_locate(a.lay, b, slot, blk, row)) {
+            if (slot < 0 || slot >= a.capacity || !kv_locate(a.lay, cseq, slot, blk, row)) {
                 if (lane == 0) record_error(kErrBadLength);
                 continue;
             }
@@ -185,6 +214,7 @@ __global__ void __launch_bounds__(256, (D == 128 && RPQ >= 4) ? 2 : 3) qkv_epilo
     __shared__ float s_sin[kQwTokens][D];
     __shared__ float s_gamma[2][D];
     __shared__ int64_t s_slot[kQwTokens];
+    __shared__ int s_seq[kQwTokens];
 
     pdl_trigger();   // a decode launched next may start its set-up (it waits for this grid)
     const int tid = threadIdx.x;
@@ -222,7 +252,9 @@ __global__ void __launch_bounds__(256, (D == 128 && RPQ >= 4) ? 2 : 3) qkv_epilo
         const int tk = blockIdx.x * kQwTokens + tid;
         if (tk < ntok) {
             const int bb = tk / a.S, ss = tk - bb * a.S;
-            s_slot[tid] = (a.cache_start ? (int64_t)a.cache_start[bb] : a.uniform_start) + ss;
+            int seq;
+            s_slot[tid] = cache_slot(a, bb, ss, seq);
+            s_seq[tid] = seq;
         }
     }
     for (int idx = tid; idx < kQwTokens * D; idx += blockDim.x) {
@@ -248,6 +280,7 @@ __global__ void __launch_bounds__(256, (D == 128 && RPQ >= 4) ? 2 : 3) qkv_epilo
     if (!tok_ok) return;
 
     const int64_t slot = s_slot[tl];
+    const int cseq = s_seq[tl];
 #pragma unroll
     for (int t = 0; t < RPQ; ++t) {
         const int head = hq + kQwPerTok * t;
@@ -293,7 +326,7 @@ __global__ void __launch_bounds__(256, (D == 128 && RPQ >= 4) ? 2 : 3) qkv_epilo
             dst = a.q_out + (((int64_t)b * a.H + r.h) * a.S + s) * D;
         } else {
             int blk, row;
-            if (slot < 0 || slot >= a.capacity || !kv_locate(a.lay, b, slot, blk, row)) {
+            if (slot < 0 || slot >= a.capacity || !kv_locate(a.lay, cseq, slot, blk, row)) {
                 if (j == 0) record_error(kErrBadLength);
                 continue;
             }
@@ -324,7 +357,8 @@ int epilogue_entry(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh, cons
                    int64_t rope_row_sb, int64_t rope_row_ss, const void* q_norm_weight, const void* k_norm_weight,
                    double rms_norm_eps, void* q_out, void* k_cache, void* v_cache, int64_t cache_sb,
                    int64_t cache_sh, int64_t cache_st, int64_t cache_capacity, const KvLayout& lay,
-                   const int32_t* cache_start, int64_t uniform_cache_start, mllm_stream_t stream) {
+                   const int32_t* cache_start, int64_t uniform_cache_start, mllm_stream_t stream,
+                   const int32_t* cu_seqlens = nullptr, int n_seqs = 0) {
     if (batch < 0 || seq_len < 0 || num_heads <= 0 || num_kv_heads <= 0)
         return fail(MLLM_ERR_INVALID_ARGUMENT, "qkv_epilogue: bad sizes");
     if (num_heads % num_kv_heads != 0)
@@ -368,6 +402,8 @@ int epilogue_entry(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh, cons
     a.lay = lay;
     a.cache_start = cache_start;
     a.uniform_start = uniform_cache_start;
+    a.cu_seqlens = cu_seqlens;
+    a.n_seqs = n_seqs;
 
     // Many tokens (prefill): 4 heads per warp keeps 4 rows in flight per warp.  Few tokens
     // (decode): one head per warp spreads the little work over more SMs.
@@ -446,4 +482,46 @@ extern "C" int mllm_qkv_epilogue_paged_bf16(const void* q, int64_t q_sb, int64_t
                           kv->v_pool, kv->block_stride, kv->head_stride, kv->row_stride,
                           (int64_t)kv->max_blocks_per_seq * kv->block_size, lay, cache_start, uniform_cache_start,
                           stream);
+}
+
+// Packed sequences: the tokens run as one sequence (q/k/v rows `total_tokens` apart by the token
+// strides, positions[t], Q out [H, total_tokens, D]); only the cache rows follow cu_seqlens.
+static int varlen_checks(int total_tokens, const int64_t* positions, const int32_t* cu_seqlens, int batch) {
+    if (total_tokens < 0 || batch < 0) return fail(MLLM_ERR_INVALID_ARGUMENT, "qkv_epilogue_varlen: bad sizes");
+    if (total_tokens > 0 && (batch == 0 || cu_seqlens == nullptr || positions == nullptr))
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "qkv_epilogue_varlen: cu_seqlens, positions and batch >= 1 required");
+    return MLLM_OK;
+}
+
+extern "C" int mllm_qkv_epilogue_varlen_bf16(const void* q, int64_t q_st, int64_t q_sh, const void* k, int64_t k_st,
+                                             int64_t k_sh, const void* v, int64_t v_st, int64_t v_sh,
+                                             int total_tokens, int num_heads, int num_kv_heads, int head_dim,
+                                             const int64_t* positions, double rope_theta, const void* q_norm_weight,
+                                             const void* k_norm_weight, double rms_norm_eps, void* q_out,
+                                             void* k_cache, void* v_cache, int64_t cache_sb, int64_t cache_sh,
+                                             int64_t cache_st, int64_t cache_capacity, const int32_t* cu_seqlens,
+                                             int batch, const int32_t* cache_start, mllm_stream_t stream) {
+    if (int st = varlen_checks(total_tokens, positions, cu_seqlens, batch)) return st;
+    return epilogue_entry(q, 0, q_st, q_sh, k, 0, k_st, k_sh, v, 0, v_st, v_sh, 1, total_tokens, num_heads,
+                          num_kv_heads, head_dim, positions, 0, 1, rope_theta, nullptr, nullptr, 0, 0, q_norm_weight,
+                          k_norm_weight, rms_norm_eps, q_out, k_cache, v_cache, cache_sb, cache_sh, cache_st,
+                          cache_capacity, KvLayout{}, cache_start, 0, stream, cu_seqlens, batch);
+}
+
+extern "C" int mllm_qkv_epilogue_varlen_paged_bf16(const void* q, int64_t q_st, int64_t q_sh, const void* k,
+                                                   int64_t k_st, int64_t k_sh, const void* v, int64_t v_st,
+                                                   int64_t v_sh, int total_tokens, int num_heads, int num_kv_heads,
+                                                   int head_dim, const int64_t* positions, double rope_theta,
+                                                   const void* q_norm_weight, const void* k_norm_weight,
+                                                   double rms_norm_eps, void* q_out, const mllm_paged_kv* kv,
+                                                   const int32_t* cu_seqlens, int batch, const int32_t* cache_start,
+                                                   mllm_stream_t stream) {
+    if (int st = varlen_checks(total_tokens, positions, cu_seqlens, batch)) return st;
+    KvLayout lay;
+    if (int st = paged_layout(kv, 0, head_dim, "qkv_epilogue_varlen_paged", &lay)) return st;
+    return epilogue_entry(q, 0, q_st, q_sh, k, 0, k_st, k_sh, v, 0, v_st, v_sh, 1, total_tokens, num_heads,
+                          num_kv_heads, head_dim, positions, 0, 1, rope_theta, nullptr, nullptr, 0, 0, q_norm_weight,
+                          k_norm_weight, rms_norm_eps, q_out, kv->k_pool, kv->v_pool, kv->block_stride,
+                          kv->head_stride, kv->row_stride, (int64_t)kv->max_blocks_per_seq * kv->block_size, lay,
+                          cache_start, 0, stream, cu_seqlens, batch);
 }

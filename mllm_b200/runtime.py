@@ -206,9 +206,10 @@ class PagedKVCache:
         self._host_lengths[dst], self._host_lengths[src] = self._host_lengths[src], 0
         self.lengths[src] = 0
 
-    def slot(self, seq: int) -> "PagedSlot":
-        """A one-sequence view of row `seq` (prefill of one request while other rows are live)."""
-        return PagedSlot(self, seq)
+    def slot(self, seq: int, count: int = 1) -> "PagedSlot":
+        """A view of rows seq .. seq + count - 1 as a batch of `count` (prefill of new requests
+        while other rows are live)."""
+        return PagedSlot(self, seq, count)
 
     # -- the KVCache interface the attention functions use --
     def host_lengths(self) -> list[int]:
@@ -226,7 +227,7 @@ class PagedKVCache:
         self.set_lengths([self._host_lengths[b] + add[b] for b in range(B)])
 
     def length_of(self, batch: int) -> int:
-        lens = set(self._host_lengths[:batch])
+        lens = set(self.host_lengths()[:batch])
         if len(lens) != 1:
             raise RuntimeError("PagedKVCache: ragged batch has no single length")
         return lens.pop()
@@ -246,54 +247,61 @@ class PagedKVCache:
 
 
 class PagedSlot(PagedKVCache):
-    """Row `seq` of a PagedKVCache seen as a batch of one: the same pools, the parent's block-table
-    row and length (shared memory), and reserve/advance acting on that row."""
+    """Rows `seq` .. `seq + count - 1` of a PagedKVCache seen as a batch of `count`: the same
+    pools, the parent's block-table rows and lengths (shared memory), and reserve/advance acting
+    on those rows."""
 
-    def __init__(self, parent: PagedKVCache, seq: int):   # no pool allocation: a view
-        self._parent, self._seq = parent, seq
+    def __init__(self, parent: PagedKVCache, seq: int, count: int = 1):   # no pool allocation: a view
+        if count < 1 or seq < 0 or seq + count > parent.block_table.shape[0]:
+            raise RuntimeError("PagedSlot: rows outside the parent cache")
+        self._parent, self._seq, self._count = parent, seq, count
         self.block_size = parent.block_size
         self.num_blocks = parent.num_blocks
         self.max_blocks_per_seq = parent.max_blocks_per_seq
         self.k_pool, self.v_pool = parent.k_pool, parent.v_pool
-        self.block_table = parent.block_table[seq:seq + 1]
-        self.lengths = parent.lengths[seq:seq + 1]
+        self.block_table = parent.block_table[seq:seq + count]
+        self.lengths = parent.lengths[seq:seq + count]
+
+    def _row(self, seq: int) -> int:
+        if not 0 <= seq < self._count:
+            raise RuntimeError("PagedSlot: sequence outside the view")
+        return self._seq + seq
 
     @property
     def free_blocks(self) -> int:
         return self._parent.free_blocks
 
     def blocks_of(self, seq: int) -> list[int]:
-        return self._parent.blocks_of(self._seq + seq)
+        return self._parent.blocks_of(self._row(seq))
 
     def reserve(self, seq: int, rows: int) -> None:
-        if seq != 0:
-            raise RuntimeError("PagedSlot: a view holds one sequence")
-        self._parent.reserve(self._seq, rows)
+        self._parent.reserve(self._row(seq), rows)
 
     def release(self, seq: int = 0) -> None:
-        self._parent.release(self._seq)
+        self._parent.release(self._row(seq))
 
     def move(self, src: int, dst: int) -> None:
         raise RuntimeError("PagedSlot: move rows on the parent cache")
 
     def host_lengths(self) -> list[int]:
-        return [self._parent.host_lengths()[self._seq]]
+        return self._parent.host_lengths()[self._seq:self._seq + self._count]
 
     def set_lengths(self, lens: list[int]) -> None:
-        if len(lens) != 1:
-            raise RuntimeError("PagedSlot: a view holds one sequence")
-        self._parent.reserve(self._seq, lens[0])
-        self._parent._host_lengths[self._seq] = lens[0]
-        self.lengths.fill_(lens[0])
+        if len(lens) > self._count:
+            raise RuntimeError("PagedSlot: more lengths than sequences in the view")
+        for b, n in enumerate(lens):
+            self._parent.reserve(self._seq + b, n)
+            self._parent._host_lengths[self._seq + b] = n
+        self.lengths[:len(lens)].copy_(torch.tensor(lens, dtype=torch.int32), non_blocking=True)
 
     def advance(self, n, batch: int | None = None) -> None:
-        self.set_lengths([self.host_lengths()[0] + (n[0] if isinstance(n, list) else n)])
-
-    def length_of(self, batch: int) -> int:
-        return self.host_lengths()[0]
+        B = batch if batch is not None else (len(n) if isinstance(n, list) else self._count)
+        add = n if isinstance(n, list) else [n] * B
+        cur = self.host_lengths()
+        self.set_lengths([cur[b] + add[b] for b in range(B)])
 
     def gather(self, seq: int, rows: int):
-        return self._parent.gather(self._seq + seq, rows)
+        return self._parent.gather(self._row(seq), rows)
 
 
 class DecodeWorkspace:
@@ -382,6 +390,92 @@ def prefill_attention(q: torch.Tensor, kv_cache: KVCache, num_kv_heads: int) -> 
     abi.call("mllm_prefill_attention_bf16", _ptr(q), _ptr(kv_cache.key_buf), _ptr(kv_cache.value_buf),
              csb, csh, cst, B, H, num_kv_heads, D, S, kv_len, 1.0 / math.sqrt(D), _ptr(out),
              abi.stream_handle())
+    return out
+
+
+def _cu_seqlens(q_lens: list[int], device) -> tuple[list[int], torch.Tensor]:
+    """Row offsets of packed sequences: host list and int32 device tensor [len(q_lens) + 1]."""
+    if any(n < 0 for n in q_lens):
+        raise RuntimeError("packed sequences: lengths must be >= 0")
+    cu = [0]
+    for n in q_lens:
+        cu.append(cu[-1] + n)
+    return cu, torch.tensor(cu, dtype=torch.int32).to(device, non_blocking=True)
+
+
+def qkv_epilogue_packed(q, k, v, kv_cache, q_lens: list[int], rope_theta: float, positions=None,
+                        q_norm_weight=None, k_norm_weight=None, eps: float = 1e-6) -> torch.Tensor:
+    """qkv_epilogue for several sequences of different lengths packed on one token axis (one
+    launch).  q [T, H, D] and k/v [T, Hkv, D] (strided views of the projections, D contiguous);
+    sequence b owns the next q_lens[b] tokens, which go to cache slots lengths[b] + s of cache
+    sequence b; the lengths advance by q_lens[b].  positions: int64 [T] (default: each token's
+    cache slot).  Returns Q [H, T, D] (rotated), the layout prefill_attention_packed reads."""
+    for n, t in (("q", q), ("k", k), ("v", v)):
+        _check_cuda_bf16(n, t)
+        if t.dim() != 3 or t.stride(2) != 1:
+            raise RuntimeError(f"Attention: {n} must be rank-3 [T, h, D] with D contiguous")
+    T, H, D = q.shape
+    Hkv = k.shape[1]
+    if H % Hkv != 0:
+        raise RuntimeError("Attention: num_heads must be divisible by num_kv_heads.")
+    B = len(q_lens)
+    cu, cu_dev = _cu_seqlens(q_lens, q.device)
+    if cu[-1] != T:
+        raise RuntimeError("packed sequences: q_lens must sum to the token count")
+    if T == 0:
+        return torch.empty((H, 0, D), dtype=BF16, device=q.device)
+    before = kv_cache.host_lengths()[:B]
+    if positions is None:
+        positions = torch.cat([torch.arange(before[b], before[b] + q_lens[b], dtype=torch.int64)
+                               for b in range(B)]).to(q.device, non_blocking=True)
+    pos = positions.to(device=q.device, dtype=torch.int64).contiguous()
+    if pos.numel() != T:
+        raise RuntimeError("packed sequences: one position per token")
+    qn = kn = None
+    if q_norm_weight is not None:
+        qn = q_norm_weight.to(BF16).contiguous()
+        kn = k_norm_weight.to(BF16).contiguous()
+    q_out = torch.empty((H, T, D), dtype=BF16, device=q.device)
+    start = kv_cache.lengths[:B].clone()    # slots of the new rows: the lengths before this call
+    common = (_ptr(q), q.stride(0), q.stride(1), _ptr(k), k.stride(0), k.stride(1), _ptr(v), v.stride(0),
+              v.stride(1), T, H, Hkv, D, _ptr(pos), float(rope_theta), _ptr(qn), _ptr(kn), float(eps),
+              _ptr(q_out))
+    if isinstance(kv_cache, PagedKVCache):
+        kv_cache.advance(list(q_lens), batch=B)   # reserves the blocks; raises before any launch
+        kv = kv_cache.descriptor()
+        abi.call("mllm_qkv_epilogue_varlen_paged_bf16", *common, C.byref(kv), _ptr(cu_dev), B, _ptr(start),
+                 abi.stream_handle())
+        return q_out
+    if B != len(kv_cache.host_lengths()):
+        raise RuntimeError("packed sequences: one length per cache sequence")
+    kv_cache.advance(list(q_lens))                # raises before any launch if the cache is full
+    csb, csh, cst = kv_cache.strides
+    abi.call("mllm_qkv_epilogue_varlen_bf16", *common, _ptr(kv_cache.key_buf), _ptr(kv_cache.value_buf), csb,
+             csh, cst, kv_cache.capacity, _ptr(cu_dev), B, _ptr(start), abi.stream_handle())
+    return q_out
+
+
+def prefill_attention_packed(q: torch.Tensor, kv_cache, q_lens: list[int], num_kv_heads: int) -> torch.Tensor:
+    """Causal attention of packed sequences: Q [H, T, D] (qkv_epilogue_packed's output, sequence
+    b owning the next q_lens[b] rows, its newest rows) over each sequence's cache rows
+    0 .. lengths[b] - 1 -> [T, H*D]."""
+    H, T, D = q.shape
+    B = len(q_lens)
+    cu, cu_dev = _cu_seqlens(q_lens, q.device)
+    if cu[-1] != T:
+        raise RuntimeError("packed sequences: q_lens must sum to the token count")
+    out = torch.empty((T, H * D), dtype=BF16, device=q.device)
+    max_q = max(q_lens) if q_lens else 0
+    kv_lens = kv_cache.lengths[:B]
+    if isinstance(kv_cache, PagedKVCache):
+        kv = kv_cache.descriptor()
+        abi.call("mllm_prefill_attention_varlen_paged_bf16", _ptr(q), C.byref(kv), _ptr(cu_dev), _ptr(kv_lens), B,
+                 H, num_kv_heads, D, T, max_q, 1.0 / math.sqrt(D), _ptr(out), abi.stream_handle())
+        return out
+    csb, csh, cst = kv_cache.strides
+    abi.call("mllm_prefill_attention_varlen_bf16", _ptr(q), _ptr(kv_cache.key_buf), _ptr(kv_cache.value_buf),
+             csb, csh, cst, kv_cache.capacity, _ptr(cu_dev), _ptr(kv_lens), B, H, num_kv_heads, D, T, max_q,
+             1.0 / math.sqrt(D), _ptr(out), abi.stream_handle())
     return out
 
 
@@ -621,6 +715,22 @@ class Attention:
         q, k, v = _project_qkv(hidden, w_q, w_k, w_v, num_heads, num_kv_heads, head_dim)
         return Attention.forward_projected(q, k, v, w_o, num_heads, num_kv_heads, head_dim,
                                            rope_theta, position_ids, kv_cache)
+
+
+def attention_block_packed(h, w_q, w_k, w_v, w_o, num_heads: int, num_kv_heads: int, head_dim: int,
+                           rope_theta: float, q_lens: list[int], kv_cache, w_q_norm=None, w_k_norm=None,
+                           rms_norm_eps: float = 1e-6, positions=None):
+    """attention_block for several prompts (or prompt chunks) of different lengths in one pass:
+    h [T, hidden] holds the sequences' new rows back to back, sequence b the next q_lens[b] rows,
+    appended to cache sequence b.  One projection, one epilogue and one attention launch for all
+    of them; returns the o_proj output [T, hidden] (or [T, H*D] with w_o None)."""
+    if h.dim() != 2:
+        raise RuntimeError("attention_block_packed: h must be [T, hidden]")
+    q, k, v = _project_qkv(h.unsqueeze(0), w_q, w_k, w_v, num_heads, num_kv_heads, head_dim)
+    qr = qkv_epilogue_packed(q[0].transpose(0, 1), k[0].transpose(0, 1), v[0].transpose(0, 1), kv_cache, q_lens,
+                             rope_theta, positions, w_q_norm, w_k_norm, rms_norm_eps)
+    out = prefill_attention_packed(qr, kv_cache, q_lens, num_kv_heads)
+    return out if w_o is None else _linear(out, w_o)
 
 
 def attention_block(h, w_q, w_k, w_v, w_o, num_heads: int, num_kv_heads: int, head_dim: int,

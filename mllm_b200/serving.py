@@ -7,8 +7,10 @@ a time (Scheduler.cpp:45-77).  Here requests of any length share the GPU:
     0..n-1, so one decode step over all of them is one fused decode launch per layer
     (`mllm_decode_step_paged_bf16`, per-sequence lengths and positions);
   * a request joins when a row is free and every layer has blocks for its whole length (prompt
-    plus new tokens), so a running request is never preempted; its prompt is prefilled alone
-    into row n through a one-row view (`PagedSlot`);
+    plus new tokens), so a running request is never preempted; the prompts that join in one
+    step are prefilled together, packed back to back, into rows n.. through a view of those rows
+    (`PagedSlot`): one projection, epilogue and attention launch per layer for all of them
+    (`mllm_qkv_epilogue_varlen_paged_bf16`, `mllm_prefill_attention_varlen_paged_bf16`);
   * a finished request's blocks go back to the pools and the last live row moves into its row
     (`PagedKVCache.move`: a block-table row copy, no K/V copy);
   * the next tokens of all live rows come from one device sampler call (`mllm_sample`) and one
@@ -102,6 +104,23 @@ class DecoderModel:
         x = rms_norm(h[:, -1], self.norm, s.eps)
         return torch.nn.functional.linear(x, self.lm_head).float()
 
+    def forward_packed(self, ids: torch.Tensor, q_lens: list[int], caches) -> torch.Tensor:
+        """Several prompts in one pass: ids int64 [T] holds them back to back (prompt b the next
+        q_lens[b] tokens, appended to cache sequence b at its current length).  Returns the fp32
+        logits of each prompt's last row [len(q_lens), vocab]."""
+        s = self.s
+        h = self.embed[ids]
+        for lw, cache in zip(self.layers, caches):
+            x = rms_norm(h, lw["ln1"], s.eps)
+            h = h + rt.attention_block_packed(x, lw["w_q"], lw["w_k"], lw["w_v"], lw["w_o"], s.heads, s.kv_heads,
+                                              s.head_dim, s.rope_theta, q_lens, cache, lw["q_norm"], lw["k_norm"],
+                                              s.eps)
+            x = rms_norm(h, lw["ln2"], s.eps)
+            h = h + swiglu_mlp(x, lw["w_gate"], lw["w_up"], lw["w_down"])
+        last = torch.tensor([sum(q_lens[:b + 1]) - 1 for b in range(len(q_lens))], device=h.device)
+        x = rms_norm(h[last], self.norm, s.eps)
+        return torch.nn.functional.linear(x, self.lm_head).float()
+
 
 @dataclass
 class Request:
@@ -162,20 +181,35 @@ class ContinuousBatcher:
 
     def _admit(self) -> None:
         dev = self.model.embed.device if hasattr(self.model, "embed") else "cpu"
-        while self.waiting and len(self.live) < self.max_batch:
+        first = len(self.live)
+        joined: list[Request] = []
+        while self.waiting and first + len(joined) < self.max_batch:
             r = self.waiting[0]
             need = -(-r.rows // self.block_size)
             if any(c.free_blocks < need for c in self.caches):
                 break                        # first come, first served: wait for blocks
             self.waiting.pop(0)
-            row = len(self.live)
+            row = first + len(joined)
             for c in self.caches:
                 c.reserve(row, r.rows)       # the whole request's blocks, up front
-            views = [c.slot(row) for c in self.caches]
-            ids = torch.tensor([r.prompt], dtype=torch.int64, device=dev)
-            pos = torch.arange(len(r.prompt), dtype=torch.int64, device=dev)
-            logits = self.model.forward(ids, pos, views)
-            self._emit(r, self._pick(logits)[0], logits[0])
+            joined.append(r)
+        if not joined:
+            return
+        if hasattr(self.model, "forward_packed"):
+            # every joining prompt in one pass: rows first .. first+k-1, one launch per kernel
+            views = [c.slot(first, len(joined)) for c in self.caches]
+            ids = torch.tensor([t for r in joined for t in r.prompt], dtype=torch.int64, device=dev)
+            logits = self.model.forward_packed(ids, [len(r.prompt) for r in joined], views)
+        else:
+            rows = []
+            for i, r in enumerate(joined):
+                views = [c.slot(first + i) for c in self.caches]
+                ids = torch.tensor([r.prompt], dtype=torch.int64, device=dev)
+                pos = torch.arange(len(r.prompt), dtype=torch.int64, device=dev)
+                rows.append(self.model.forward(ids, pos, views))
+            logits = torch.cat(rows)
+        for r, t, row in zip(joined, self._pick(logits), logits):
+            self._emit(r, t, row)
             self.live.append(r)
 
     def _retire(self) -> None:

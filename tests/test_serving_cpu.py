@@ -82,3 +82,56 @@ def test_move_keeps_block_ownership():
     v = c.slot(1)
     v.advance(3)
     assert c.host_lengths()[1] == 8 and v.length_of(1) == 8
+
+
+class PackedCountingModel(CountingModel):
+    """Also takes several prompts in one pass (forward_packed), as DecoderModel does."""
+
+    def forward_packed(self, ids, q_lens, caches):
+        v = caches[0]
+        assert len(v.host_lengths()) == len(q_lens) and all(n == 0 for n in v.host_lengths())
+        assert ids.numel() == sum(q_lens)
+        for c in caches:
+            c.advance(list(q_lens), batch=len(q_lens))
+        self.calls.append(("packed", tuple(q_lens)))
+        last = torch.tensor([sum(q_lens[:b + 1]) - 1 for b in range(len(q_lens))])
+        logits = torch.zeros(len(q_lens), self.vocab)
+        logits[torch.arange(len(q_lens)), (ids[last] + 1) % self.vocab] = 1.0
+        return logits
+
+
+def test_joining_prompts_are_prefilled_together():
+    m = PackedCountingModel()
+    bat = ContinuousBatcher(m, max_batch=3, num_blocks=8, block_size=128)
+    specs = [([5, 6, 7], 4), ([100] * 200, 3), ([40], 6), ([9] * 129, 2), ([1, 2], 1)]
+    ids = [bat.submit(p, n) for p, n in specs]
+    while bat.waiting or bat.live:
+        bat.step()
+        lens = bat.caches[0].host_lengths()
+        for i, r in enumerate(bat.live):
+            assert lens[i] == len(r.prompt) + len(r.tokens) - 1
+    out = {rid: r.tokens for rid, r in bat.done.items()}
+    for rid, (p, n) in zip(ids, specs):
+        assert out[rid] == [(p[-1] + k) % m.vocab for k in range(1, n + 1)]
+    packed = [c[1] for c in m.calls if c[0] == "packed"]
+    assert packed[0] == (3, 200, 1)              # the first three prompts in one pass
+    assert sum(len(p) for p in packed) == len(specs)
+    for c in bat.caches:
+        assert c.free_blocks == 8 and all(x == 0 for x in c.host_lengths())
+
+
+def test_slot_view_of_several_rows():
+    c = rt.PagedKVCache(8, 1, 8, 128, max_seqs=4, device="cpu")
+    c.set_lengths([10, 0, 0, 0])
+    v = c.slot(1, 2)
+    v.advance([130, 5], batch=2)
+    assert c.host_lengths() == [10, 130, 5, 0] and c.lengths.tolist() == [10, 130, 5, 0]
+    assert v.host_lengths() == [130, 5] and v.lengths.tolist() == [130, 5]
+    assert len(c.blocks_of(1)) == 2 and len(v.blocks_of(1)) == 1
+    assert v.block_table.shape[0] == 2 and v.block_table[0, :2].tolist() == c.blocks_of(1)
+    with pytest.raises(RuntimeError):
+        v.reserve(2, 1)                          # outside the view
+    with pytest.raises(RuntimeError):
+        c.slot(3, 2)                             # past the parent's rows
+    v.release(0)
+    assert c.host_lengths() == [10, 0, 5, 0] and c.free_blocks == 8 - 2
