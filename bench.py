@@ -661,8 +661,8 @@ def run_serve(args):
     n_req, new_tok, serial_sample = args.serve_requests, 32, 4
     prompts = [rng.integers(0, shape.vocab, int(n)).tolist() for n in rng.integers(64, 513, n_req)]
 
-    def serve(batch, reqs):
-        bat = ContinuousBatcher(model, max_batch=batch, num_blocks=batch * 5 + 8, block_size=128)
+    def serve(batch, reqs, graphs=True):
+        bat = ContinuousBatcher(model, max_batch=batch, num_blocks=batch * 5 + 8, block_size=128, graphs=graphs)
         for p in reqs:
             bat.submit(p, new_tok)
         torch.cuda.synchronize()
@@ -670,6 +670,7 @@ def run_serve(args):
         out = bat.run()
         torch.cuda.synchronize()
         dt = time.perf_counter() - t0
+        serve.graph_steps, serve.steps = bat.graph_steps, bat.steps
         del bat
         torch.cuda.empty_cache()
         return dt, sum(len(t) for t in out.values()), sum(len(p) for p in reqs)
@@ -706,13 +707,19 @@ def run_serve(args):
     n_admit = min(16, n_req)
     packed_ms, admit_tok = admit_ms(n_admit, True)
     single_ms, _ = admit_ms(n_admit, False)
+    serve(args.serve_batch, prompts)   # warm-up at full size: the large packed prefill's allocations
+    dt_e, tok_e, _ = serve(args.serve_batch, prompts, graphs=False)
     dt_b, tok_b, ptok_b = serve(args.serve_batch, prompts)
+    steps_b, graph_b = serve.steps, serve.graph_steps
     dt_s, tok_s, ptok_s = serve(1, prompts[:serial_sample])
     line = {"metric": "batched greedy serving through mllm_b200.serving (continuous batching over the paged KV cache)",
             "workload": f"Qwen3-8B geometry, random bf16 weights; {n_req} requests, prompts U[64, 512] tokens, "
                         f"{new_tok} new tokens each",
             "batched": {"max_batch": args.serve_batch, "seconds": dt_b, "new_tokens": tok_b, "prompt_tokens": ptok_b,
-                        "new_tokens_per_s": tok_b / dt_b},
+                        "new_tokens_per_s": tok_b / dt_b, "decode_steps": steps_b,
+                        "decode_steps_from_graphs": graph_b},
+            "batched_eager": {"seconds": dt_e, "new_tokens_per_s": tok_e / dt_e,
+                              "note": "the same run with every decode step launched kernel by kernel"},
             "one_at_a_time": {"requests": serial_sample, "seconds": dt_s, "new_tokens": tok_s,
                               "prompt_tokens": ptok_s, "new_tokens_per_s": tok_s / dt_s},
             "speedup_new_tokens_per_s": (tok_b / dt_b) / (tok_s / dt_s),

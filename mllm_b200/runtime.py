@@ -45,6 +45,8 @@ class KVCache:
     that read `key.size(2)` (the runners' decode position, QwenRunner.cpp:301-310) see the
     cache length.  `lengths` holds per-sequence lengths for ragged batches."""
 
+    capture_max_len = None   # set while a CUDA graph of decode steps is captured (decode_step)
+
     def __init__(self, batch: int, num_kv_heads: int, head_dim: int, capacity: int,
                  device="cuda", zero: bool = True):
         alloc = torch.zeros if zero else torch.empty
@@ -98,6 +100,11 @@ class KVCache:
         self._host_lengths = list(lens)
         self.lengths.copy_(torch.tensor(lens, dtype=torch.int32), non_blocking=True)
 
+    def advance_host(self, n: int, batch: int) -> None:
+        """The host copy of the lengths after a replayed decode graph advanced the device copy."""
+        for b in range(batch):
+            self._host_lengths[b] += n
+
 
 class RoPE:
     @staticmethod
@@ -138,6 +145,8 @@ class PagedKVCache:
     and zeroed when freed (`release`), so the rows past a sequence's length in its last block are
     always finite.  The reference's KVCache (KVCache.h:9-28) is one contiguous tensor per layer;
     this is the serving-format step beyond it."""
+
+    capture_max_len = None   # set while a CUDA graph of decode steps is captured (decode_step)
 
     def __init__(self, num_blocks: int, num_kv_heads: int, head_dim: int, block_size: int = 256,
                  max_seqs: int = 64, max_blocks_per_seq: int | None = None, device="cuda"):
@@ -225,6 +234,12 @@ class PagedKVCache:
         B = batch if batch is not None else (len(n) if isinstance(n, list) else len(self._host_lengths))
         add = n if isinstance(n, list) else [n] * B
         self.set_lengths([self._host_lengths[b] + add[b] for b in range(B)])
+
+    def advance_host(self, n: int, batch: int) -> None:
+        """The host copy of the lengths after a replayed decode graph advanced the device copy
+        (the blocks were reserved before the graph was captured)."""
+        for b in range(batch):
+            self._host_lengths[b] += n
 
     def length_of(self, batch: int) -> int:
         lens = set(self.host_lengths()[:batch])
@@ -318,6 +333,54 @@ class DecodeWorkspace:
 
 
 _WS = DecodeWorkspace()
+
+
+class GraphScratch:
+    """Device scratch owned by one captured CUDA graph: the decode and projection workspaces
+    its kernels were recorded with.  The module's shared workspaces grow by reallocation, which
+    would leave a graph writing into freed memory; these buffers live as long as the graph
+    (hold the object beside it) and are never replaced while a capture is recording."""
+
+    def __init__(self):
+        self._keep: list[torch.Tensor] = []
+        self._cur: dict = {}
+
+    def get(self, key: str, nbytes: int, device) -> torch.Tensor:
+        buf = self._cur.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+            self._keep.append(buf)      # an earlier, smaller one stays alive for the nodes that use it
+            self._cur[key] = buf
+        return buf
+
+
+_capture_scratch: GraphScratch | None = None
+
+
+class graph_scratch:
+    """`with graph_scratch(s):` around a CUDA graph capture makes the kernels recorded inside it
+    take their workspaces from `s`."""
+
+    def __init__(self, scratch: GraphScratch):
+        self.scratch = scratch
+
+    def __enter__(self):
+        global _capture_scratch
+        self.prev, _capture_scratch = _capture_scratch, self.scratch
+        return self.scratch
+
+    def __exit__(self, *exc):
+        global _capture_scratch
+        _capture_scratch = self.prev
+        return False
+
+
+def _capturing() -> bool:
+    if not torch.cuda.is_available() or not torch.cuda.is_current_stream_capturing():
+        return False
+    if _capture_scratch is None:
+        raise RuntimeError("capturing a CUDA graph of these kernels needs runtime.graph_scratch")
+    return True
 
 
 def qkv_epilogue(q, k, v, kv_cache: KVCache, positions: torch.Tensor, rope_theta: float,
@@ -492,7 +555,7 @@ def decode_attention(q: torch.Tensor, kv_cache: KVCache, num_kv_heads: int,
     out = torch.empty((B, 1, H * D), dtype=BF16, device=q.device)
     lib = abi.load()
     nbytes = lib.mllm_decode_attention_workspace_size(B, H, num_kv_heads, D, L)
-    ws = _WS.get(nbytes, q.device)
+    ws = _capture_scratch.get("decode", nbytes, q.device) if _capturing() else _WS.get(nbytes, q.device)
     if isinstance(kv_cache, PagedKVCache):
         kv = kv_cache.descriptor()
         abi.call("mllm_decode_attention_paged_bf16", _ptr(qq), C.byref(kv), _ptr(kv_cache.lengths), B, H,
@@ -529,15 +592,25 @@ def decode_step(q, k, v, kv_cache: KVCache, positions: torch.Tensor, rope_theta:
     if q_norm_weight is not None:
         qn = q_norm_weight.to(BF16).contiguous()
         kn = k_norm_weight.to(BF16).contiguous()
-    if isinstance(kv_cache, PagedKVCache):
-        kv_cache.advance(1, batch=B)   # reserves the blocks; raises before any launch if the pool is full
+    capturing = _capturing()
+    if capturing:
+        # Recorded into a CUDA graph that replays this step many times: the lengths advance on the
+        # device (the caller advances the host copy after each replay, and reserved the blocks
+        # beforehand), and the bound on every sequence's length is the one the graph was made for.
+        if kv_cache.capture_max_len is None:
+            raise RuntimeError("decode_step: set the cache's capture_max_len before capturing a graph")
+        kv_cache.lengths[:B] += 1
+        L = min(kv_cache.capture_max_len, kv_cache.capacity)
     else:
-        kv_cache.advance(1)   # raises before any launch if the cache is full
-    L = min(max(kv_cache.host_lengths()[:B]), kv_cache.capacity)
+        if isinstance(kv_cache, PagedKVCache):
+            kv_cache.advance(1, batch=B)   # reserves the blocks; raises before any launch if the pool is full
+        else:
+            kv_cache.advance(1)   # raises before any launch if the cache is full
+        L = min(max(kv_cache.host_lengths()[:B]), kv_cache.capacity)
     out = torch.empty((B, 1, H * D), dtype=BF16, device=q.device)
     lib = abi.load()
     nbytes = lib.mllm_decode_attention_workspace_size(B, H, num_kv_heads, D, L)
-    ws = _WS.get(nbytes, q.device)
+    ws = _capture_scratch.get("decode", nbytes, q.device) if capturing else _WS.get(nbytes, q.device)
     if isinstance(kv_cache, PagedKVCache):
         kv = kv_cache.descriptor()
         abi.call("mllm_decode_step_paged_bf16",
@@ -633,7 +706,10 @@ def linear(x: torch.Tensor, weights) -> torch.Tensor:
     wst = (C.c_int64 * W)(*[w.stride(0) for w in weights])
     nf = (C.c_int64 * W)(*n)
     need = abi.load().mllm_linear_workspace_size(T, W, nf, K)
-    ws = _linear_workspace(x.device, need)
+    if need and _capturing():
+        ws = _capture_scratch.get("linear", need, x.device)
+    else:
+        ws = _linear_workspace(x.device, need)
     abi.call("mllm_linear_bf16", _ptr(x2), x2.stride(0), T, K, W, wp, wst, nf, _ptr(out), out.stride(0),
              _ptr(ws), ws.numel() if ws is not None else 0, abi.stream_handle())
     return out.view(*lead, sum(n))

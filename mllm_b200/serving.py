@@ -122,6 +122,40 @@ class DecoderModel:
         return torch.nn.functional.linear(x, self.lm_head).float()
 
 
+class DecodeGraph:
+    """One decode step of `n` live rows (embedding, every layer, final norm, lm_head) recorded
+    once as a CUDA graph and then replayed each step: the host issues one graph launch instead of
+    the step's several hundred kernel launches.  A replay is valid while the batch has exactly n
+    rows, every row's cache length stays below `max_len` (the decode plan recorded in the graph)
+    and its blocks are reserved; block-table rows may change between replays, since the kernels
+    read the tables from device memory.  The caches' device lengths advance inside the graph;
+    the caller advances their host copies after each replay (PagedKVCache.advance_host)."""
+
+    def __init__(self, model, caches, n: int, max_len: int):
+        dev = model.embed.device
+        self.n, self.max_len = n, max_len
+        self.ids = torch.zeros((n, 1), dtype=torch.int64, device=dev)
+        self.pos = torch.zeros(n, dtype=torch.int64, device=dev)
+        self.scratch = rt.GraphScratch()
+        self.graph = torch.cuda.CUDAGraph()
+        for c in caches:
+            c.capture_max_len = max_len
+        try:
+            with rt.graph_scratch(self.scratch), torch.cuda.graph(self.graph):
+                self.logits = model.forward(self.ids, self.pos, caches)
+        finally:
+            for c in caches:
+                c.capture_max_len = None
+
+    def replay(self, ids: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """ids int64 [n, 1], pos int64 [n] -> the logits [n, vocab] (overwritten by the next
+        replay)."""
+        self.ids.copy_(ids)
+        self.pos.copy_(pos)
+        self.graph.replay()
+        return self.logits
+
+
 @dataclass
 class Request:
     rid: int
@@ -143,8 +177,16 @@ class ContinuousBatcher:
     new_caches(num_blocks, block_size, max_seqs, max_blocks_per_seq)."""
 
     def __init__(self, model, max_batch: int, num_blocks: int, block_size: int = 256,
-                 max_blocks_per_seq: int | None = None, record_logits: bool = False):
+                 max_blocks_per_seq: int | None = None, record_logits: bool = False, graphs: bool = True,
+                 max_graphs: int = 8):
         self.model = model
+        # CUDA graphs of the decode step, one per batch size, recorded when a size repeats
+        emb = getattr(model, "embed", None)
+        self.graphs = graphs and emb is not None and emb.is_cuda
+        self.max_graphs = max_graphs
+        self._graphs: dict[int, DecodeGraph] = {}
+        self._last_n = 0
+        self.graph_steps = 0   # decode steps that replayed a recorded graph
         self.max_batch = max_batch
         self.caches = model.new_caches(num_blocks, block_size, max_batch, max_blocks_per_seq)
         self.block_size = block_size
@@ -241,10 +283,38 @@ class ContinuousBatcher:
         ids = torch.tensor([[r.tokens[-1]] for r in self.live], dtype=torch.int64, device=dev)
         lens = self.caches[0].host_lengths()[:n]
         pos = torch.tensor(lens, dtype=torch.int64, device=dev)   # the new token's position
-        logits = self.model.forward(ids, pos, self.caches)
+        g = self._decode_graph(n)
+        if g is not None:
+            logits = g.replay(ids, pos)
+            for c in self.caches:
+                c.advance_host(1, n)
+            self.graph_steps += 1
+        else:
+            logits = self.model.forward(ids, pos, self.caches)
         for r, t, row in zip(self.live, self._pick(logits), logits):
             self._emit(r, t, row)
         self.steps += 1
+
+    def _decode_graph(self, n: int):
+        """The recorded decode step for n rows, recorded now if the previous step had n rows too
+        (a batch that keeps its size); None: run the step eagerly."""
+        if not self.graphs:
+            return None
+        repeat, self._last_n = self._last_n == n, n
+        # every live row stays below its request's rows; round up so that one graph serves a while
+        need = max(r.rows for r in self.live)
+        bound = min(-(-need // 256) * 256, self.caches[0].capacity)
+        g = self._graphs.get(n)
+        if g is not None and g.max_len >= need:
+            return g
+        if not repeat:
+            return None
+        self._graphs.pop(n, None)
+        while len(self._graphs) >= self.max_graphs:
+            self._graphs.pop(next(iter(self._graphs)))
+        g = DecodeGraph(self.model, self.caches, n, bound)
+        self._graphs[n] = g
+        return g
 
     def run(self) -> dict[int, list[int]]:
         """Step until every submitted request has finished; returns the tokens of each."""
