@@ -703,6 +703,26 @@ def run_serve(args):
         torch.cuda.empty_cache()
         return best * 1e3, sum(len(p) for p in reqs)
 
+    def step_ms(rows, graphs, steps=10):
+        """Median wall-clock time of one steady decode step of `rows` live requests (sampling
+        and the host read included), after admission and the step that records the graph."""
+        bat = ContinuousBatcher(model, max_batch=rows, num_blocks=rows * 5 + 8, block_size=128, graphs=graphs)
+        for p in prompts[:rows]:
+            bat.submit(p, new_tok)
+        bat.step()
+        bat.step()
+        times = []
+        for _ in range(steps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            bat.step()
+            torch.cuda.synchronize()
+            times.append((time.perf_counter() - t0) * 1e3)
+        assert len(bat.live) == rows
+        del bat
+        torch.cuda.empty_cache()
+        return statistics.median(times)
+
     serve(4, prompts[:4])     # warm-up: library set-up, cuBLAS handles, allocator
     n_admit = min(16, n_req)
     packed_ms, admit_tok = admit_ms(n_admit, True)
@@ -712,6 +732,8 @@ def run_serve(args):
     dt_b, tok_b, ptok_b = serve(args.serve_batch, prompts)
     steps_b, graph_b = serve.steps, serve.graph_steps
     dt_s, tok_s, ptok_s = serve(1, prompts[:serial_sample])
+    rows = min(64, n_req)
+    step_graph, step_eager = step_ms(rows, True), step_ms(rows, False)
     line = {"metric": "batched greedy serving through mllm_b200.serving (continuous batching over the paged KV cache)",
             "workload": f"Qwen3-8B geometry, random bf16 weights; {n_req} requests, prompts U[64, 512] tokens, "
                         f"{new_tok} new tokens each",
@@ -723,6 +745,8 @@ def run_serve(args):
             "one_at_a_time": {"requests": serial_sample, "seconds": dt_s, "new_tokens": tok_s,
                               "prompt_tokens": ptok_s, "new_tokens_per_s": tok_s / dt_s},
             "speedup_new_tokens_per_s": (tok_b / dt_b) / (tok_s / dt_s),
+            "decode_step_ms": {"rows": rows, "graph": step_graph, "eager": step_eager,
+                               "timing": "wall clock per steady step, median of 10, sampling and host read included"},
             "prefill_admission": {"prompts": n_admit, "prompt_tokens": admit_tok, "packed_ms": packed_ms,
                                   "one_per_prompt_ms": single_ms, "speedup": single_ms / packed_ms,
                                   "timing": "wall clock, best of 3, 36 layers + final norm + lm_head"},
