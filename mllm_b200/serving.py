@@ -14,7 +14,9 @@ a time (Scheduler.cpp:45-77).  Here requests of any length share the GPU:
   * a finished request's blocks go back to the pools and the last live row moves into its row
     (`PagedKVCache.move`: a block-table row copy, no K/V copy);
   * the next tokens of all live rows come from one device sampler call (`mllm_sample`) and one
-    device-to-host read per step.
+    device-to-host read per step;
+  * while the batch keeps its size, the decode step replays a CUDA graph recorded for that size
+    (`DecodeGraph`): one launch per step instead of several hundred.
 
 `DecoderModel` is the layer stack of TransformerBlock::Forward (TransformerBlock.h:51-195) with
 the reference's RMSNorm (RMSNorm.h:27-64) and SwiGLU MLP (MLP.h:31-43) as LibTorch ops, the
