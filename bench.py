@@ -411,7 +411,8 @@ def run_gpu(args, rank, world, device):
         stream.wait_stream(side)
         torch.cuda.synchronize()
         gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr):
+        scratch = rt.GraphScratch()   # the recorded launches' workspace, alive as long as the graph
+        with rt.graph_scratch(scratch), torch.cuda.graph(gr):
             for i in range(n):
                 fn(i)
         gr.replay()
@@ -424,7 +425,7 @@ def run_gpu(args, rank, world, device):
             gr.replay()
         a1.record(stream)
         torch.cuda.synchronize()
-        del gr
+        del gr, scratch
         return max_over_ranks(a0.elapsed_time(a1) / (reps * n) * 1e3)
 
     proj = {"ours_us": graphed_us(lambda i: rt.linear(hx, ring[i % 4])),
