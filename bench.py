@@ -505,6 +505,8 @@ def run_gpu(args, rank, world, device):
         torch.cuda.synchronize()
         barrier()
         attn_ms = max_over_ranks(p0.elapsed_time(p1)) / ksteps
+        varlen = prefill_varlen_leg(args, lib, device, gen, Hr, Hkvr, scale, sh, stream, barrier, max_over_ranks,
+                                    ksteps)
         # the layer's exchange step, timed separately (o_proj GEMM, then the all-reduce)
         evo = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(ksteps)]
         barrier()
@@ -554,7 +556,7 @@ def run_gpu(args, rank, world, device):
             barrier()
             peer_ms = max_over_ranks(p0.elapsed_time(p1)) / ksteps
             ex.close()
-        pre = {"peer_ms": peer_ms, "pre_ms": pre_ms, "attn_ms": attn_ms, "steps": ksteps, "oproj_ms": oproj_ms, "overlap_ms": overlap_ms,
+        pre = {"varlen": varlen, "peer_ms": peer_ms, "pre_ms": pre_ms, "attn_ms": attn_ms, "steps": ksteps, "oproj_ms": oproj_ms, "overlap_ms": overlap_ms,
                "allreduce_ms": ar_ms if world > 1 else 0.0, "allreduce_bytes": ar_bytes if world > 1 else 0,
                "allreduce_busbw_gbs": (2 * (world - 1) / world * ar_bytes / (ar_ms * 1e-3) / 1e9)
                if world > 1 and ar_ms > 0 else None}
@@ -643,6 +645,81 @@ def run_gpu(args, rank, world, device):
             "rag": rag, "clocks": clocks,
             "launches_per_step": launches_per_step, "plan": (plan_rows.value, plan_chunks.value),
             "h2d": qkv.numel() * 2, "d2h": out.numel() * 2}
+
+
+VAR_B, VAR_LMIN, VAR_LMAX, VAR_SEED = 32, 512, 8192, 77
+
+
+def prefill_varlen_leg(args, lib, device, gen, Hr, Hkvr, scale, sh, stream, barrier, max_over_ranks, ksteps):
+    """Packed prefill of 32 prompts of U[512, 8192] rows (seeded) over a paged cache, one
+    mllm_prefill_attention_varlen_paged_bf16 launch, against one mllm_prefill_attention_paged_bf16
+    launch per prompt on the same rows.  FLOPs = sum_b 4 H D S_b (S_b + 1) / 2."""
+    import ctypes as C
+    import numpy as np
+    import torch
+    from mllm_b200 import abi
+    lens = np.random.default_rng(VAR_SEED).integers(VAR_LMIN, VAR_LMAX + 1, VAR_B).tolist()
+    T, blk = sum(lens), 256
+    nblk = [-(-L // blk) for L in lens]
+    pool = torch.randn(sum(nblk), Hkvr, blk, D, device=device, generator=gen).bfloat16()
+    vpool = torch.randn_like(pool)
+    perm = torch.randperm(sum(nblk), generator=torch.Generator().manual_seed(VAR_SEED)).tolist()
+    table = torch.zeros(VAR_B, max(nblk), dtype=torch.int32)
+    k = 0
+    for b, nb in enumerate(nblk):
+        table[b, :nb] = torch.tensor(perm[k:k + nb], dtype=torch.int32)
+        k += nb
+    table = table.to(device)
+    ps = pool.stride()
+    kv = abi.PagedKV(pool.data_ptr(), vpool.data_ptr(), ps[0], ps[1], ps[2], sum(nblk), blk, table.data_ptr(),
+                     table.stride(0), max(nblk))
+    q = torch.randn(Hr, T, D, device=device, generator=gen).bfloat16()
+    out = torch.empty(T, Hr * D, dtype=torch.bfloat16, device=device)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=device)
+    kvl = torch.tensor(lens, dtype=torch.int32, device=device)
+    # the same prompts one launch each: Q [1, H, S, D] per prompt, the table row of that prompt
+    q1 = [q[:, int(cu[b]):int(cu[b]) + L].unsqueeze(0).contiguous() for b, L in enumerate(lens)]
+    o1 = [torch.empty(1, L, Hr * D, dtype=torch.bfloat16, device=device) for L in lens]
+    kv1 = [abi.PagedKV(pool.data_ptr(), vpool.data_ptr(), ps[0], ps[1], ps[2], sum(nblk), blk,
+                       table.data_ptr() + b * table.stride(0) * 4, table.stride(0), max(nblk)) for b in range(VAR_B)]
+
+    def packed():
+        st = lib.mllm_prefill_attention_varlen_paged_bf16(q.data_ptr(), C.byref(kv), cu.data_ptr(), kvl.data_ptr(),
+                                                          VAR_B, Hr, Hkvr, D, T, max(lens), scale, out.data_ptr(), sh)
+        assert st == 0, lib.mllm_attn_last_error()
+
+    def one_each():
+        for b, L in enumerate(lens):
+            st = lib.mllm_prefill_attention_paged_bf16(q1[b].data_ptr(), C.byref(kv1[b]), 1, Hr, Hkvr, D, L, L,
+                                                       scale, o1[b].data_ptr(), sh)
+            assert st == 0, lib.mllm_attn_last_error()
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(ksteps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1)) / ksteps
+
+    ms_packed, ms_each = timed(packed), timed(one_each)
+    same = all(torch.equal(out[int(cu[b]):int(cu[b]) + L].view(torch.int16), o1[b][0].view(torch.int16))
+               for b, L in enumerate(lens))
+    fl = sum(4.0 * Hr * D * L * (L + 1) / 2 for L in lens)
+    _, tf_peak, peak_src = load_peaks()
+    tf = fl / (ms_packed * 1e-3) / 1e12
+    return {"workload": f"{VAR_B} prompts of U[{VAR_LMIN}, {VAR_LMAX}] rows (seed {VAR_SEED}, {T} rows), "
+                        f"{Hr} q / {Hkvr} kv heads, paged cache (256-row blocks, shuffled)",
+            "value": tf, "unit": "TFLOP/s", "ms": ms_packed, "one_launch_per_prompt_ms": ms_each,
+            "speedup": ms_each / ms_packed, "bit_identical_to_one_launch_per_prompt": same,
+            "roofline": {"bound": "tensor", "kernel": "prefill_kernel<128> (packed)", "achieved": tf,
+                         "peak": tf_peak, "unit": "TFLOP/s", "frac": tf / tf_peak, "peak_source": peak_src}}
 
 
 def run_serve(args):
@@ -1008,7 +1085,8 @@ def main():
             "roofline": {"bound": "tensor", "kernel": "prefill_kernel<128>",
                          "achieved": fl / n / (p["attn_ms"] * 1e-3) / 1e12, "peak": tf_peak, "unit": "TFLOP/s",
                          "frac": fl / n / (p["attn_ms"] * 1e-3) / 1e12 / tf_peak, "peak_source": peak_src,
-                         "traffic": profile_traffic("prefill_qwen3_8b_b4_s8192")}}
+                         "traffic": profile_traffic("prefill_qwen3_8b_b4_s8192")},
+            "varlen": p["varlen"]}
     if res["rag"] is not None:
         r = res["rag"]
         ach = r["bytes_per_rank"] / (r["ms"] * 1e-3) / 1e9
