@@ -15,7 +15,8 @@ KV bytes read (2 * B * Hkv * L * D * 2 B = 536,870,912 B per step) / step time. 
 same step as two calls (mllm_qkv_epilogue_bf16, then mllm_decode_attention_bf16).
 
 Secondary (`prefill`): Qwen3-8B causal prefill attention, batch 4 x 8192 rows, same head
-geometry; FLOPs = 4 * B * H * D * S(S+1)/2 = 2.199e12 per step.
+geometry; FLOPs = 4 * B * H * D * S(S+1)/2 = 2.199e12 per step.  `prefill.varlen`: 32 prompts of
+U[512, 8192] rows packed into one launch over a paged cache, against one launch per prompt.
 
 Secondary (`ragged_decode`): Qwen3-14B-shaped decode over a ragged batch -- 64 requests whose
 cache lengths are drawn from U[256, 32768] with a fixed seed, 40 q heads / 8 kv heads,
