@@ -110,3 +110,35 @@ def test_no_device_is_reported(lib):
         has_gpu = False
     if not has_gpu:
         assert st in (3, 5)
+
+
+def test_varlen_argument_validation(lib):
+    """The packed-sequence entry points reject inconsistent sizes and missing arrays on the host;
+    an empty packed batch needs no device."""
+    kv = abi.PagedKV(16, 16, 8 * 256 * 128, 256 * 128, 128, 4, 256, 16, 4, 4)
+    cu, lens = 32, 48                    # stand-in device addresses, never dereferenced here
+
+    def attn(cu_=cu, lens_=lens, batch=2, H=8, Hkv=2, D=128, total=10, max_q=8, kvp=kv):
+        return lib.mllm_prefill_attention_varlen_paged_bf16(16, C.byref(kvp), cu_, lens_, batch, H, Hkv, D, total,
+                                                            max_q, 0.1, 16, None)
+    assert attn(cu_=None) == 1 and b"cu_q_lens" in lib.mllm_attn_last_error()
+    assert attn(lens_=None) == 1 and b"kv_lens" in lib.mllm_attn_last_error()
+    assert attn(total=17) == 1 and b"max_q_len" in lib.mllm_attn_last_error()   # 17 rows > 2 x 8
+    assert attn(H=6, Hkv=4) == 1 and b"divisible" in lib.mllm_attn_last_error()
+    assert attn(D=96) == 2
+    bad = abi.PagedKV(16, 16, 8 * 256 * 128, 256 * 128, 128, 4, 100, 16, 4, 4)   # block_size % 128
+    assert attn(kvp=bad) == 1 and b"block_size" in lib.mllm_attn_last_error()
+    assert attn(total=0) == 0            # no rows: nothing to launch
+    st = lib.mllm_prefill_attention_varlen_bf16(16, 16, 16, 0, 0, 0, 0, cu, lens, 2, 8, 2, 128, 10, 8, 0.1, 16,
+                                                None)
+    assert st == 1 and b"cache_capacity" in lib.mllm_attn_last_error()
+
+    def epi(cu_=cu, pos=64, batch=2, total=10, qn=None, kn=None):
+        return lib.mllm_qkv_epilogue_varlen_paged_bf16(16, 1536, 128, 16, 1536, 128, 16, 1536, 128, total, 8, 2,
+                                                       128, pos, 1e6, qn, kn, 1e-6, 16, C.byref(kv), cu_, batch,
+                                                       None, None)
+    assert epi(cu_=None) == 1 and b"cu_seqlens" in lib.mllm_attn_last_error()
+    assert epi(pos=None) == 1
+    assert epi(batch=0) == 1
+    assert epi(qn=16) == 1 and b"norm weights" in lib.mllm_attn_last_error()
+    assert epi(total=0, cu_=None, batch=0) == 0
