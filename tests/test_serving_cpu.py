@@ -135,3 +135,49 @@ def test_slot_view_of_several_rows():
         c.slot(3, 2)                             # past the parent's rows
     v.release(0)
     assert c.host_lengths() == [10, 0, 5, 0] and c.free_blocks == 8 - 2
+
+
+def test_decode_graph_policy(monkeypatch):
+    """When the batcher records a decode graph (a batch size seen two steps running), reuses it
+    (same size, rows within its bound), records again (a longer request joined) or evicts one
+    (more sizes than max_graphs).  The graph class is a stand-in: this runs on CPU."""
+    from mllm_b200 import serving
+
+    made = []
+
+    class FakeGraph:
+        def __init__(self, model, caches, n, max_len):
+            self.n, self.max_len = n, max_len
+            made.append((n, max_len))
+
+        def replay(self, ids, pos):
+            for c in bat.caches:                 # the recorded step advances the device lengths
+                c.lengths[:self.n] += 1
+            return bat.model.forward_logits(ids)
+
+    class Model(CountingModel):
+        def forward_logits(self, ids):
+            B = ids.shape[0]
+            logits = torch.zeros(B, self.vocab)
+            logits[torch.arange(B), (ids[:, -1] + 1) % self.vocab] = 1.0
+            return logits
+
+    monkeypatch.setattr(serving, "DecodeGraph", FakeGraph)
+    bat = ContinuousBatcher(Model(), max_batch=2, num_blocks=12, block_size=128, graphs=False, max_graphs=1)
+    bat.graphs = True                            # as on a GPU model
+    a = bat.submit([1] * 10, 6)
+    bat.step()                                   # admission + an eager step (first time n = 1)
+    assert made == [] and bat.graph_steps == 0
+    bat.step()                                   # n = 1 again: recorded and replayed
+    assert made == [(1, 256)] and bat.graph_steps == 1
+    bat.step()
+    assert made == [(1, 256)] and bat.graph_steps == 2
+    b = bat.submit([2] * 300, 3)                 # joins: n = 2, 303 rows -> bound 512
+    bat.step()
+    assert len(made) == 1                        # a new size: eager this step
+    bat.step()
+    assert made[-1] == (2, 512) and list(bat._graphs) == [2]   # max_graphs = 1: the n = 1 graph is gone
+    out = bat.run()
+    assert out[a] == [(1 + k) % 1000 for k in range(1, 7)] and out[b] == [3, 4, 5]
+    for c in bat.caches:
+        assert c.host_lengths() == [0] * 2 and c.lengths.tolist() == [0, 0] and c.free_blocks == 12
