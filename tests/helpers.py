@@ -6,7 +6,7 @@ import math
 
 import numpy as np
 
-# bf16 outputs vs the reference's fp32 result
+# tolerance of bf16 outputs against the reference's fp32 result (rtol and atol 2e-2)
 RTOL = 2e-2
 ATOL = 2e-2
 
