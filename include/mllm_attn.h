@@ -48,7 +48,7 @@ typedef struct CUstream_st* mllm_stream_t;
 typedef enum mllm_status {
     MLLM_OK = 0,
     MLLM_ERR_INVALID_ARGUMENT = 1, /* shape, stride, alignment or pointer rejected on the host */
-    MLLM_ERR_UNSUPPORTED = 2,      /* valid request this build does not implement (e.g. head_dim) */
+    MLLM_ERR_UNSUPPORTED = 2,      /* valid request this library does not implement (e.g. head_dim) */
     MLLM_ERR_CUDA = 3,             /* a CUDA runtime / driver call failed */
     MLLM_ERR_WORKSPACE = 4,        /* workspace missing or smaller than *_workspace_size() */
     MLLM_ERR_NO_DEVICE = 5,        /* current device is not sm_100 */

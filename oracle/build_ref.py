@@ -6,8 +6,8 @@ The reference (pym2282/mLLM) is header-only C++17 on LibTorch for the attention 
 (src/core/runtime/{Attention,RoPE,KVCache,RMSNorm,Linear,MLP,TransformerBlock}.h).
 Its own CMakeLists.txt is Windows-only, so this recipe compiles oracle/ref_binding.cpp,
 which #includes those headers straight from the reference tree, with g++ against the
-installed LibTorch.  The output goes to oracle/_ref/ (git-ignored; it travels to the
-GPU box with the rest of the working tree, where the reference tree itself is absent).
+installed LibTorch.  The output goes to oracle/_ref/ (git-ignored; it is copied with the rest
+of the working tree to machines that do not have the reference tree).
 
 Usage:  python oracle/build_ref.py [--reference /path/to/mLLM] [--force]
 """
