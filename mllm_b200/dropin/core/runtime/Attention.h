@@ -148,10 +148,14 @@ namespace mllm
             if (S == 1)
             {
                 // decode: the new token's epilogue (QK-norm, RoPE, append at row `start`) and the
-                // attention over all start + 1 rows in one fused launch
+                // attention over all start + 1 rows in one fused launch.  While a CUDA graph of the
+                // layer is recorded, the lengths come from the device (row lens[b] - 1 is appended)
+                // and the plan covers the cache's capacity, so that every replay is valid.
+                b200::DecodeGraphContext* graph = b200::ActiveDecodeGraph();
                 const int64_t L = start + 1;
+                const int64_t plan_len = graph ? graph->plan_len : L;
                 const size_t bytes =
-                    mllm_decode_attention_workspace_size((int)B, num_heads, num_kv_heads, head_dim, (int)L);
+                    mllm_decode_attention_workspace_size((int)B, num_heads, num_kv_heads, head_dim, (int)plan_len);
                 auto ws = b200::DecodeWorkspace(bytes, q.device());
                 b200::Check(
                     mllm_decode_step_bf16(
@@ -159,10 +163,14 @@ namespace mllm
                         v.data_ptr(), v.stride(0), v.stride(1), pos.data_ptr<int64_t>(), 0, rope_theta,
                         nullptr, nullptr, 0, qn.defined() ? qn.data_ptr() : nullptr,
                         kn.defined() ? kn.data_ptr() : nullptr, rms_norm_eps, ks.data_ptr(), vs.data_ptr(),
-                        ks.stride(0), ks.stride(1), ks.stride(2), nullptr, (int)B, num_heads, num_kv_heads,
-                        head_dim, (int)L, scale, out.data_ptr(), ws.data_ptr(), (size_t)ws.numel(), stream),
+                        ks.stride(0), ks.stride(1), ks.stride(2), graph ? graph->lens.data_ptr<int32_t>() : nullptr,
+                        (int)B, num_heads, num_kv_heads, head_dim, (int)plan_len, scale, out.data_ptr(),
+                        ws.data_ptr(), (size_t)ws.numel(), stream),
                     "Attention (decode step)");
-                cache->SetLength(L);
+                if (graph == nullptr)
+                {
+                    cache->SetLength(L);
+                }
             }
             else
             {

@@ -6,6 +6,8 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <torch/torch.h>
 
+#include <cstdint>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -18,6 +20,36 @@ namespace mllm
         inline mllm_stream_t CurrentStream()
         {
             return reinterpret_cast<mllm_stream_t>(at::cuda::getCurrentCUDAStream().stream());
+        }
+
+        // Bumped whenever a shared workspace below is reallocated: a CUDA graph recorded with the
+        // old buffer must not be replayed after that.
+        inline uint64_t& WorkspaceGeneration()
+        {
+            thread_local uint64_t generation = 0;
+            return generation;
+        }
+
+        // Set while a decode layer is recorded as a CUDA graph: the decode step then reads each
+        // sequence's length (including the new token) from `lens` on the device, sizes its plan
+        // for `plan_len` rows, and leaves the host-side cache length to the recorder.
+        struct DecodeGraphContext
+        {
+            torch::Tensor lens;   // int32 [B]
+            int64_t plan_len;
+        };
+
+        inline DecodeGraphContext*& ActiveDecodeGraph()
+        {
+            thread_local DecodeGraphContext* ctx = nullptr;
+            return ctx;
+        }
+
+        // Decode layers replay CUDA graphs when MLLM_B200_DECODE_GRAPHS=1 (read at every call).
+        inline bool DecodeGraphsEnabled()
+        {
+            const char* v = std::getenv("MLLM_B200_DECODE_GRAPHS");
+            return v != nullptr && v[0] == '1' && v[1] == '\0';
         }
 
         // Converts a nonzero mllm_status into std::runtime_error, the reference's convention.
@@ -56,6 +88,7 @@ namespace mllm
             {
                 ws = torch::zeros({(int64_t)std::max<size_t>(bytes, (size_t)1 << 20)},
                                   torch::TensorOptions().dtype(torch::kUInt8).device(dev));
+                ++WorkspaceGeneration();
             }
             return ws;
         }
@@ -117,6 +150,7 @@ namespace mllm
             {
                 ws = torch::zeros({(int64_t)std::max<size_t>(bytes, 256)},
                                   torch::TensorOptions().dtype(torch::kUInt8).device(dev));
+                ++WorkspaceGeneration();
             }
             return ws;
         }
