@@ -866,8 +866,17 @@ def run_generate(args):
         ref_logits = []       # reference last-position logits per step (bf16, host)
         dropin_tf_logits = []  # drop-in logits under teacher forcing (bf16, host)
         tf = {}
-        for flavor in ("reference", "dropin"):
-            mod = load(flavor)
+        mods = {}
+        graph_tokens = None
+        for flavor in ("reference", "dropin", "dropin_graphs"):
+            kind = "dropin" if flavor == "dropin_graphs" else flavor
+            if kind not in mods:
+                mods[kind] = load(kind)
+            mod = mods[kind]
+            if flavor == "dropin_graphs":
+                # a fresh drop-in runner with its decode layers replayed as CUDA graphs: the timed
+                # decode includes recording every layer (steps 2 and 3)
+                os.environ["MLLM_B200_DECODE_GRAPHS"] = "1"
             runner = mod.Runner(d)
             if flavor == "dropin":
                 # teacher forcing: the reference's own greedy tokens fed to the drop-in runner
@@ -913,10 +922,13 @@ def run_generate(args):
             tokens = torch.cat(toks, 1)
             if flavor == "reference":
                 ref_tokens, ref_margins = tokens, torch.stack(margins, 1)
-            else:
+            elif flavor == "dropin":
                 new_tokens = tokens
+            else:
+                graph_tokens = tokens
             del runner
             torch.cuda.empty_cache()
+            os.environ.pop("MLLM_B200_DECODE_GRAPHS", None)
     # fp32 floor: the same (bf16-valued) weights in fp32 through the reference runner, fed the
     # same tokens -- how far each bf16 runner's logits are from a higher-precision run.
     if args.fp32_floor:
@@ -952,6 +964,12 @@ def run_generate(args):
             "reference_runner": results["reference"], "dropin_runner": results["dropin"],
             "speedup_prefill": results["reference"]["prefill_s"] / results["dropin"]["prefill_s"],
             "speedup_decode": results["reference"]["decode_s"] / results["dropin"]["decode_s"],
+            "dropin_runner_decode_graphs": dict(
+                results["dropin_graphs"],
+                speedup_decode=results["reference"]["decode_s"] / results["dropin_graphs"]["decode_s"],
+                tokens_identical_to_eager_dropin=float((graph_tokens == new_tokens).float().mean()),
+                note="MLLM_B200_DECODE_GRAPHS=1 on a fresh runner; the timed decode includes recording "
+                     "every layer"),
             "tokens_identical_fraction": float(same.float().mean()),
             "sequences_fully_identical": int(sum(1 for f in first_div if not f["diverged"])),
             "first_divergence": first_div, "teacher_forced": tf,
