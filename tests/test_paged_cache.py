@@ -68,3 +68,24 @@ def test_abi_rejects_bad_descriptors(lib):
     st = lib.mllm_decode_attention_paged_bf16(16, C.byref(ok), None, 1, 8, 2, 128, 4 * 256 + 1, 0.1, 16, 256,
                                               1 << 20, None)
     assert st == 1 and b"max_blocks_per_seq" in lib.mllm_attn_last_error()
+
+
+def test_packed_helpers_check_on_the_host():
+    """The packed-sequence helpers refuse bad input before any launch: CPU tensors, ragged
+    lengths that do not add up to the token count, negative lengths, and a hidden state that is
+    not [T, hidden].  No cache is touched."""
+    from mllm_b200 import runtime as rt
+    c = PagedKVCache(num_blocks=4, num_kv_heads=2, head_dim=64, block_size=128, max_seqs=2, device="cpu")
+    q = torch.zeros(10, 4, 64, dtype=torch.bfloat16)
+    k = torch.zeros(10, 2, 64, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        rt.qkv_epilogue_packed(q, k, k, c, [4, 6], 1e6)
+    with pytest.raises(RuntimeError, match="lengths must be >= 0"):
+        rt._cu_seqlens([3, -1], "cpu")
+    assert rt._cu_seqlens([3, 0, 5], "cpu")[0] == [0, 3, 3, 8]
+    with pytest.raises(RuntimeError, match="sum to the token count"):
+        rt.prefill_attention_packed(torch.zeros(4, 10, 64, dtype=torch.bfloat16), c, [4, 5], 2)
+    with pytest.raises(RuntimeError, match=r"\[T, hidden\]"):
+        rt.attention_block_packed(torch.zeros(1, 10, 256, dtype=torch.bfloat16), None, None, None, None, 4, 2, 64,
+                                  1e6, [10], c)
+    assert c.host_lengths() == [0, 0] and c.free_blocks == 4
