@@ -468,8 +468,9 @@ def _cu_seqlens(q_lens: list[int], device) -> tuple[list[int], torch.Tensor]:
 
 def qkv_epilogue_packed(q, k, v, kv_cache, q_lens: list[int], rope_theta: float, positions=None,
                         q_norm_weight=None, k_norm_weight=None, eps: float = 1e-6) -> torch.Tensor:
-    """qkv_epilogue for several sequences of different lengths packed on one token axis (one
-    launch).  q [T, H, D] and k/v [T, Hkv, D] (strided views of the projections, D contiguous);
+    """qkv_epilogue (TransformerBlock.h:103-107,130-134 and Attention.h:157-208) for several
+    sequences of different lengths packed on one token axis, in one launch; the reference runs one
+    sequence's prompt per Generate call (QwenRunner.cpp:420-545).  q [T, H, D] and k/v [T, Hkv, D] (strided views of the projections, D contiguous);
     sequence b owns the next q_lens[b] tokens, which go to cache slots lengths[b] + s of cache
     sequence b; the lengths advance by q_lens[b].  positions: int64 [T] (default: each token's
     cache slot).  Returns Q [H, T, D] (rotated), the layout prefill_attention_packed reads."""
@@ -519,8 +520,8 @@ def qkv_epilogue_packed(q, k, v, kv_cache, q_lens: list[int], rope_theta: float,
 
 
 def prefill_attention_packed(q: torch.Tensor, kv_cache, q_lens: list[int], num_kv_heads: int) -> torch.Tensor:
-    """Causal attention of packed sequences: Q [H, T, D] (qkv_epilogue_packed's output, sequence
-    b owning the next q_lens[b] rows, its newest rows) over each sequence's cache rows
+    """Causal attention (Attention.h:220-316) of packed sequences: Q [H, T, D]
+    (qkv_epilogue_packed's output, sequence b owning the next q_lens[b] rows, its newest rows) over each sequence's cache rows
     0 .. lengths[b] - 1 -> [T, H*D]."""
     H, T, D = q.shape
     B = len(q_lens)
@@ -796,7 +797,8 @@ class Attention:
 def attention_block_packed(h, w_q, w_k, w_v, w_o, num_heads: int, num_kv_heads: int, head_dim: int,
                            rope_theta: float, q_lens: list[int], kv_cache, w_q_norm=None, w_k_norm=None,
                            rms_norm_eps: float = 1e-6, positions=None):
-    """attention_block for several prompts (or prompt chunks) of different lengths in one pass:
+    """attention_block (TransformerBlock.h:77-195, attention half) for several prompts (or prompt
+    chunks) of different lengths in one pass:
     h [T, hidden] holds the sequences' new rows back to back, sequence b the next q_lens[b] rows,
     appended to cache sequence b.  One projection, one epilogue and one attention launch for all
     of them; returns the o_proj output [T, hidden] (or [T, H*D] with w_o None)."""
