@@ -53,7 +53,7 @@ THETA, EPS = 1e6, 1e-6
 DEC_B, DEC_L = 32, 4096
 PRE_B, PRE_S = 4, 8192
 # Qwen3-14B ragged decode: 64 requests, lengths U[256, 32768] (seeded), 40 layers
-RAG_B, RAG_H, RAG_HKV, RAG_LAYERS = 64, 40, 8, 40
+RAG_B, RAG_H, RAG_HKV, RAG_LAYERS, RAG_HIDDEN = 64, 40, 8, 40, 5120
 RAG_LMIN, RAG_LMAX, RAG_SEED = 256, 32768, 14
 
 
@@ -145,10 +145,15 @@ class ClockSampler:
 # ------------------------------------------------------------------------------------------
 
 def cpu_reference_decode(steps: int, warmup: int, budget_s: float = 90.0):
-    """The reference's fp32 CPU path (Attention::ForwardProjected via oracle/_ref) on a bounded
-    sample of the decode workload: `sample_b` of the 32 sequences, full cache length, all heads
-    (QK-norm prologue included, as TransformerBlock.h runs it).  Falls back to the numpy port of
-    the oracle when the compiled reference is absent.  Returns a dict for the JSON line."""
+    """The reference's fp32 CPU path on a bounded sample of the decode workload, timed for the
+    same work the GPU step does: QK-norm + RoPE + KV append + attention over the cache, without
+    the q/k/v projections and o_proj.  The reference has no entry point for that part alone (its
+    Attention::ForwardProjected ends with o_proj, Attention.h:322-325), so each sample times the
+    whole Qwen3 attention step (q/k/v Linear, the per-head RMSNorm of TransformerBlock.h:103-134,
+    ForwardProjected) and, right after, its four Linear calls alone on the same shapes, and the
+    attention time is the difference of the medians.  `sample_b` of the 32 sequences at full
+    cache length and all heads; oracle/_ref is the reference compiled from its sources, the numpy
+    port of the oracle stands in when it is absent.  Returns a dict for the JSON line."""
     import numpy as np
     import torch
 
@@ -168,6 +173,7 @@ def cpu_reference_decode(steps: int, warmup: int, budget_s: float = 90.0):
     kc = torch.randn(sample_b, HKV, L - 1, D, generator=g)
     vc = torch.randn(sample_b, HKV, L - 1, D, generator=g)
     h = torch.randn(sample_b, 1, HIDDEN, generator=g)
+    a = torch.randn(sample_b, 1, H * D, generator=g)
     w_q = torch.randn(H * D, HIDDEN, generator=g) * 0.02
     w_k = torch.randn(HKV * D, HIDDEN, generator=g) * 0.02
     w_v = torch.randn(HKV * D, HIDDEN, generator=g) * 0.02
@@ -176,7 +182,7 @@ def cpu_reference_decode(steps: int, warmup: int, budget_s: float = 90.0):
     gk = 1 + 0.1 * torch.randn(D, generator=g)
     pos = torch.tensor([L - 1])
 
-    def one():
+    def full():
         if R is not None:
             q = R.linear(h, w_q).view(sample_b, 1, H, D).transpose(1, 2)
             q = R.rms_norm(q, gq, EPS)
@@ -192,21 +198,41 @@ def cpu_reference_decode(steps: int, warmup: int, budget_s: float = 90.0):
             cache = O.KVCache(kc.numpy(), vc.numpy())
             O.attention_forward_projected(q, k, v, w_o.numpy(), H, HKV, D, THETA, pos.numpy(), cache)
 
+    def linears():
+        if R is not None:
+            R.linear(h, w_q)
+            R.linear(h, w_k)
+            R.linear(h, w_v)
+            R.linear(a, w_o)
+        else:
+            hn, an = h.numpy(), a.numpy()
+            for w_, x_ in ((w_q, hn), (w_k, hn), (w_v, hn), (w_o, an)):
+                x_ @ w_.numpy().T
+
     for _ in range(max(1, min(warmup, 2))):
-        one()
-    times = []
+        full()
+        linears()
+    t_full, t_lin = [], []
     t_start = time.perf_counter()
     for _ in range(steps):
         t0 = time.perf_counter()
-        one()
-        times.append(time.perf_counter() - t0)
+        full()
+        t1 = time.perf_counter()
+        linears()
+        t2 = time.perf_counter()
+        t_full.append(t1 - t0)
+        t_lin.append(t2 - t1)
         if time.perf_counter() - t_start > budget_s:
             break
-    med = statistics.median(times)
+    med_full, med_lin = statistics.median(t_full), statistics.median(t_lin)
+    med = med_full - med_lin
     nbytes = decode_kv_bytes(sample_b, HKV, L, D)
     return {"value": nbytes / med / 1e9, "unit": "GB/s", "cores": cores, "kind": kind,
-            "sample": f"{sample_b} of {DEC_B} sequences (L={L}, all {H} q heads), fp32 CPU, median of "
-                      f"{len(times)} runs", "steps_timed": len(times), "ms_per_step": med * 1e3}
+            "sample": f"{sample_b} of {DEC_B} sequences (L={L}, all {H} q heads), fp32 CPU: QK-norm + RoPE + KV "
+                      f"append + attention = median of the whole attention step ({med_full * 1e3:.2f} ms) minus "
+                      f"median of its q/k/v/o Linear calls timed alone ({med_lin * 1e3:.2f} ms), {len(t_full)} runs",
+            "steps_timed": len(t_full), "ms_per_step": med * 1e3, "full_step_ms": med_full * 1e3,
+            "linear_ms": med_lin * 1e3}
 
 
 # ------------------------------------------------------------------------------------------
@@ -226,6 +252,11 @@ def run_gpu(args, rank, world, device):
     stream = torch.cuda.current_stream()
     sh = stream.cuda_stream
     gen = torch.Generator(device=device).manual_seed(1000 + rank)
+    comm = None
+    if world > 1:
+        # the library's own communicator (mllm_comm_*: non-blocking NCCL with a watchdog)
+        from mllm_b200.comm import Communicator
+        comm = Communicator.from_process_group(timeout_s=60.0)
 
     # ------------------------------- decode workload -------------------------------
     B, L = DEC_B, DEC_L
@@ -296,6 +327,9 @@ def run_gpu(args, rank, world, device):
         epilogue(qkv)
         decode(out)
     torch.cuda.synchronize()
+
+    # the head-sharded layer against the unsharded one, before anything is timed
+    tp_parity = tp_parity_leg(rank, world, device, comm, barrier) if world > 1 else None
 
     sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
                            else int(os.environ.get("LOCAL_RANK", 0)))
@@ -542,8 +576,8 @@ def run_gpu(args, rank, world, device):
         # can read; its owner pulls it from every rank, sums and pushes the rows to every rank
         # (mllm_b200.tp.PeerExchange)
         peer_ms = None
+        from mllm_b200.tp import PeerExchange
         if world > 1:
-            from mllm_b200.tp import PeerExchange
             ex = PeerExchange(Bp * S, HIDDEN, sub=4)
             for _ in range(2):
                 ex(attn2d, w_o)
@@ -557,7 +591,46 @@ def run_gpu(args, rank, world, device):
             barrier()
             peer_ms = max_over_ranks(p0.elapsed_time(p1)) / ksteps
             ex.close()
-        pre = {"varlen": varlen, "peer_ms": peer_ms, "pre_ms": pre_ms, "attn_ms": attn_ms, "steps": ksteps, "oproj_ms": oproj_ms, "overlap_ms": overlap_ms,
+        # The whole attention layer of the step (QKV epilogue + attention + o_proj + exchange), for
+        # every exchange, with the total work fixed (4 x 8192 tokens, 32 q heads) whatever N is.
+        from mllm_b200.tp import SeqParallelOProj
+        w_o_full = (0.02 * torch.randn(HIDDEN, H * D, device=device, generator=gen)).bfloat16()
+        layer_modes = {}
+        if world == 1:
+            layer_modes["single_gpu"] = lambda: torch.matmul(op.view(Bp * S, H * D), w_o_full.t(), out=o_part)
+        else:
+            import torch.distributed as dist
+            layer_modes["gemm_then_nccl_allreduce"] = lambda: (oproj_p(), dist.all_reduce(o_part))
+            layer_modes["gemm_then_comm_allreduce"] = lambda: (oproj_p(), comm.all_reduce(o_part))
+            layer_modes["chunked_overlap"] = lambda: oproj_allreduce(attn2d, w_o)
+            sp_nccl = SeqParallelOProj(Bp * S, HIDDEN)
+            sp_comm = SeqParallelOProj(Bp * S, HIDDEN, comm=comm)
+            layer_modes["seqpar_nccl"] = lambda: sp_nccl(attn2d, w_o_full)
+            layer_modes["seqpar_comm"] = lambda: sp_comm(attn2d, w_o_full)
+            ex_l = PeerExchange(Bp * S, HIDDEN, sub=4)
+            layer_modes["peer_exchange"] = lambda: ex_l(attn2d, w_o)
+        layer_ms = {}
+        for name, exch in layer_modes.items():
+            for _ in range(2):
+                epi_p()
+                attn_p()
+                exch()
+            barrier()
+            torch.cuda.synchronize()
+            p0.record(stream)
+            for i in range(ksteps):
+                epi_p()
+                attn_p()
+                exch()
+            p1.record(stream)
+            torch.cuda.synchronize()
+            barrier()
+            layer_ms[name] = max_over_ranks(p0.elapsed_time(p1)) / ksteps
+        if world > 1:
+            ex_l.close()
+        del w_o_full
+        pre = {"layer_ms": layer_ms,
+               "varlen": varlen, "peer_ms": peer_ms, "pre_ms": pre_ms, "attn_ms": attn_ms, "steps": ksteps, "oproj_ms": oproj_ms, "overlap_ms": overlap_ms,
                "allreduce_ms": ar_ms if world > 1 else 0.0, "allreduce_bytes": ar_bytes if world > 1 else 0,
                "allreduce_busbw_gbs": (2 * (world - 1) / world * ar_bytes / (ar_ms * 1e-3) / 1e9)
                if world > 1 and ar_ms > 0 else None}
@@ -600,7 +673,52 @@ def run_gpu(args, rank, world, device):
         r1.record(stream)
         torch.cuda.synchronize()
         barrier()
-        rag = {"ms": max_over_ranks(r0.elapsed_time(r1) / rsteps), "steps": rsteps,
+        # The Qwen3-14B decode step as its 40 layers run it: per layer the decode over this rank's
+        # kv heads, the o_proj of its q heads' outputs ([64, Hr*D] x [5120, Hr*D]^T, a partial
+        # [64, 5120]) and the all-reduce of that partial (mllm_comm_all_reduce_bf16, NCCL) --
+        # recorded as one CUDA graph of 40 layers and replayed.  Every layer reads the same
+        # cache: its 4.4 GB (per GPU: / N) is far larger than L2, so each layer streams it anew.
+        w_or = (0.02 * torch.randn(RAG_HIDDEN, Hr * D, device=device, generator=gen)).bfloat16()
+        part_r = torch.empty(RAG_B, RAG_HIDDEN, dtype=torch.bfloat16, device=device)
+
+        def exch_r():
+            torch.matmul(orr, w_or.t(), out=part_r)
+            if comm is not None:
+                comm.all_reduce(part_r)
+
+        def graph_ms(body, reps):
+            side = torch.cuda.Stream(device=device)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):
+                body()
+            stream.wait_stream(side)
+            torch.cuda.synchronize()
+            barrier()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                for _ in range(RAG_LAYERS):
+                    body()
+            gr.replay()
+            torch.cuda.synchronize()
+            barrier()
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g0.record(stream)
+            for _ in range(reps):
+                gr.replay()
+            g1.record(stream)
+            torch.cuda.synchronize()
+            barrier()
+            ms = max_over_ranks(g0.elapsed_time(g1) / reps)
+            del gr   # holds NCCL work: released before the communicator
+            torch.cuda.synchronize()
+            return ms
+
+        greps = max(3, min(args.steps, 10))
+        step_ms = graph_ms(lambda: (decode_r(), exch_r()), greps)
+        exch_ms = graph_ms(exch_r, greps)
+        rag_layer = {"step_ms": step_ms, "oproj_exchange_ms": exch_ms, "reps": greps}
+        del w_or, part_r
+        rag = {"layer": rag_layer, "ms": max_over_ranks(r0.elapsed_time(r1) / rsteps), "steps": rsteps,
                "bytes_per_rank": int(lens_np.sum()) * 2 * Hkvr * D * 2, "sum_len": int(lens_np.sum()),
                "max_len": Lmax, "contiguous_cache_bytes": 2 * kr.numel() * 2}
         del kr, vr
@@ -641,11 +759,70 @@ def run_gpu(args, rank, world, device):
         del pk, qr, orr, ws_r
 
     clocks = sampler.stop() if rank == 0 else None
-    return {"elapsed_ms": elapsed_ms, "dec_ms": dec_ms, "unfused_ms": unfused_ms, "e2e_ms": e2e_ms, "pre": pre,
+    if comm is not None:
+        torch.cuda.synchronize()
+        comm.close()
+    return {"tp_parity": tp_parity, "elapsed_ms": elapsed_ms, "dec_ms": dec_ms, "unfused_ms": unfused_ms, "e2e_ms": e2e_ms, "pre": pre,
             "proj": proj,
             "rag": rag, "clocks": clocks,
             "launches_per_step": launches_per_step, "plan": (plan_rows.value, plan_chunks.value),
             "h2d": qkv.numel() * 2, "d2h": out.numel() * 2}
+
+
+TP_B, TP_S, TP_STEPS = 2, 384, 2
+
+
+def tp_parity_leg(rank, world, device, comm, barrier):
+    """The head-sharded attention layer against the unsharded one, on every rank, for every
+    o_proj exchange: a Qwen3-8B-shaped layer (hidden 4096, 32 q / 8 kv heads, head_dim 128,
+    QK-norm, theta 1e6), batch 2, prefill of 384 rows then two decode steps, weights and inputs
+    from one seed on every rank.  Each rank runs its kv-head group through mllm_b200.tp and its
+    full output must lie within rtol = atol = 2e-2 of runtime.attention_block over all heads
+    (the same path on one GPU).  Returns {"max_excess": ..., "ok": ..., "modes": {...}}; the
+    excess is max(|got - ref| - (atol + rtol |ref|)) over ranks, steps and elements."""
+    import torch
+    import torch.distributed as dist
+    from mllm_b200 import runtime as rt, tp
+    g = torch.Generator(device=device).manual_seed(2024)
+    r = lambda *shape, s=0.02: (s * torch.randn(*shape, device=device, generator=g)).bfloat16()
+    w = {"w_q": r(H * D, HIDDEN), "w_k": r(HKV * D, HIDDEN), "w_v": r(HKV * D, HIDDEN), "w_o": r(HIDDEN, H * D)}
+    gq = (1 + 0.1 * torch.randn(D, device=device, generator=g)).bfloat16()
+    gk = (1 + 0.1 * torch.randn(D, device=device, generator=g)).bfloat16()
+    xs = [r(TP_B, TP_S, HIDDEN, s=1.0)] + [r(TP_B, 1, HIDDEN, s=1.0) for _ in range(TP_STEPS)]
+    pos = lambda i: torch.arange(TP_S, device=device) if i == 0 else torch.tensor([TP_S + i - 1], device=device)
+    cache = rt.KVCache(TP_B, HKV, D, TP_S + TP_STEPS)
+    ref = [rt.attention_block(x, w["w_q"], w["w_k"], w["w_v"], w["w_o"], H, HKV, D, THETA, pos(i), cache, gq, gk,
+                              EPS).float() for i, x in enumerate(xs)]
+    shard = tp.shard_heads(H, HKV, world, rank)
+    wq, wk, wv, wo = tp.shard_weights(shard, D, w["w_q"], w["w_k"], w["w_v"], w["w_o"])
+    modes = {}
+    for mode in ("nccl_chunked", "comm", "peer", "seqpar"):
+        ex = {}
+        if mode == "peer":
+            ex = {TP_B * TP_S: tp.PeerExchange(TP_B * TP_S, HIDDEN), TP_B: tp.PeerExchange(TP_B, HIDDEN, sub=1)}
+        elif mode == "seqpar":
+            ex = {TP_B * TP_S: tp.SeqParallelOProj(TP_B * TP_S, HIDDEN, comm=comm)}
+        c = rt.KVCache(TP_B, shard.num_kv_heads, D, TP_S + TP_STEPS)
+        excess = -1e30
+        for i, x in enumerate(xs):
+            e = ex.get(x.shape[0] * x.shape[1])
+            w_o_use = w["w_o"] if isinstance(e, tp.SeqParallelOProj) else wo
+            out = tp.tp_attention_block(x, shard, D, THETA, pos(i), c, wq, wk, wv, w_o_use, gq, gk, EPS,
+                                        overlap_chunks=3, exchange=e,
+                                        comm=comm if mode in ("comm", "seqpar") else None).float()
+            excess = max(excess, float((out - ref[i]).abs().sub(2e-2 + 2e-2 * ref[i].abs()).max()))
+        torch.cuda.synchronize()
+        for e in ex.values():
+            if hasattr(e, "close"):
+                e.close()
+        t = torch.tensor([excess], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        modes[mode] = {"max_excess": float(t.item()), "ok": float(t.item()) <= 0.0}
+        barrier()
+    worst = max(m["max_excess"] for m in modes.values())
+    return {"case": f"Qwen3-8B-shaped layer, batch {TP_B}, prefill {TP_S} rows + {TP_STEPS} decode steps, "
+                    f"kv-head groups over {world} GPUs, vs the unsharded layer at rtol = atol = 2e-2",
+            "max_excess": worst, "ok": worst <= 0.0, "modes": modes}
 
 
 VAR_B, VAR_LMIN, VAR_LMAX, VAR_SEED = 32, 512, 8192, 77
@@ -1073,6 +1250,8 @@ def main():
                          "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                          "peak_source": peak_src, "traffic": profile_traffic("decode_qwen3_8b_b32_l4096")},
             "cpu_baseline": cpu, "clocks": res["clocks"]}
+    if res["tp_parity"] is not None:
+        line["tp_parity"] = res["tp_parity"]
     if res["proj"] is not None:
         pj = res["proj"]
         q_gbs = pj["bytes"] / (pj["ours_us"] * 1e-6) / 1e9
@@ -1106,6 +1285,17 @@ def main():
                          "frac": fl / n / (p["attn_ms"] * 1e-3) / 1e12 / tf_peak, "peak_source": peak_src,
                          "traffic": profile_traffic("prefill_qwen3_8b_b4_s8192")},
             "varlen": p["varlen"]}
+        lm = p["layer_ms"]
+        best = min(lm, key=lm.get)
+        line["layer"] = {
+            "workload": f"the whole attention layer of the Qwen3-8B prefill step (batch {PRE_B} x {PRE_S}): QKV "
+                        f"epilogue + causal attention + o_proj + the o_proj exchange, heads split over {n} GPU(s)",
+            "scaling": "strong", "ms": lm[best], "exchange": best, "ms_by_exchange": lm,
+            "note": "single_gpu: o_proj GEMM with the whole w_o; gemm_then_*_allreduce: column-slice GEMM, then "
+                    "the all-reduce of the [B*S, hidden] partial (torch NCCL, or the library's mllm_comm); "
+                    "chunked_overlap: the GEMM in 4 pieces overlapping their all-reduces; seqpar_*: attention "
+                    "rows all-to-all to their row's owner, full-K o_proj there, all-gather of the output rows "
+                    "(torch NCCL, or mllm_comm for the all-gather); peer_exchange: pull-sum-push over peer memory"}
     if res["rag"] is not None:
         r = res["rag"]
         ach = r["bytes_per_rank"] / (r["ms"] * 1e-3) / 1e9
@@ -1119,6 +1309,15 @@ def main():
             "roofline": {"bound": "hbm", "kernel": "decode_split_kernel<128> + decode_combine_kernel",
                          "achieved": ach, "peak": hbm_peak, "unit": "GB/s", "frac": ach / hbm_peak,
                          "peak_source": peak_src},
+            "layer_step": {
+                "ms_per_step_all_layers": r["layer"]["step_ms"],
+                "ms_per_layer": r["layer"]["step_ms"] / RAG_LAYERS,
+                "oproj_and_allreduce_ms_per_step": r["layer"]["oproj_exchange_ms"],
+                "collective_share": r["layer"]["oproj_exchange_ms"] / r["layer"]["step_ms"],
+                "timing": f"{RAG_LAYERS} layers recorded in one CUDA graph, replayed {r['layer']['reps']} times",
+                "note": "per layer: decode over this rank's kv heads, o_proj of its q heads ([64, Hr*D] x "
+                        "[5120, Hr*D]^T) and mllm_comm_all_reduce_bf16 of the [64, 5120] partial (no collective "
+                        "at one GPU); oproj_and_allreduce_ms_per_step times those two alone"},
             "paged": {"value": r["bytes_per_rank"] * n / (r["paged_ms"] * 1e-3) / 1e9, "unit": "GB/s",
                       "ms_per_layer": r["paged_ms"], "block_size": r["paged_block_size"],
                       "cache_bytes_per_rank": r["paged_pool_bytes"],

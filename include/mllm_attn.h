@@ -23,7 +23,9 @@
  *   - Every call is asynchronous on `stream` (NULL = the legacy default stream) and
  *     returns an mllm_status; no C++ exception crosses this boundary.  Argument errors are
  *     detected on the host before anything is launched.
- *   - The library never allocates device memory; callers pass workspaces.
+ *   - The attention, sampling and projection entry points never allocate device memory;
+ *     callers pass workspaces.  Only mllm_ipc_alloc (the shared buffers of the tensor-parallel
+ *     exchange) and the communicator set-up of mllm_comm_* allocate, once, at set-up.
  *   - Not thread-safe per stream, like the reference runtime (one Generate at a time).
  */
 #ifndef MLLM_ATTN_H_
@@ -53,7 +55,9 @@ typedef enum mllm_status {
     MLLM_ERR_WORKSPACE = 4,        /* workspace missing or smaller than *_workspace_size() */
     MLLM_ERR_NO_DEVICE = 5,        /* current device is not sm_100 */
     MLLM_ERR_DEVICE_TIMEOUT = 6,   /* a kernel's bounded wait expired (see mllm_attn_device_status) */
-    MLLM_ERR_DEVICE_LENGTH = 7     /* a device-side length exceeded its host-given capacity */
+    MLLM_ERR_DEVICE_LENGTH = 7,    /* a device-side length exceeded its host-given capacity */
+    MLLM_ERR_COMM = 8,             /* a communicator failed (NCCL error, a peer lost) or was aborted */
+    MLLM_ERR_COMM_TIMEOUT = 9      /* a collective ran past its deadline; the communicator was aborted */
 } mllm_status;
 
 /* Version of this ABI (bumped on any signature change). */
@@ -184,14 +188,18 @@ MLLM_API int mllm_decode_attention_bf16(const void* q, const void* k_cache, cons
  *   whose mllm_decode_attention_workspace_size() exceeds 16 MiB is rejected with
  *   MLLM_ERR_WORKSPACE (C2-sized work -- 32 sequences x 8 kv heads x 4096 rows at
  *   head_dim 128 -- needs about 8.1 MiB).
- *   The first call on each device looks up the array's device address (cudaGetSymbolAddress);
- *   make that first call before any CUDA stream capture begins.
+ *   The first call in each CUDA context of a device (the first call of the process, and the
+ *   first after cudaDeviceReset or after the primary context was released and made again)
+ *   looks up the array's device address (cudaGetSymbolAddress) and caches it under the
+ *   context's ID; make that first call before any CUDA stream capture begins.
  *   All calls on a device share the array, which keeps the previous call's contents.  Its
  *   first 256 bytes are the work-item counter of the decode workspace: zero from the start
- *   (static storage) and set back to zero by every call that uses it; the partials after it
- *   are always written earlier in a call than they are read, so nothing needs clearing.  Calls
- *   that overlap on the GPU -- concurrent streams, or several host threads -- race on it:
- *   serialise them. */
+ *   (static storage) and set back to zero by every call that uses it -- by the combine kernel,
+ *   or, when a call fails after its split kernel was launched, by a memset queued behind it;
+ *   the partials after it are always written earlier in a call than they are read, so nothing
+ *   needs clearing.  Only a failed CUDA context (after which nothing in it is usable) can
+ *   leave the counter dirty.  Calls that overlap on the GPU -- concurrent streams, or several
+ *   host threads -- race on it: serialise them. */
 MLLM_API int mllm_decode_attention_noalloc_bf16(const void* q, const void* k_cache, const void* v_cache,
                                                 int64_t cache_sb, int64_t cache_sh, int64_t cache_st,
                                                 const int32_t* kv_lens, int batch, int num_heads,
@@ -427,6 +435,8 @@ MLLM_API int mllm_linear_bf16(const void* x, int64_t x_stride, int tokens, int64
  *       release (flag may be a peer's memory)
  *   mllm_wait_u32: the stream's later work waits until (int32)(*flag - value) >= 0; gives up
  *       after about four seconds and records MLLM_ERR_DEVICE_TIMEOUT (mllm_attn_device_status)
+ *   mllm_wait_u32_timeout: the same wait, giving up after timeout_us microseconds of device
+ *       time (1 us .. 60 s), for callers that want a short deadline
  *   mllm_sum_bf16: dsts[d][i] = sum over s of srcs[s][i] for every d < n_dst, fp32 in the order
  *       s = 0, 1, ..., one rounding to bf16; 1..8 sources and destinations (either may be a
  *       peer's opened allocation), 16-byte aligned, count a multiple of 8 */
@@ -439,8 +449,47 @@ MLLM_API int mllm_ipc_close_handle(void* ptr);
 MLLM_API int mllm_copy_async(void* dst, const void* src, size_t bytes, mllm_stream_t stream);
 MLLM_API int mllm_signal_u32(uint32_t* flag, uint32_t value, mllm_stream_t stream);
 MLLM_API int mllm_wait_u32(const uint32_t* flag, uint32_t value, mllm_stream_t stream);
+MLLM_API int mllm_wait_u32_timeout(const uint32_t* flag, uint32_t value, uint32_t timeout_us, mllm_stream_t stream);
 MLLM_API int mllm_sum_bf16(void* const* dsts, int n_dst, const void* const* srcs, int n_src, int64_t count,
                            mllm_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------
+ * Communicators for the tensor-parallel exchange.  No counterpart in the reference, which runs
+ * every layer on one device (QwenRunner.cpp:236,328): sharding attention by KV-head group makes
+ * o_proj (Attention.h:322-325) a sum of per-rank partials, and these carry that sum over NVLink
+ * with NCCL, one process per GPU.  The C++ drop-in's tensor-parallel mode
+ * (b200::TensorParallel) and mllm_b200/tp.py call them.
+ *   mllm_comm_unique_id: fills MLLM_COMM_ID_BYTES bytes on one rank; the caller hands them to
+ *       every rank (its own side channel: a store, a file, MPI)
+ *   mllm_comm_init: every rank, on its own current device: a NON-BLOCKING NCCL communicator
+ *       (ncclConfig_t.blocking = 0) plus a watchdog thread.  Set-up, tear-down and every
+ *       collective are bounded by timeout_s seconds.
+ *   mllm_comm_all_reduce_bf16: recv[i] = sum over ranks of send[i] (bf16, in place allowed),
+ *       enqueued on `stream` after its earlier work; the o_proj exchange
+ *   mllm_comm_all_gather_bf16: recv = the ranks' send buffers (send_count elements each)
+ *       concatenated in rank order
+ *   Failure detection: the watchdog tracks each collective by an event recorded behind it and
+ *   polls every 5 ms.  An asynchronous NCCL error (a peer failed or left) or a collective still
+ *   running timeout_s after it was enqueued aborts the communicator (ncclCommAbort ends its
+ *   kernels); from then on every call returns MLLM_ERR_COMM or MLLM_ERR_COMM_TIMEOUT and the
+ *   caller builds a new communicator.  mllm_comm_status polls once and reports that state;
+ *   mllm_comm_abort aborts on request (the host learned by itself that a peer is gone);
+ *   mllm_comm_in_flight counts the tracked collectives not yet complete.  Collectives enqueued
+ *   while `stream` is captured into a CUDA graph are not tracked.
+ *   mllm_comm_destroy: finalises (bounded) and frees a healthy communicator; frees an aborted
+ *   one.  Stops the watchdog.  Must not race with other calls on the communicator. */
+#define MLLM_COMM_ID_BYTES 128
+typedef struct mllm_comm* mllm_comm_t;
+MLLM_API int mllm_comm_unique_id(void* id);
+MLLM_API int mllm_comm_init(const void* id, int nranks, int rank, double timeout_s, mllm_comm_t* comm);
+MLLM_API int mllm_comm_all_reduce_bf16(mllm_comm_t comm, const void* send, void* recv, size_t count,
+                                       mllm_stream_t stream);
+MLLM_API int mllm_comm_all_gather_bf16(mllm_comm_t comm, const void* send, void* recv, size_t send_count,
+                                       mllm_stream_t stream);
+MLLM_API int mllm_comm_status(mllm_comm_t comm);
+MLLM_API int mllm_comm_in_flight(mllm_comm_t comm);
+MLLM_API int mllm_comm_abort(mllm_comm_t comm);
+MLLM_API int mllm_comm_destroy(mllm_comm_t comm);
 
 #ifdef __cplusplus
 } /* extern "C" */

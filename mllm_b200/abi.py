@@ -21,7 +21,7 @@ MLLM_OK = 0
 STATUS_NAMES = {
     0: "MLLM_OK", 1: "MLLM_ERR_INVALID_ARGUMENT", 2: "MLLM_ERR_UNSUPPORTED", 3: "MLLM_ERR_CUDA",
     4: "MLLM_ERR_WORKSPACE", 5: "MLLM_ERR_NO_DEVICE", 6: "MLLM_ERR_DEVICE_TIMEOUT",
-    7: "MLLM_ERR_DEVICE_LENGTH",
+    7: "MLLM_ERR_DEVICE_LENGTH", 8: "MLLM_ERR_COMM", 9: "MLLM_ERR_COMM_TIMEOUT",
 }
 
 _i = C.c_int
@@ -90,7 +90,16 @@ SIGNATURES = {
     "mllm_copy_async": (_i, [_p, _p, _sz, _p]),
     "mllm_signal_u32": (_i, [_p, C.c_uint32, _p]),
     "mllm_wait_u32": (_i, [_p, C.c_uint32, _p]),
+    "mllm_wait_u32_timeout": (_i, [_p, C.c_uint32, C.c_uint32, _p]),
     "mllm_sum_bf16": (_i, [C.POINTER(C.c_void_p), _i, C.POINTER(C.c_void_p), _i, _i64, _p]),
+    "mllm_comm_unique_id": (_i, [_p]),
+    "mllm_comm_init": (_i, [_p, _i, _i, _d, C.POINTER(C.c_void_p)]),
+    "mllm_comm_all_reduce_bf16": (_i, [_p, _p, _p, _sz, _p]),
+    "mllm_comm_all_gather_bf16": (_i, [_p, _p, _p, _sz, _p]),
+    "mllm_comm_status": (_i, [_p]),
+    "mllm_comm_in_flight": (_i, [_p]),
+    "mllm_comm_abort": (_i, [_p]),
+    "mllm_comm_destroy": (_i, [_p]),
     "mllm_sample_workspace_size": (_sz, [_i, _i]),
     "mllm_sample": (_i, [_p, _i, _i64, _i, _i, _p, _i64, _p, _f, _i, _f, _i, _f, C.c_uint64, C.c_uint64, _p, _p,
                          _sz, _p]),

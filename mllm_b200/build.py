@@ -4,7 +4,8 @@
 
 Every .cu file under mllm_b200/csrc is compiled with nvcc for sm_100a (whole-program device
 code per file: no relocatable device code, which would make ptxas ignore setmaxnreg) and
-linked into one shared library with the CUDA runtime linked statically.  The library exports only the
+linked into one shared library with the CUDA runtime linked statically and NCCL linked
+dynamically (the libnccl.so.2 that PyTorch loads, found through an rpath).  The library exports only the
 extern "C" entry points declared in include/mllm_attn.h.
 """
 from __future__ import annotations
@@ -32,6 +33,21 @@ def nvcc() -> str:
         if cand and os.path.exists(cand):
             return cand
     raise RuntimeError("nvcc not found")
+
+
+def nccl_lib_dir() -> str:
+    """Directory of the libnccl.so.2 that PyTorch itself loads (the library links the same one, so a
+    process that holds both has one NCCL); the system copy otherwise."""
+    import importlib.util
+    spec = importlib.util.find_spec("nvidia")
+    for base in (list(spec.submodule_search_locations) if spec and spec.submodule_search_locations else []):
+        d = os.path.join(base, "nccl", "lib")
+        if os.path.exists(os.path.join(d, "libnccl.so.2")):
+            return d
+    for d in ("/usr/lib/x86_64-linux-gnu", "/usr/local/cuda/lib64"):
+        if os.path.exists(os.path.join(d, "libnccl.so.2")):
+            return d
+    raise RuntimeError("libnccl.so.2 not found")
 
 
 def lib_path() -> str:
@@ -62,8 +78,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
     os.makedirs(LIB_DIR, exist_ok=True)
     os.makedirs(OBJ_DIR, exist_ok=True)
     cc = nvcc()
-    objs = []
-    for src in _sources():
+    def compile_one(src):
         obj = os.path.join(OBJ_DIR, os.path.basename(src).replace(".cu", ".o"))
         cmd = [cc, *ARCH, *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-c", src, "-o", obj]
         if ptxas_verbose:
@@ -71,10 +86,17 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)
-        objs.append(obj)
+        return obj
+
+    # one nvcc per translation unit, in parallel (each is independent whole-program device code)
+    import concurrent.futures as cf
+    with cf.ThreadPoolExecutor(max_workers=max(1, min(len(_sources()), os.cpu_count() or 1))) as ex:
+        objs = list(ex.map(compile_one, _sources()))
     tmp = out + ".tmp"
+    nccl_dir = nccl_lib_dir()
     cmd = [cc, *ARCH, "-shared", "-cudart", "static", *objs, "-o", tmp,
-           "-Xcompiler", "-fPIC", "-Xlinker", "--exclude-libs,ALL"]
+           "-Xcompiler", "-fPIC", "-Xlinker", "--exclude-libs,ALL",
+           f"-L{nccl_dir}", "-Xlinker", f"-rpath,{nccl_dir}", "-l:libnccl.so.2"]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)

@@ -103,7 +103,7 @@ int encode_kv_map(CUtensorMap* map, const void* base, int64_t d, int64_t rows, i
 
 using namespace mllm_b200;
 
-extern "C" int mllm_attn_abi_version(void) { return 5; }
+extern "C" int mllm_attn_abi_version(void) { return 6; }
 
 extern "C" const char* mllm_attn_status_string(int status) {
     switch (status) {
@@ -115,6 +115,8 @@ extern "C" const char* mllm_attn_status_string(int status) {
         case MLLM_ERR_NO_DEVICE: return "no sm_100 device";
         case MLLM_ERR_DEVICE_TIMEOUT: return "device wait timed out";
         case MLLM_ERR_DEVICE_LENGTH: return "device length out of range";
+        case MLLM_ERR_COMM: return "communicator failed or aborted";
+        case MLLM_ERR_COMM_TIMEOUT: return "collective timed out";
         default: return "unknown status";
     }
 }

@@ -713,8 +713,12 @@ int launch_decode_d(DecodeArgs& a, const CUtensorMap& tmK, const CUtensorMap& tm
         return st;
     if (a.nch > 1) {
         if (int st = check_cuda(launch_pdl(decode_combine_kernel<D>, dim3(a.Hkv, a.B), dim3(128), 0, s, a),
-                                "decode_combine_kernel launch"))
+                                "decode_combine_kernel launch")) {
+            // The split grid is queued and takes items from the counter, which only the combine
+            // resets: zero it in stream order so the workspace's next call starts clean.
+            (void)cudaMemsetAsync(workspace, 0, kHeaderBytes, s);
             return st;
+        }
     }
     return MLLM_OK;
 }
@@ -877,23 +881,66 @@ constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
 static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[kNoAllocScratchBytes];
 
 constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mutex;
-void* g_noalloc_ptr[kMaxDevices] = {};
 
-// Device address of the scratch array on the current device.  The first call on a device looks
-// it up with cudaGetSymbolAddress (host code cannot use the array's name as a device address).
+// The array's address belongs to one CUDA context: after cudaDeviceReset, or once the primary
+// context is released and created again, the module is loaded anew and may sit elsewhere.  So
+// the cached address is keyed by the context's unique ID (cuCtxGetId), and looked up again
+// whenever the current context is a different one.
+struct ScratchAddr {
+    unsigned long long ctx_id;   // 0: not cached
+    void* ptr;
+};
+std::mutex g_noalloc_mutex;
+ScratchAddr g_noalloc_addr[kMaxDevices] = {};
+
+using PfnCtxGetCurrent = CUresult (*)(CUcontext*);
+using PfnCtxGetId = CUresult (*)(CUcontext, unsigned long long*);
+
+// ID of the calling thread's current context; false if there is none yet (or the driver has no
+// cuCtxGetId), in which case the caller looks the address up every time.
+bool current_ctx_id(unsigned long long* id) {
+    static PfnCtxGetCurrent get_current = nullptr;
+    static PfnCtxGetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<PfnCtxGetCurrent>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<PfnCtxGetId>(p);
+    });
+    if (!get_current || !get_id) return false;
+    CUcontext ctx = nullptr;
+    if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return false;
+    return get_id(ctx, id) == CUDA_SUCCESS && *id != 0;
+}
+
+// Device address of the scratch array in the current context.  The first call in a context
+// looks it up with cudaGetSymbolAddress (host code cannot use the array's name as a device
+// address; that lookup also creates the primary context if there is none yet).
 int noalloc_scratch(void** out) {
     int dev = 0;
     if (int st = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return st;
     if (dev < 0 || dev >= kMaxDevices) return fail(MLLM_ERR_UNSUPPORTED, "decode_attention_noalloc: device index too large");
+    unsigned long long id = 0;
+    bool have_id = current_ctx_id(&id);
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (g_noalloc_ptr[dev] == nullptr) {
-        void* p = nullptr;
-        if (int st = check_cuda(cudaGetSymbolAddress(&p, g_decode_noalloc_scratch), "cudaGetSymbolAddress(scratch)"))
-            return st;
-        g_noalloc_ptr[dev] = p;
+    ScratchAddr& c = g_noalloc_addr[dev];
+    if (have_id && c.ctx_id == id && c.ptr != nullptr) {
+        *out = c.ptr;
+        return MLLM_OK;
     }
-    *out = g_noalloc_ptr[dev];
+    void* p = nullptr;
+    if (int st = check_cuda(cudaGetSymbolAddress(&p, g_decode_noalloc_scratch), "cudaGetSymbolAddress(scratch)"))
+        return st;
+    if (!have_id) have_id = current_ctx_id(&id);
+    c.ctx_id = have_id ? id : 0ull;
+    c.ptr = p;
+    *out = p;
     return MLLM_OK;
 }
 
@@ -942,9 +989,10 @@ extern "C" int mllm_decode_attention_noalloc_bf16(const void* q, const void* k_c
                                64, kTile))
         return st;
 
-    // The scratch begins with the work-item counter: zero from the start (static storage) and
-    // reset by the combine kernel of every call that takes items from it.  Every partial the
-    // combine reads is written earlier in the same call.  So nothing needs clearing between calls.
+    // The scratch begins with the work-item counter: zero from the start (static storage), reset
+    // by the combine kernel of every call that takes items from it, and reset in stream order
+    // when the combine cannot be launched.  Every partial the combine reads is written earlier
+    // in the same call.  So nothing needs clearing between calls.
     DecodeArgs a = {};
     a.q = (const __nv_bfloat16*)q;
     a.kv_lens = kv_lens;

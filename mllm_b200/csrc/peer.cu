@@ -38,6 +38,27 @@ __global__ void wait_kernel(const uint32_t* flag, uint32_t value) {
     record_error(kErrTimeout);
 }
 
+// The same wait bounded by device time (%globaltimer, ns) instead of a poll count.  The poll
+// count is capped too (far above any timeout the host accepts), so the loop ends even if the
+// timer were to stall.
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+__global__ void wait_for_kernel(const uint32_t* flag, uint32_t value, uint64_t timeout_ns) {
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 0; i < (1u << 31); ++i) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+        if ((int32_t)(v - value) >= 0) return;
+        if (global_ns() - t0 > timeout_ns) break;
+        if (i > 64) __nanosleep(256);
+    }
+    record_error(kErrTimeout);
+}
+
 constexpr int kMaxSum = 8;
 struct SumPtrs {
     const uint4* src[kMaxSum];
@@ -172,6 +193,16 @@ extern "C" int mllm_wait_u32(const uint32_t* flag, uint32_t value, mllm_stream_t
     if (!flag || !aligned(flag, 4)) return fail(MLLM_ERR_INVALID_ARGUMENT, "wait_u32: bad flag pointer");
     wait_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(flag, value);
     if (int st = check_cuda(cudaGetLastError(), "wait_u32 launch")) return st;
+    return ok();
+}
+
+extern "C" int mllm_wait_u32_timeout(const uint32_t* flag, uint32_t value, uint32_t timeout_us,
+                                     mllm_stream_t stream) {
+    if (!flag || !aligned(flag, 4)) return fail(MLLM_ERR_INVALID_ARGUMENT, "wait_u32_timeout: bad flag pointer");
+    if (timeout_us < 1 || timeout_us > 60u * 1000u * 1000u)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "wait_u32_timeout: timeout must lie in [1 us, 60 s]");
+    wait_for_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(flag, value, (uint64_t)timeout_us * 1000ull);
+    if (int st = check_cuda(cudaGetLastError(), "wait_u32_timeout launch")) return st;
     return ok();
 }
 

@@ -87,6 +87,12 @@ struct PrefillArgs {
     const int32_t* kv_lens;
     int total_q;
     int64_t max_rows;     // cache rows a sequence may address
+    // Grid order.  0: grid (n_mblocks, H, B), each (head, sequence)'s blocks heaviest first,
+    // one (head, sequence) after another, so that a sequence's K/V stays in L2 while its blocks
+    // run.  1: grid (H, B, n_mblocks), the heaviest block of every (head, sequence) before any
+    // lighter one (longest-first over the whole launch), for launches whose K/V fits in L2 anyway
+    // and whose few waves would otherwise end on the heavy blocks of the last heads.
+    int heavy_first;
 };
 
 __device__ __forceinline__ uint32_t col_s(int i) { return (uint32_t)(i * kBN); }
@@ -115,9 +121,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int mb = a.n_mblocks - 1 - (int)blockIdx.x;  // longest (most causal work) blocks first
-    const int h = blockIdx.y;
-    const int b = blockIdx.z;
+    // longest (most causal work) blocks first; see PrefillArgs::heavy_first for the two orders
+    const int mb = a.n_mblocks - 1 - (int)(a.heavy_first ? blockIdx.z : blockIdx.x);
+    const int h = a.heavy_first ? (int)blockIdx.x : (int)blockIdx.y;
+    const int b = a.heavy_first ? (int)blockIdx.y : (int)blockIdx.z;
     const int g = h / a.n_rep;
     const int m0 = mb * (kQTiles * kBM);
     int q_len = a.q_len, kv_len = a.kv_len;
@@ -463,7 +470,13 @@ int prefill_entry(const void* q, const void* k_cache, const void* v_cache, int64
     a.kv_lens = packed.kv_lens;
     a.total_q = packed.total_q;
     a.max_rows = packed.max_rows;
-    dim3 grid(a.n_mblocks, num_heads, batch);
+    // Heavy blocks of all heads first when the launch's K/V (read by every block of a head)
+    // fits in half the L2: then nothing is lost by interleaving the heads, and a launch of few
+    // waves does not end on the heaviest blocks of its last heads.  Packed sequences keep the
+    // per-sequence order (their K/V working sets are large and uneven).
+    const double kv_bytes = 4.0 * batch * num_kv_heads * (double)kv_len * head_dim;
+    a.heavy_first = (!varlen && kv_bytes <= 64.0 * (1 << 20) && a.n_mblocks <= 65535) ? 1 : 0;
+    dim3 grid = a.heavy_first ? dim3(num_heads, batch, a.n_mblocks) : dim3(a.n_mblocks, num_heads, batch);
     cudaStream_t s = (cudaStream_t)stream;
     // The kernel moves registers between warpgroups with setmaxnreg; that is only safe if the
     // compiled kernel launches with the register count the split was sized for (otherwise the

@@ -4,9 +4,12 @@
    LlamaRunner.cpp) with this directory ahead of the reference's own include path, proving
    that the drop-in headers keep every symbol and signature the runners use.  It needs the
    reference tree (build container only) and writes objects under mllm_b200/_build/.
-2. `build_facade_module()` builds tests/facade/mllm_facade*.so, a Python binding of the
-   drop-in headers used by the GPU tests (RMSNorm/Linear/MLP come from the reference tree,
-   unchanged, so this too is built where the reference is present; the .so travels).
+2. `build_runner_module(flavor)` links the same unchanged runners into a Python module, built
+   once on the reference's own runtime headers and once on the drop-in headers, which the GPU
+   tests and the generate benchmark load side by side.
+
+The reference tree is found at $MLLM_REFERENCE_DIR, else in a directory named `reference` beside
+this repository's checkout; where neither exists the recipes are skipped.
 
 The reference tree spells the runner interface header `ImodelRunner.h` but includes it as
 `IModelRunner.h` (works only on case-insensitive file systems), so a one-file shim directory
@@ -23,7 +26,14 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
 ROOT = os.path.dirname(PKG)
 BUILD = os.path.join(PKG, "_build")
-REFERENCE = "/root/reference"
+
+
+def reference_dir() -> str:
+    """The reference tree: $MLLM_REFERENCE_DIR, else `reference` beside the repository."""
+    return os.environ.get("MLLM_REFERENCE_DIR") or os.path.join(os.path.dirname(ROOT), "reference")
+
+
+REFERENCE = reference_dir()
 
 
 def _torch_flags():
@@ -127,23 +137,6 @@ def build_runner_module(flavor: str, reference: str = REFERENCE, verbose: bool =
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(compile_one, srcs))
     cmd = ["g++", "-shared", "-fPIC", *objs, "-o", out, *libs, *extra,
-           "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-lc10", "-lc10_cuda", "-ltorch_python"]
-    if verbose:
-        print(" ".join(cmd), file=sys.stderr)
-    subprocess.run(cmd, check=True)
-    return out
-
-
-def build_facade_module(reference: str = REFERENCE, verbose: bool = False) -> str:
-    from mllm_b200 import build as libbuild
-    lib = libbuild.build()
-    inc, libs, defs = _torch_flags()
-    src = os.path.join(ROOT, "tests", "facade", "facade_binding.cpp")
-    out_dir = os.path.join(ROOT, "tests", "facade")
-    out = os.path.join(out_dir, "mllm_facade" + sysconfig.get_config_var("EXT_SUFFIX"))
-    cmd = ["g++", "-std=c++17", "-O2", "-shared", "-fPIC", "-w", *defs, "-DTORCH_EXTENSION_NAME=mllm_facade",
-           f"-I{sysconfig.get_paths()['include']}", *include_flags(reference), *inc, src, "-o", out, *libs,
-           f"-L{os.path.dirname(lib)}", f"-Wl,-rpath,$ORIGIN/../../mllm_b200/lib", "-lmllm_attn",
            "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-lc10", "-lc10_cuda", "-ltorch_python"]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)

@@ -7,7 +7,9 @@ attention path shards naturally by KV-head group:
     w_q / w_k / w_v   row slices   (the projections of the owned heads)
     QK-norm, RoPE, KV cache, prefill / decode attention   fully local
     w_o               column slice (o_proj of the owned heads' outputs) -> a partial [B, S, hidden]
-  and the partial outputs are summed by ONE all-reduce (NCCL over NVLink on GPUs).
+  and the partial outputs are summed by ONE all-reduce (NCCL over NVLink on GPUs), or -- the
+  same exchange by token rows (SeqParallelOProj) -- the attention rows go to their row's owner,
+  which runs o_proj with the whole w_o, and the output rows are all-gathered.
 
 `attention_fn` computes the local attention block; the default is the B200 path
 (mllm_b200.runtime.attention_block).  The all-reduce uses the given torch.distributed group.
@@ -238,23 +240,88 @@ class PeerExchange:
         self.base = None
 
 
+class SeqParallelOProj:
+    """The o_proj exchange by token rows instead of by partial sums.
+
+    Head sharding leaves rank q with the attention output of its heads for every token,
+    attn_q [T, Hr*D].  The all-reduce form multiplies that by w_o's column slice and sums the N
+    partials [T, hidden] over the ranks: each rank sends and receives about 2 (N-1)/N of the
+    partial (ring), and every output is a sum of N bf16-rounded partials.  This form moves the
+    attention output instead:
+
+      1. all-to-all: the rows of attn_q split into N blocks; block r goes to rank r, so rank r
+         holds rows [r T/N, (r+1) T/N) of every rank's heads, i.e. the full [T/N, H*D] input
+         of o_proj for its rows (the ranks' heads are contiguous and in rank order);
+      2. one GEMM with the whole w_o (replicated, [hidden, H*D]) for those rows, written into
+         this rank's slice of the output;
+      3. all-gather of the slices: every rank ends with the full [T, hidden].
+
+    Per rank that is (N-1)/N of attn_q (Hr*D wide, 1/N of the hidden size) out and in, plus
+    (N-1)/N of the output in: about half the NVLink bytes of the ring all-reduce.  And every
+    output row is ONE full-K GEMM, as on a single GPU, with no bf16 rounding of partials.  The
+    reference's o_proj is that single GEMM (Attention.h:322-325).  T must be a multiple of N.
+    Collectives run on the given torch.distributed group (NCCL), or the all-gather on a
+    `Communicator` when one is given."""
+
+    def __init__(self, rows: int, hidden: int, group=None, comm=None, device=None):
+        import torch
+        import torch.distributed as dist
+        self.group, self.comm = group, comm
+        self.N = dist.get_world_size(group)
+        self.r = dist.get_rank(group)
+        if rows % self.N != 0:
+            raise ValueError(f"SeqParallelOProj: {rows} rows do not split over {self.N} ranks")
+        self.rows, self.hidden = rows, hidden
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+
+    def __call__(self, attn, w_o):
+        """attn [rows, Hr*D] (this rank's heads), w_o [hidden, H*D] (the whole weight): returns
+        attn_all @ w_o.T as [rows, hidden] on every rank."""
+        import torch
+        import torch.distributed as dist
+        N, r, T = self.N, self.r, self.rows
+        Tn, Hd = T // N, attn.shape[1]
+        assert attn.shape[0] == T and w_o.shape == (self.hidden, N * Hd)
+        recv = torch.empty((N, Tn, Hd), dtype=attn.dtype, device=attn.device)
+        dist.all_to_all_single(recv, attn.contiguous(), group=self.group)
+        a = recv.permute(1, 0, 2).reshape(Tn, N * Hd)
+        out = torch.empty((T, self.hidden), dtype=attn.dtype, device=attn.device)
+        mine = out[r * Tn:(r + 1) * Tn]
+        torch.matmul(a, w_o.t(), out=mine)
+        if self.comm is not None:
+            self.comm.all_gather(mine, out)
+        else:
+            dist.all_gather_into_tensor(out, mine, group=self.group)
+        return out
+
+
 def tp_attention_block(h, shard: HeadShard, head_dim: int, rope_theta: float, position_ids, kv_cache,
                        w_q, w_k, w_v, w_o, w_q_norm=None, w_k_norm=None, rms_norm_eps: float = 1e-6,
-                       group=None, attention_fn=None, overlap_chunks: int = 4, exchange=None):
+                       group=None, attention_fn=None, overlap_chunks: int = 4, exchange=None, comm=None):
     """The attention half of TransformerBlock::Forward on this rank's heads, then the o_proj
     all-reduce.  Weights are this rank's slices (shard_weights); kv_cache holds only the owned
     kv heads.  Returns the full [B, S, hidden] attention output on every rank.  On the B200 path
-    (attention_fn None) the o_proj GEMM and the all-reduce are overlapped chunk by chunk
-    (oproj_allreduce), or, with a PeerExchange for this many rows, exchanged over NVLink copy
-    engines; a given attention_fn projects itself and its result is all-reduced whole."""
+    (attention_fn None) the o_proj exchange is, by what the caller passes:
+      - an `exchange` built for this many rows: a PeerExchange (an SM kernel pulls the partials
+        over NVLink peer memory, sums them and pushes the rows back, mllm_sum_bf16) with w_o this
+        rank's column slice, or a SeqParallelOProj with w_o the WHOLE weight;
+      - a `comm` (Communicator): the column-slice GEMM, then one mllm_comm_all_reduce_bf16;
+      - otherwise the GEMM and torch.distributed's all-reduce overlapped chunk by chunk
+        (oproj_allreduce).
+    A given attention_fn projects itself and its result is all-reduced whole."""
     import torch.distributed as dist
     if attention_fn is None:
+        import torch
+
         from .runtime import attention_block
         B, S, _ = h.shape
         attn = attention_block(h, w_q, w_k, w_v, None, shard.num_heads, shard.num_kv_heads, head_dim, rope_theta,
                                position_ids, kv_cache, w_q_norm, w_k_norm, rms_norm_eps)
         if exchange is not None and shard.world > 1 and exchange.rows == B * S:
             return exchange(attn.reshape(B * S, -1), w_o).view(B, S, -1)
+        if comm is not None and shard.world > 1:
+            part = torch.matmul(attn.reshape(B * S, -1), w_o.t())
+            return comm.all_reduce(part).view(B, S, -1)
         return oproj_allreduce(attn.reshape(B * S, -1), w_o, group, overlap_chunks).view(B, S, -1)
     partial = attention_fn(h, w_q, w_k, w_v, w_o, shard.num_heads, shard.num_kv_heads, head_dim, rope_theta,
                            position_ids, kv_cache, w_q_norm, w_k_norm, rms_norm_eps)

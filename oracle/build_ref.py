@@ -10,6 +10,9 @@ installed LibTorch.  The output goes to oracle/_ref/ (git-ignored; it is copied 
 of the working tree to machines that do not have the reference tree).
 
 Usage:  python oracle/build_ref.py [--reference /path/to/mLLM] [--force]
+
+The reference tree defaults to $MLLM_REFERENCE_DIR, else a directory named `reference` beside
+this repository's checkout.
 """
 from __future__ import annotations
 
@@ -22,7 +25,8 @@ import sysconfig
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
 MODULE = "mllm_ref"
-DEFAULT_REFERENCE = "/root/reference"
+DEFAULT_REFERENCE = (os.environ.get("MLLM_REFERENCE_DIR")
+                     or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 
 def output_path() -> str:

@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_status_strings(lib):
-    assert lib.mllm_attn_abi_version() == 5
+    assert lib.mllm_attn_abi_version() == 6
     for code in abi.STATUS_NAMES:
         assert lib.mllm_attn_status_string(code)
     assert lib.mllm_attn_status_string(99) == b"unknown status"

@@ -136,3 +136,39 @@ def test_oproj_allreduce_chunks_equal_the_whole_exchange():
         assert p.exitcode == 0
     for rank, out, ref in res:
         np.testing.assert_allclose(out, ref, rtol=1e-5, atol=1e-4, err_msg=f"rank {rank}")
+
+
+def _seqpar_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        T, E, H, D = 24, 64, 8, 16
+        g = torch.Generator().manual_seed(7)
+        attn_all = torch.randn(T, H * D, generator=g)          # every head's attention rows
+        w_o = torch.randn(E, H * D, generator=g) * 0.1
+        shard = tp.shard_heads(H, H // 2, world, rank)
+        mine = attn_all[:, shard.q_heads[0] * D:shard.q_heads[1] * D].contiguous()
+        ex = tp.SeqParallelOProj(T, E, device=torch.device("cpu"))
+        out = ex(mine, w_o)
+        q.put((rank, out.numpy(), (attn_all @ w_o.t()).numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sequence_parallel_oproj_equals_unsharded():
+    """SeqParallelOProj (all-to-all of the attention rows, full-K o_proj per row block,
+    all-gather): every rank holds the unsharded o_proj output, each row one full-K GEMM."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_seqpar_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r, got, want in res:
+        np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5, err_msg=f"rank {r}")
