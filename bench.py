@@ -655,9 +655,10 @@ def run_gpu(args, rank, world, device):
         rsb, rsh, rst = kr.stride()[:3]
 
         def decode_r():
+            # on torch's current stream: the stream being captured when the layer step is recorded
             st = lib.mllm_decode_attention_bf16(qr.data_ptr(), kr.data_ptr(), vr.data_ptr(), rsb, rsh, rst,
                                                 lens_r.data_ptr(), RAG_B, Hr, Hkvr, D, Lmax, scale, orr.data_ptr(),
-                                                ws_r.data_ptr(), ws_r_bytes, sh)
+                                                ws_r.data_ptr(), ws_r_bytes, torch.cuda.current_stream().cuda_stream)
             assert st == 0, lib.mllm_attn_last_error()
 
         rsteps = max(3, min(args.steps, 50))

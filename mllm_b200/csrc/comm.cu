@@ -14,7 +14,8 @@
 // on every call on it returns MLLM_ERR_COMM (an asynchronous error, or an abort on request) or
 // MLLM_ERR_COMM_TIMEOUT, and the caller rebuilds its communicator.  Set-up and tear-down are
 // bounded by the same deadline.  Collectives enqueued while the stream is being captured into a
-// CUDA graph are not tracked (they run when the graph is launched).
+// CUDA graph are not tracked (they run when the graph is launched), and the watchdog's own
+// queries run in relaxed capture mode, so they never invalidate a graph being recorded.
 #include <nccl.h>
 
 #include <atomic>
@@ -85,6 +86,16 @@ void NcclOps::release(cudaEvent_t e) {
 void NcclOps::abort() {
     if (!c->aborted.exchange(true)) ncclCommAbort(c->nccl);
 }
+
+// Sets the calling thread's stream-capture interaction mode to relaxed for its lifetime: the
+// watchdog queries events, which a thread in the default (global) mode may not do while any
+// thread records a CUDA graph in global mode -- the query would invalidate that recording.  In
+// relaxed mode the query is allowed and the other thread's capture is unaffected.
+struct RelaxedCapture {
+    cudaStreamCaptureMode prev = cudaStreamCaptureModeRelaxed;
+    RelaxedCapture() { cudaThreadExchangeStreamCaptureMode(&prev); }
+    ~RelaxedCapture() { cudaThreadExchangeStreamCaptureMode(&prev); }
+};
 
 int state_status(CommState s) {
     switch (s) {
@@ -199,6 +210,7 @@ extern "C" int mllm_comm_init(const void* id, int nranks, int rank, double timeo
     mllm_comm* raw = c.get();
     c->thread = std::thread([raw] {
         cudaSetDevice(raw->device);
+        RelaxedCapture relaxed;   // never disturbs a graph recorded by another thread
         while (!raw->stop.load()) {
             raw->wd->poll();
             std::this_thread::sleep_for(std::chrono::milliseconds(5));
@@ -230,6 +242,7 @@ extern "C" int mllm_comm_all_gather_bf16(mllm_comm_t comm, const void* send, voi
 
 extern "C" int mllm_comm_status(mllm_comm_t comm) {
     if (!comm) return fail(MLLM_ERR_INVALID_ARGUMENT, "comm_status: null communicator");
+    RelaxedCapture relaxed;
     if (int st = state_status(comm->wd->poll())) return st;
     return ok();
 }

@@ -91,6 +91,35 @@ def test_single_rank_communicator(lib):
         comm.close()
 
 
+def test_watchdog_does_not_disturb_graph_capture(lib):
+    """A collective tracked by the watchdog, then a CUDA graph recorded (torch's default global
+    capture mode) for longer than the watchdog's poll interval: the watchdog's event query runs
+    during the recording and must not invalidate it; the graph then replays the collective."""
+    from mllm_b200.comm import Communicator, unique_id
+    comm = Communicator(0, 1, unique_id(), timeout_s=20.0)
+    try:
+        x = torch.randn(4096, device="cuda").bfloat16()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            comm.all_reduce(x)          # tracked: its event sits in the watchdog's queue
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        y = torch.zeros_like(x)
+        with torch.cuda.graph(g):
+            time.sleep(0.05)            # several watchdog polls happen while recording
+            y.add_(x)
+            comm.all_reduce(y)
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(y, x)
+        assert comm.status() == 0
+        del g
+    finally:
+        comm.close()
+
+
 def _two_rank_worker(rank, port, q):
     import datetime
 
