@@ -540,6 +540,17 @@ def run_gpu(args, rank, world, device):
         torch.cuda.synchronize()
         barrier()
         attn_ms = max_over_ranks(p0.elapsed_time(p1)) / ksteps
+        # the QKV epilogue alone (QK-norm + RoPE + cache append of all 4 x 8192 tokens)
+        barrier()
+        torch.cuda.synchronize()
+        p0.record(stream)
+        for i in range(ksteps):
+            epi_p()
+        p1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        epi_ms = max_over_ranks(p0.elapsed_time(p1)) / ksteps
+        epi_bytes = 2 * qkv_p.numel() * 2   # each head row read once and written once
         varlen = prefill_varlen_leg(args, lib, device, gen, Hr, Hkvr, scale, sh, stream, barrier, max_over_ranks,
                                     ksteps)
         # the layer's exchange step, timed separately (o_proj GEMM, then the all-reduce)
@@ -629,7 +640,7 @@ def run_gpu(args, rank, world, device):
         if world > 1:
             ex_l.close()
         del w_o_full
-        pre = {"layer_ms": layer_ms,
+        pre = {"layer_ms": layer_ms, "epi_ms": epi_ms, "epi_bytes": epi_bytes,
                "varlen": varlen, "peer_ms": peer_ms, "pre_ms": pre_ms, "attn_ms": attn_ms, "steps": ksteps, "oproj_ms": oproj_ms, "overlap_ms": overlap_ms,
                "allreduce_ms": ar_ms if world > 1 else 0.0, "allreduce_bytes": ar_bytes if world > 1 else 0,
                "allreduce_busbw_gbs": (2 * (world - 1) / world * ar_bytes / (ar_ms * 1e-3) / 1e9)
@@ -1286,6 +1297,13 @@ def main():
                          "frac": fl / n / (p["attn_ms"] * 1e-3) / 1e12 / tf_peak, "peak_source": peak_src,
                          "traffic": profile_traffic("prefill_qwen3_8b_b4_s8192")},
             "varlen": p["varlen"]}
+        epi_gbs = p["epi_bytes"] / (p["epi_ms"] * 1e-3) / 1e9
+        line["prefill"]["qkv_epilogue"] = {
+            "ms": p["epi_ms"], "tokens": PRE_B * PRE_S,
+            "roofline": {"bound": "hbm", "kernel": "qkv_epilogue_row_kernel<128>", "achieved": epi_gbs,
+                         "peak": hbm_peak, "unit": "GB/s", "frac": epi_gbs / hbm_peak, "peak_source": peak_src,
+                         "algorithmic_bytes": p["epi_bytes"],
+                         "note": "q/k/v head rows read once, q rows and the K/V cache rows written once"}}
         lm = p["layer_ms"]
         best = min(lm, key=lm.get)
         line["layer"] = {

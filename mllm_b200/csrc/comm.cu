@@ -222,6 +222,7 @@ extern "C" int mllm_comm_init(const void* id, int nranks, int rank, double timeo
 
 extern "C" int mllm_comm_all_reduce_bf16(mllm_comm_t comm, const void* send, void* recv, size_t count,
                                          mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_comm_all_reduce_bf16");
     if (int st = usable(comm)) return st;
     if (count == 0) return ok();
     if (!send || !recv) return fail(MLLM_ERR_INVALID_ARGUMENT, "comm_all_reduce: null buffer");
@@ -232,6 +233,7 @@ extern "C" int mllm_comm_all_reduce_bf16(mllm_comm_t comm, const void* send, voi
 
 extern "C" int mllm_comm_all_gather_bf16(mllm_comm_t comm, const void* send, void* recv, size_t send_count,
                                          mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_comm_all_gather_bf16");
     if (int st = usable(comm)) return st;
     if (send_count == 0) return ok();
     if (!send || !recv) return fail(MLLM_ERR_INVALID_ARGUMENT, "comm_all_gather: null buffer");

@@ -766,6 +766,7 @@ extern "C" int mllm_decode_attention_bf16(const void* q, const void* k_cache, co
                                           const int32_t* kv_lens, int batch, int num_heads, int num_kv_heads,
                                           int head_dim, int max_kv_len, float softmax_scale, void* out,
                                           void* workspace, size_t workspace_bytes, mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_decode_attention_bf16");
     if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_kv_len <= 0)
         return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention: bad sizes");
     if (num_heads % num_kv_heads != 0)
@@ -813,6 +814,7 @@ extern "C" int mllm_decode_attention_paged_bf16(const void* q, const mllm_paged_
                                                 int batch, int num_heads, int num_kv_heads, int head_dim,
                                                 int max_kv_len, float softmax_scale, void* out, void* workspace,
                                                 size_t workspace_bytes, mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_decode_attention_paged_bf16");
     if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_kv_len <= 0)
         return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention: bad sizes");
     if (num_heads % num_kv_heads != 0)
@@ -952,6 +954,7 @@ extern "C" int mllm_decode_attention_noalloc_bf16(const void* q, const void* k_c
                                                   const int32_t* kv_lens, int batch, int num_heads,
                                                   int num_kv_heads, int head_dim, int max_kv_len,
                                                   float softmax_scale, void* out, mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_decode_attention_noalloc_bf16");
     if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_kv_len <= 0)
         return fail(MLLM_ERR_INVALID_ARGUMENT, "decode_attention_noalloc: bad sizes");
     if (num_heads % num_kv_heads != 0)
@@ -1104,6 +1107,7 @@ extern "C" int mllm_decode_step_bf16(const void* q, int64_t q_sb, int64_t q_sh, 
                                      int64_t cache_st, const int32_t* kv_lens, int batch, int num_heads,
                                      int num_kv_heads, int head_dim, int max_kv_len, float softmax_scale, void* out,
                                      void* workspace, size_t workspace_bytes, mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_decode_step_bf16");
     return decode_step_entry(q, q_sb, q_sh, k, k_sb, k_sh, v, v_sb, v_sh, positions, pos_sb, rope_theta, rope_cos,
                              rope_sin, rope_row_sb, q_norm_weight, k_norm_weight, rms_norm_eps, k_cache, v_cache,
                              cache_sb, cache_sh, cache_st, max_kv_len, batch, KvLayout{}, kv_lens, batch, num_heads,
@@ -1120,6 +1124,7 @@ extern "C" int mllm_decode_step_paged_bf16(const void* q, int64_t q_sb, int64_t 
                                            int batch, int num_heads, int num_kv_heads, int head_dim, int max_kv_len,
                                            float softmax_scale, void* out, void* workspace, size_t workspace_bytes,
                                            mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_decode_step_paged_bf16");
     KvLayout lay;
     if (int st = paged_layout(kv, max_kv_len, head_dim, "decode_step_paged", &lay)) return st;
     return decode_step_entry(q, q_sb, q_sh, k, k_sb, k_sh, v, v_sb, v_sh, positions, pos_sb, rope_theta, rope_cos,

@@ -4,6 +4,7 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 #include <stdint.h>
 
 #include <string>
@@ -42,6 +43,16 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
 }
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// An NVTX range around a host call (the launch side of an entry point), visible to Nsight and
+// ncu's NVTX filters.  Header-only NVTX3: without a profiler attached it costs a pointer check.
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
+#define MLLM_NVTX_RANGE(name) ::mllm_b200::NvtxRange mllm_nvtx_range_(name)
 
 // Per-translation-unit device status readers (see MLLM_DEFINE_STATUS_READER).
 int read_clear_status_decode(cudaStream_t s, unsigned* out);

@@ -358,6 +358,7 @@ extern "C" int mllm_linear_bf16(const void* x, int64_t x_stride, int tokens, int
                                 const void* const* weights, const int64_t* weight_strides,
                                 const int64_t* out_features, void* out, int64_t out_stride, void* workspace,
                                 size_t workspace_bytes, mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_linear_bf16");
     int64_t total = 0;
     if (!weights) return fail(MLLM_ERR_INVALID_ARGUMENT, "linear: weights must be given");
     if (int st = check_linear_args(tokens, in_features, num_weights, weights, weight_strides, out_features, &total))

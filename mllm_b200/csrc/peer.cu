@@ -208,6 +208,7 @@ extern "C" int mllm_wait_u32_timeout(const uint32_t* flag, uint32_t value, uint3
 
 extern "C" int mllm_sum_bf16(void* const* dsts, int n_dst, const void* const* srcs, int n_src, int64_t count,
                              mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_sum_bf16");
     if (n_src < 1 || n_src > kMaxSum || n_dst < 1 || n_dst > kMaxSum || count < 0 || (count % 8) != 0)
         return fail(MLLM_ERR_INVALID_ARGUMENT, "sum_bf16: 1..8 sources and destinations, count a multiple of 8");
     if (count == 0) return ok();

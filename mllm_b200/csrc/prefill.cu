@@ -521,6 +521,7 @@ extern "C" int mllm_prefill_attention_bf16(const void* q, const void* k_cache, c
                                            int64_t cache_sh, int64_t cache_st, int batch, int num_heads,
                                            int num_kv_heads, int head_dim, int q_len, int kv_len, float softmax_scale,
                                            void* out, mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_prefill_attention_bf16");
     // the K/V maps stop at kv_len: rows past it read as zero
     return prefill_entry(q, k_cache, v_cache, cache_sb, cache_sh, cache_st, kv_len, batch, KvLayout{}, batch,
                          num_heads, num_kv_heads, head_dim, q_len, kv_len, softmax_scale, out, stream);
@@ -529,6 +530,7 @@ extern "C" int mllm_prefill_attention_bf16(const void* q, const void* k_cache, c
 extern "C" int mllm_prefill_attention_paged_bf16(const void* q, const mllm_paged_kv* kv, int batch, int num_heads,
                                                  int num_kv_heads, int head_dim, int q_len, int kv_len,
                                                  float softmax_scale, void* out, mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_prefill_attention_paged_bf16");
     KvLayout lay;
     if (int st = paged_layout(kv, kv_len, head_dim, "prefill_attention_paged", &lay)) return st;
     return prefill_entry(q, kv->k_pool, kv->v_pool, kv->block_stride, kv->head_stride, kv->row_stride,
@@ -542,6 +544,7 @@ extern "C" int mllm_prefill_attention_varlen_bf16(const void* q, const void* k_c
                                                   const int32_t* kv_lens, int batch, int num_heads, int num_kv_heads,
                                                   int head_dim, int total_q, int max_q_len, float softmax_scale,
                                                   void* out, mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_prefill_attention_varlen_bf16");
     if (cu_q_lens == nullptr) return fail(MLLM_ERR_INVALID_ARGUMENT, "prefill_attention_varlen: cu_q_lens is NULL");
     if (cache_capacity <= 0 || cache_capacity > 0x7fffffffLL)
         return fail(MLLM_ERR_INVALID_ARGUMENT, "prefill_attention_varlen: bad cache_capacity");
@@ -559,6 +562,7 @@ extern "C" int mllm_prefill_attention_varlen_paged_bf16(const void* q, const mll
                                                         int num_heads, int num_kv_heads, int head_dim, int total_q,
                                                         int max_q_len, float softmax_scale, void* out,
                                                         mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_prefill_attention_varlen_paged_bf16");
     if (cu_q_lens == nullptr) return fail(MLLM_ERR_INVALID_ARGUMENT, "prefill_attention_varlen: cu_q_lens is NULL");
     KvLayout lay;
     if (int st = paged_layout(kv, 0, head_dim, "prefill_attention_varlen_paged", &lay)) return st;

@@ -10,6 +10,8 @@
 // shared with the fused decode step.
 //
 // Memory: each head row is read once (D*2 bytes) and written once (q_out or the cache row).
+#include <algorithm>
+
 #include "common.cuh"
 #include "host_util.h"
 #include "kv_layout.cuh"
@@ -221,6 +223,9 @@ __global__ void __launch_bounds__(256, (D == 128 && RPQ >= 4) ? 2 : 3) qkv_epilo
     const int lane = tid & 31;
     const int j = lane & 7;
     const int qbase = lane & ~7;
+    // the 8 lanes of this quarter-warp: the quarter-warps of a warp may take different branches
+    // (a v row, a row past the last head), so the norm's exchange names only its own lanes
+    const unsigned qmask = 0xFFu << qbase;
     const int qw = tid >> 3;
     const int tl = qw / kQwPerTok;          // token of this quarter-warp within the block
     const int hq = qw % kQwPerTok;          // its rows: heads hq + kQwPerTok * t
@@ -303,7 +308,7 @@ __global__ void __launch_bounds__(256, (D == 128 && RPQ >= 4) ? 2 : 3) qkv_epilo
                 }
                 float total = 0.f;
 #pragma unroll
-                for (int jj = 0; jj < 8; ++jj) total = __fadd_rn(total, __shfl_sync(0xffffffffu, acc, qbase + jj));
+                for (int jj = 0; jj < 8; ++jj) total = __fadd_rn(total, __shfl_sync(qmask, acc, qbase + jj));
                 const float rr = rms_scale<D>(total, a.eps);
                 const float* gw = s_gamma[r.kind];
 #pragma unroll
@@ -335,6 +340,215 @@ __global__ void __launch_bounds__(256, (D == 128 && RPQ >= 4) ? 2 : 3) qkv_epilo
         }
 #pragma unroll
         for (int m = 0; m < NE; ++m) dst[j + 8 * m] = y[m];
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Many tokens, a thread per head row: each thread brings its whole row into registers with
+// 16-byte loads (D/8 of them), norms and rotates it there and writes it with 16-byte stores.
+//
+// One thread per row keeps the reference's reduction entirely in registers: element d of the row
+// belongs to accumulator P_k[j] with j = d % 8, k = (d / 8) % 4, visited in order of d / 32, then
+// acc_j = ((P0 + P1) + P2) + P3 and the total sums acc_0 .. acc_7 in order -- the order of the
+// quarter-warp and warp kernels (qkv_math.cuh), with no exchange between lanes.  Every fp32 step
+// is the same explicitly rounded operation (the two scaling products of the norm as one f32x2
+// instruction: a product feeding a product, nothing to contract), so the outputs are
+// bit-identical to theirs.
+//
+// A block takes kRowTokens consecutive tokens: their RoPE angles are computed once (position-
+// independent factors once per block) into shared memory, then thread t takes rows t, t + 256, ...
+// of the block's tokens x heads (three per thread for the Qwen3-8B geometry).  Preconditions
+// (checked on the host): every row 16-byte aligned.
+// ---------------------------------------------------------------------------------------------
+constexpr int kRowTokens = 16;
+constexpr int kRowThreads = 256;
+
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        f[2 * i] = __uint_as_float(w[i] << 16);
+        f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+    uint4 v;
+    v.x = pack_bf16x2(f[0], f[1]);
+    v.y = pack_bf16x2(f[2], f[3]);
+    v.z = pack_bf16x2(f[4], f[5]);
+    v.w = pack_bf16x2(f[6], f[7]);
+    return v;
+}
+
+// 8 consecutive fp32 from 16-byte aligned shared memory
+__device__ __forceinline__ void load8f(const float* p, float (&f)[8]) {
+    const float4 u = reinterpret_cast<const float4*>(p)[0];
+    const float4 w = reinterpret_cast<const float4*>(p)[1];
+    f[0] = u.x; f[1] = u.y; f[2] = u.z; f[3] = u.w;
+    f[4] = w.x; f[5] = w.y; f[6] = w.z; f[7] = w.w;
+}
+
+// (d0, d1) = (a0 * b0, a1 * b1), each product rounded to nearest (one f32x2 instruction)
+__device__ __forceinline__ void mul2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+    unsigned long long a, b, d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(b0), "f"(b1));
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
+}
+
+// both values rounded to bf16 precision (round to nearest even) and widened back, exactly as
+// __bfloat162float(__float2bfloat16_rn(x)) does for each
+__device__ __forceinline__ void round_bf16x2(float& x0, float& x1) {
+    const uint32_t w = pack_bf16x2(x0, x1);
+    x0 = __uint_as_float(w << 16);
+    x1 = __uint_as_float(w & 0xffff0000u);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kRowThreads, 2) qkv_epilogue_row_kernel(EpilogueArgs a, int ntok) {
+    constexpr int NC = D / 8;            // 16-byte chunks per row
+    constexpr int AS = 2 * D + 4;        // floats per token in the angle table (cos, sin, pad)
+    __shared__ __align__(16) float s_ang[kRowTokens * AS];
+    __shared__ __align__(16) float s_gamma[2 * D];
+    __shared__ float s_inv_freq[D / 2];
+
+    pdl_trigger();   // a decode launched next may start its set-up (it waits for this grid)
+    const int tid = threadIdx.x;
+    const int th = a.H + 2 * a.Hkv;
+    const int t0 = blockIdx.x * kRowTokens;
+    const int nt = min(kRowTokens, ntok - t0);
+    const bool norm = a.q_gamma != nullptr;
+    const bool tables = a.rope_cos != nullptr;
+
+    if (norm) {
+        for (int d = tid; d < D; d += kRowThreads) {
+            s_gamma[d] = __bfloat162float(a.q_gamma[d]);
+            s_gamma[D + d] = __bfloat162float(a.k_gamma[d]);
+        }
+    }
+    if (!tables) {
+        for (int jc = tid; jc < D / 2; jc += kRowThreads) s_inv_freq[jc] = rope_angle(1, jc, D, a.log_theta);
+    }
+    __syncthreads();
+    if (tables) {
+        for (int idx = tid; idx < nt * D; idx += kRowThreads) {
+            const int tl = idx / D, col = idx - tl * D;
+            const int token = t0 + tl;
+            const int b = token / a.S, s = token - b * a.S;
+            const int64_t row = (int64_t)b * a.rope_row_sb + (int64_t)s * a.rope_row_ss;
+            s_ang[tl * AS + col] = a.rope_cos[row * D + col];
+            s_ang[tl * AS + D + col] = a.rope_sin[row * D + col];
+        }
+    } else {
+        // rope_angle: float(pos) * inv_freq[col], then cos / sin, for the first half only (the
+        // second half of a computed table equals the first)
+        for (int idx = tid; idx < nt * (D / 2); idx += kRowThreads) {
+            const int tl = idx / (D / 2), col = idx - tl * (D / 2);
+            const int token = t0 + tl;
+            const int b = token / a.S, s = token - b * a.S;
+            const float angle =
+                __fmul_rn((float)a.positions[(int64_t)b * a.pos_sb + (int64_t)s * a.pos_ss], s_inv_freq[col]);
+            s_ang[tl * AS + col] = cosf(angle);
+            s_ang[tl * AS + D + col] = sinf(angle);
+        }
+    }
+    __syncthreads();
+
+    const int rows = nt * th;
+#pragma unroll 1
+    for (int r = tid; r < rows; r += kRowThreads) {
+        const int tl = r / th, head = r - tl * th;
+        const int token = t0 + tl;
+        const int b = token / a.S, s = token - b * a.S;
+        const HeadRef hr = locate_head(a, head, b, s);
+        __nv_bfloat16* dst;
+        if (hr.kind == 0) {
+            dst = a.q_out + (((int64_t)b * a.H + hr.h) * a.S + s) * D;
+        } else {
+            int seq, blk, rw;
+            const int64_t slot = cache_slot(a, b, s, seq);
+            if (slot < 0 || slot >= a.capacity || !kv_locate(a.lay, seq, slot, blk, rw)) {
+                record_error(kErrBadLength);
+                continue;
+            }
+            dst = (hr.kind == 1 ? a.k_cache : a.v_cache) + blk * a.c_sb + hr.h * a.c_sh + rw * a.c_st;
+        }
+        const uint4* src = reinterpret_cast<const uint4*>(hr.src);
+        uint4* out = reinterpret_cast<uint4*>(dst);
+        uint4 v[NC];
+#pragma unroll
+        for (int c = 0; c < NC; ++c) v[c] = src[c];
+        if (hr.kind == 2) {
+#pragma unroll
+            for (int c = 0; c < NC; ++c) out[c] = v[c];
+            continue;
+        }
+        float rr_scale = 1.f;
+        if (norm) {
+            // P_k[j] over the row's chunks c (k = c % 4) in order of c / 4
+            float p[4][8];
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                float x[8];
+                unpack8(v[c], x);
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                    const float sq = __fmul_rn(x[jj], x[jj]);
+                    p[c & 3][jj] = c < 4 ? sq : __fadd_rn(p[c & 3][jj], sq);
+                }
+            }
+            float total = 0.f;
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj)
+                total = __fadd_rn(total, __fadd_rn(__fadd_rn(__fadd_rn(p[0][jj], p[1][jj]), p[2][jj]), p[3][jj]));
+            rr_scale = rms_scale<D>(total, a.eps);
+        }
+        const float* gw = s_gamma + (hr.kind == 0 ? 0 : D);
+        const float* cs = s_ang + tl * AS;
+        const float* sn = cs + D;
+        // RoPE.h:77-88 on the pairs (d, d + D/2): chunks c and c + NC/2
+#pragma unroll
+        for (int c = 0; c < NC / 2; ++c) {
+            float xl[8], xh[8];
+            unpack8(v[c], xl);
+            unpack8(v[c + NC / 2], xh);
+            if (norm) {
+                // RMSNorm.h:48-63: x * rsqrt(var + eps) * w, cast to bf16
+                float gl[8], gh[8];
+                load8f(gw + 8 * c, gl);
+                load8f(gw + 8 * c + D / 2, gh);
+#pragma unroll
+                for (int jj = 0; jj < 8; jj += 2) {
+                    mul2(xl[jj], xl[jj + 1], xl[jj], xl[jj + 1], rr_scale, rr_scale);
+                    mul2(xl[jj], xl[jj + 1], xl[jj], xl[jj + 1], gl[jj], gl[jj + 1]);
+                    mul2(xh[jj], xh[jj + 1], xh[jj], xh[jj + 1], rr_scale, rr_scale);
+                    mul2(xh[jj], xh[jj + 1], xh[jj], xh[jj + 1], gh[jj], gh[jj + 1]);
+                    round_bf16x2(xl[jj], xl[jj + 1]);
+                    round_bf16x2(xh[jj], xh[jj + 1]);
+                }
+            }
+            float cl[8], sl[8], ch[8], sh[8];
+            load8f(cs + 8 * c, cl);
+            load8f(sn + 8 * c, sl);
+            if (tables) {
+                load8f(cs + 8 * c + D / 2, ch);
+                load8f(sn + 8 * c + D / 2, sh);
+            } else {
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                    ch[jj] = cl[jj];
+                    sh[jj] = sl[jj];
+                }
+            }
+            float lo[8], hi[8];
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj)
+                rope_rotate_pair(xl[jj], xh[jj], cl[jj], sl[jj], ch[jj], sh[jj], lo[jj], hi[jj]);
+            out[c] = pack8(lo);
+            out[c + NC / 2] = pack8(hi);
+        }
     }
 }
 
@@ -410,6 +624,20 @@ int epilogue_entry(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh, cons
     const int total_heads = num_heads + 2 * num_kv_heads;
     const int64_t tokens = (int64_t)batch * seq_len;
     cudaStream_t st = (cudaStream_t)stream;
+    // Many tokens, every row 16-byte aligned: a thread per head row.
+    if (tokens >= 1024) {
+        bool al = aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(q_out, 16) && aligned(k_cache, 16) &&
+                  aligned(v_cache, 16);
+        for (int64_t st8 : {q_sb, q_ss, q_sh, k_sb, k_ss, k_sh, v_sb, v_ss, v_sh, cache_sb, cache_sh, cache_st})
+            al = al && (st8 % 8 == 0);
+        if (al) {
+            const unsigned blocks = (unsigned)((tokens + kRowTokens - 1) / kRowTokens);
+            if (head_dim == 128) qkv_epilogue_row_kernel<128><<<blocks, kRowThreads, 0, st>>>(a, (int)tokens);
+            else qkv_epilogue_row_kernel<64><<<blocks, kRowThreads, 0, st>>>(a, (int)tokens);
+            if (int e = check_cuda(cudaGetLastError(), "qkv_epilogue launch")) return e;
+            return ok();
+        }
+    }
     // Many tokens: the quarter-warp kernel (rows per quarter-warp = ceil(heads / 16)).
     const int rpq = (total_heads + 15) / 16;
     if (tokens >= 1024 && rpq <= 4) {
@@ -457,6 +685,7 @@ extern "C" int mllm_qkv_epilogue_bf16(const void* q, int64_t q_sb, int64_t q_ss,
                                       int64_t cache_sb, int64_t cache_sh, int64_t cache_st, int64_t cache_capacity,
                                       const int32_t* cache_start, int64_t uniform_cache_start,
                                       mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_qkv_epilogue_bf16");
     return epilogue_entry(q, q_sb, q_ss, q_sh, k, k_sb, k_ss, k_sh, v, v_sb, v_ss, v_sh, batch, seq_len, num_heads,
                           num_kv_heads, head_dim, positions, pos_sb, pos_ss, rope_theta, rope_cos, rope_sin,
                           rope_row_sb, rope_row_ss, q_norm_weight, k_norm_weight, rms_norm_eps, q_out, k_cache,
@@ -474,6 +703,7 @@ extern "C" int mllm_qkv_epilogue_paged_bf16(const void* q, int64_t q_sb, int64_t
                                             const void* k_norm_weight, double rms_norm_eps, void* q_out,
                                             const mllm_paged_kv* kv, const int32_t* cache_start,
                                             int64_t uniform_cache_start, mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_qkv_epilogue_paged_bf16");
     KvLayout lay;
     if (int st = paged_layout(kv, 0, head_dim, "qkv_epilogue_paged", &lay)) return st;
     return epilogue_entry(q, q_sb, q_ss, q_sh, k, k_sb, k_ss, k_sh, v, v_sb, v_ss, v_sh, batch, seq_len, num_heads,
@@ -501,6 +731,7 @@ extern "C" int mllm_qkv_epilogue_varlen_bf16(const void* q, int64_t q_st, int64_
                                              void* k_cache, void* v_cache, int64_t cache_sb, int64_t cache_sh,
                                              int64_t cache_st, int64_t cache_capacity, const int32_t* cu_seqlens,
                                              int batch, const int32_t* cache_start, mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_qkv_epilogue_varlen_bf16");
     if (int st = varlen_checks(total_tokens, positions, cu_seqlens, batch)) return st;
     return epilogue_entry(q, 0, q_st, q_sh, k, 0, k_st, k_sh, v, 0, v_st, v_sh, 1, total_tokens, num_heads,
                           num_kv_heads, head_dim, positions, 0, 1, rope_theta, nullptr, nullptr, 0, 0, q_norm_weight,
@@ -516,6 +747,7 @@ extern "C" int mllm_qkv_epilogue_varlen_paged_bf16(const void* q, int64_t q_st, 
                                                    double rms_norm_eps, void* q_out, const mllm_paged_kv* kv,
                                                    const int32_t* cu_seqlens, int batch, const int32_t* cache_start,
                                                    mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_qkv_epilogue_varlen_paged_bf16");
     if (int st = varlen_checks(total_tokens, positions, cu_seqlens, batch)) return st;
     KvLayout lay;
     if (int st = paged_layout(kv, 0, head_dim, "qkv_epilogue_varlen_paged", &lay)) return st;

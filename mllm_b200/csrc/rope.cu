@@ -73,6 +73,7 @@ using namespace mllm_b200;
 
 extern "C" int mllm_rope_build_cos_sin(const int64_t* positions, int64_t n, int head_dim, double rope_theta,
                                        float* cos_out, float* sin_out, mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_rope_build_cos_sin");
     if (head_dim <= 0 || head_dim % 2 != 0) return fail(MLLM_ERR_INVALID_ARGUMENT, "RoPE: head_dim must be even.");
     if (n < 0) return fail(MLLM_ERR_INVALID_ARGUMENT, "RoPE: negative position count");
     if (!(rope_theta > 0.0)) return fail(MLLM_ERR_INVALID_ARGUMENT, "RoPE: rope_theta must be positive");
@@ -89,6 +90,7 @@ extern "C" int mllm_rope_build_cos_sin(const int64_t* positions, int64_t n, int 
 extern "C" int mllm_rope_apply_bf16(const void* x, int64_t sb, int64_t sh, int64_t ss, int batch, int num_heads,
                                     int seq_len, int head_dim, const float* cos, const float* sin, void* out,
                                     mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_rope_apply_bf16");
     if (head_dim <= 0 || head_dim % 2 != 0) return fail(MLLM_ERR_INVALID_ARGUMENT, "RoPE: head_dim must be even.");
     if (batch < 0 || num_heads < 0 || seq_len < 0) return fail(MLLM_ERR_INVALID_ARGUMENT, "RoPE: negative size");
     const int64_t total = (int64_t)batch * num_heads * seq_len;

@@ -248,6 +248,7 @@ extern "C" int mllm_sample(void* logits, int logits_bf16, int64_t row_stride, in
                            float temperature, int top_k, float top_p, int use_greedy, float repetition_penalty,
                            uint64_t seed, uint64_t offset, int64_t* out_tokens, void* workspace,
                            size_t workspace_bytes, mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_sample");
     // the reference's checks (Sampler.cpp:59-81)
     if (vocab <= 0) return fail(MLLM_ERR_INVALID_ARGUMENT, "Sampler received empty logits.");
     if (!std::isfinite(temperature)) return fail(MLLM_ERR_INVALID_ARGUMENT, "Sampler temperature must be finite.");

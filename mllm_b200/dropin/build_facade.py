@@ -113,6 +113,7 @@ def build_runner_module(flavor: str, reference: str = REFERENCE, verbose: bool =
         lib = libbuild.build()
         incs = include_flags(reference)
         extra = [f"-L{os.path.dirname(lib)}", "-Wl,-rpath,$ORIGIN/../../mllm_b200/lib", "-lmllm_attn"]
+        defs = defs + ["-DMLLM_DROPIN"]
     else:
         incs = [f"-I{_shim(reference)}", f"-I{os.path.join(reference, 'src')}",
                 f"-I{os.path.join(reference, 'external')}"]

@@ -13,6 +13,10 @@
 // The projections stay LibTorch GEMMs (Linear::Forward), as in the reference, except that up to
 // 256 tokens q/k/v come from one mllm_linear_bf16 launch (b200::ProjectQKV).
 //
+// Host tensors (a runner that keeps its weights on the host, as LlamaRunner does) are staged on
+// the current CUDA device -- weights once, activations per call -- and the result returns to the
+// host; the computation itself is the same device path.
+//
 // ForwardProjectedNormed is the one addition: it takes the per-head q/k RMSNorm weights that
 // the reference applies in TransformerBlock.h:103-134 and fuses that norm into the epilogue.
 #pragma once
@@ -49,6 +53,16 @@ namespace mllm
             {
                 throw std::runtime_error("Attention: hidden must be [B, S, H].");
             }
+            if (!hidden.is_cuda())
+            {
+                // host tensors (a runner that keeps its weights on the host): computed on the
+                // device, returned on the host
+                const torch::Device dev = b200::ComputeDevice("Attention");
+                return Forward(b200::StageActivation(hidden, dev), b200::StageWeight(w_q, dev),
+                               b200::StageWeight(w_k, dev), b200::StageWeight(w_v, dev), b200::StageWeight(w_o, dev),
+                               num_heads, num_kv_heads, head_dim, rope_theta, position_ids.to(dev), kv_cache)
+                    .to(hidden.device(), hidden.scalar_type());
+            }
             const auto B = hidden.size(0);
             const auto S = hidden.size(1);
             // [B, S, h*D] -> [B, h, S, D] views; the epilogue reads them through their strides.
@@ -75,6 +89,15 @@ namespace mllm
             const torch::Tensor& position_ids,
             KVCache* kv_cache)
         {
+            if (q.defined() && !q.is_cuda())
+            {
+                const torch::Device dev = b200::ComputeDevice("Attention");
+                return ForwardProjectedNormed(b200::StageActivation(q, dev), b200::StageActivation(k, dev),
+                                              b200::StageActivation(v, dev), b200::StageWeight(w_o, dev), num_heads,
+                                              num_kv_heads, head_dim, rope_theta, position_ids.to(dev), kv_cache,
+                                              torch::Tensor(), torch::Tensor(), 0.0)
+                    .to(q.device(), q.scalar_type());
+            }
             return ForwardProjectedNormed(q, k, v, w_o, num_heads, num_kv_heads, head_dim, rope_theta,
                                           position_ids, kv_cache, torch::Tensor(), torch::Tensor(), 0.0);
         }

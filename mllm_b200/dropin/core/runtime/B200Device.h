@@ -6,10 +6,14 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <torch/torch.h>
 
+#include <c10/cuda/CUDAFunctions.h>
+
 #include <cstdint>
 #include <cstdlib>
 #include <stdexcept>
 #include <string>
+#include <functional>
+#include <unordered_map>
 
 #include "mllm_attn.h"
 
@@ -50,6 +54,133 @@ namespace mllm
         {
             const char* v = std::getenv("MLLM_B200_DECODE_GRAPHS");
             return v != nullptr && v[0] == '1' && v[1] == '\0';
+        }
+
+        // ---- Host tensors ----
+        // A runner may keep its weights and activations on the host: the reference's LlamaRunner
+        // never moves them to CUDA (LlamaRunner.cpp:111-187, 189-281).  The drop-in then stages
+        // them on the current CUDA device -- each weight once, the activations per call -- runs
+        // the layer there, and hands the result back on the host.  The work itself never runs on
+        // the CPU.
+
+        // The current CUDA device; there is no CPU path to fall back to.
+        inline torch::Device ComputeDevice(const char* who)
+        {
+            if (!torch::cuda::is_available())
+            {
+                throw std::runtime_error(std::string(who) + ": the B200 attention path needs a CUDA device.");
+            }
+            return torch::Device(torch::kCUDA, c10::cuda::current_device());
+        }
+
+        // Device copy (bf16, contiguous) of a host weight, made on first use and kept while the
+        // weight lives unchanged.  The cache holds a reference to the host tensor, so its address
+        // cannot be reused by another tensor while it is cached, and re-stages the weight when its
+        // version counter has moved (an in-place write since).  CUDA tensors pass through.
+        inline torch::Tensor StageWeight(const torch::Tensor& w, const torch::Device& dev)
+        {
+            if (!w.defined() || w.is_cuda())
+            {
+                return w;
+            }
+            struct Entry
+            {
+                torch::Tensor host;
+                int64_t version;
+                torch::Tensor device;
+            };
+            thread_local std::unordered_map<const void*, Entry> cache;
+            const void* key = w.unsafeGetTensorImpl();
+            auto it = cache.find(key);
+            if (it != cache.end() && it->second.version == (int64_t)w._version() && it->second.device.device() == dev)
+            {
+                return it->second.device;
+            }
+            torch::Tensor d = w.to(dev, torch::kBFloat16).contiguous();
+            cache[key] = Entry{w, (int64_t)w._version(), d};
+            return d;
+        }
+
+        // An activation on the compute device in bf16 (a copy when it lives on the host).
+        inline torch::Tensor StageActivation(const torch::Tensor& x, const torch::Device& dev)
+        {
+            if (!x.defined() || (x.is_cuda() && x.scalar_type() == torch::kBFloat16))
+            {
+                return x;
+            }
+            return x.to(dev, torch::kBFloat16);
+        }
+
+        // ---- Tensor parallelism (no counterpart in the reference, which runs on one device) ----
+        // With a communicator set, TransformerBlock::Forward runs only this rank's KV-head group:
+        // kv heads [rank*Hkv/world, (rank+1)*Hkv/world) and their query heads, with the row slices
+        // of w_q/w_k/w_v and the column slice of w_o (cut once per weight and cached), a KV cache
+        // that holds those kv heads only, and the o_proj partial summed over the ranks by
+        // mllm_comm_all_reduce_bf16 on the current stream.  Every rank runs the same runner on the
+        // same inputs (one process per GPU); norms, MLP, embeddings and lm_head are replicated.
+        // The caller owns the communicator (mllm_comm_init) and clears the setting before it
+        // destroys it.
+        struct TensorParallel
+        {
+            mllm_comm_t comm = nullptr;
+            int rank = 0;
+            int world = 1;
+        };
+
+        inline TensorParallel& ActiveTensorParallel()
+        {
+            static TensorParallel tp;
+            return tp;
+        }
+
+        // world == 1 (or comm == nullptr) turns tensor parallelism off.
+        inline void SetTensorParallel(mllm_comm_t comm, int rank, int world)
+        {
+            if (world < 1 || rank < 0 || rank >= world || (world > 1 && comm == nullptr))
+            {
+                throw std::runtime_error("TensorParallel: bad rank / world / communicator");
+            }
+            ActiveTensorParallel() = world > 1 ? TensorParallel{comm, rank, world} : TensorParallel{};
+        }
+
+        // Rows [r0, r1) (dim 0) or columns (dim 1) of a weight, contiguous, cut once and cached
+        // (the cache holds the source, so its address stays unique while cached).
+        inline torch::Tensor ShardWeight(const torch::Tensor& w, int dim, int64_t r0, int64_t r1)
+        {
+            if (!w.defined())
+            {
+                return w;
+            }
+            struct Key
+            {
+                const void* impl;
+                int dim;
+                int64_t r0, r1;
+                bool operator==(const Key& o) const { return impl == o.impl && dim == o.dim && r0 == o.r0 && r1 == o.r1; }
+            };
+            struct KeyHash
+            {
+                size_t operator()(const Key& k) const
+                {
+                    return std::hash<const void*>()(k.impl) ^ (std::hash<int64_t>()(k.r0 * 31 + k.r1) << 1) ^ k.dim;
+                }
+            };
+            struct Entry
+            {
+                torch::Tensor source;
+                int64_t version;
+                torch::Tensor shard;
+            };
+            thread_local std::unordered_map<Key, Entry, KeyHash> cache;
+            const Key key{w.unsafeGetTensorImpl(), dim, r0, r1};
+            auto it = cache.find(key);
+            if (it != cache.end() && it->second.version == (int64_t)w._version())
+            {
+                return it->second.shard;
+            }
+            torch::Tensor s = w.narrow(dim, r0, r1 - r0).contiguous();
+            cache[key] = Entry{w, (int64_t)w._version(), s};
+            return s;
         }
 
         // Converts a nonzero mllm_status into std::runtime_error, the reference's convention.

@@ -6,6 +6,7 @@
 // repetition penalty is applied in place as the reference does (Sampler.cpp:12-46) but without
 // its device sync per previous token, then the greedy argmax or the top-k / top-p draw.  Per
 // call that is one copy of the history to the device and one read of the token back.
+// Host logits are copied to the current CUDA device and sampled there.
 // Header-only: link it instead of the reference's Sampler.cpp.
 #pragma once
 
@@ -50,7 +51,18 @@ namespace mllm
             }
             if (!logits.is_cuda())
             {
-                throw std::runtime_error("Sampler: the B200 build samples CUDA logits only (no CPU path).");
+                // host logits (LlamaRunner keeps its lm_head on the host): sampled on the device;
+                // the repetition penalty's in-place writes are copied back, as the reference
+                // leaves them in its argument (Sampler.cpp:12-46)
+                const torch::Device dev = b200::ComputeDevice("Sampler");
+                torch::Tensor d = logits.to(dev).contiguous();
+                const int64_t token =
+                    Sample(d, temperature, top_k, top_p, use_greedy, previous_tokens, repetition_penalty);
+                if (repetition_penalty > 1.0f && !previous_tokens.empty())
+                {
+                    logits.copy_(d);
+                }
+                return token;
             }
             if (logits.scalar_type() != torch::kBFloat16 && logits.scalar_type() != torch::kFloat32)
             {

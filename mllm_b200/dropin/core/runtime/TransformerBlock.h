@@ -10,6 +10,13 @@
 // to 256 tokens the three GEMMs are one mllm_linear_bf16 launch (b200::ProjectQKV).
 // RMSNorm, Linear and MLP are the reference's own headers, unchanged.
 //
+// A runner that keeps its weights on the host (LlamaRunner) is served on the GPU all the same:
+// the layer's weights are staged on the device once and the hidden state per call (FromHost).
+//
+// With b200::SetTensorParallel (one process per GPU, a communicator from mllm_comm_init), each
+// rank runs its KV-head group of the attention and the o_proj partials are all-reduced
+// (HeadSharded); the unchanged runners drive it exactly as they drive one GPU.
+//
 // With MLLM_B200_DECODE_GRAPHS=1, decode steps (one new token per sequence over an initialized
 // cache) replay a CUDA graph of the whole layer once its inputs are stable: the runners launch
 // every layer's few dozen kernels from the host each step (QwenRunner.cpp:349-375).  A layer is
@@ -80,6 +87,17 @@ namespace mllm
             const torch::Tensor& position_ids,
             KVCache* kv_cache)
         {
+            if (!hidden.is_cuda())
+            {
+                return FromHost(hidden, lw, num_heads, num_kv_heads, head_dim, rope_theta, rms_norm_eps, use_qk_norm,
+                                position_ids, kv_cache);
+            }
+            const b200::TensorParallel& tp = b200::ActiveTensorParallel();
+            if (tp.world > 1)
+            {
+                return HeadSharded(hidden, lw, num_heads, num_kv_heads, head_dim, rope_theta, rms_norm_eps,
+                                   use_qk_norm, position_ids, kv_cache, tp);
+            }
             if (kv_cache != nullptr && kv_cache->IsInitialized() && hidden.dim() == 3 && hidden.size(1) == 1 &&
                 hidden.is_cuda() && position_ids.is_cuda() && b200::DecodeGraphsEnabled() &&
                 b200::ActiveDecodeGraph() == nullptr)
@@ -92,6 +110,110 @@ namespace mllm
         }
 
     private:
+        // A runner whose weights and hidden states live on the host (LlamaRunner): the whole layer
+        // runs on the current CUDA device -- weights staged once (b200::StageWeight), the hidden
+        // state and positions copied per call, the KV cache kept on the device -- and the output
+        // comes back on the host in the hidden state's dtype.
+        static torch::Tensor FromHost(
+            const torch::Tensor& hidden,
+            const LayerWeights& lw,
+            int num_heads,
+            int num_kv_heads,
+            int head_dim,
+            double rope_theta,
+            double rms_norm_eps,
+            bool use_qk_norm,
+            const torch::Tensor& position_ids,
+            KVCache* kv_cache)
+        {
+            const torch::Device dev = b200::ComputeDevice("TransformerBlock");
+            LayerWeights g;
+            g.input_layernorm = b200::StageWeight(lw.input_layernorm, dev);
+            g.post_attention_layernorm = b200::StageWeight(lw.post_attention_layernorm, dev);
+            g.w_q = b200::StageWeight(lw.w_q, dev);
+            g.w_k = b200::StageWeight(lw.w_k, dev);
+            g.w_v = b200::StageWeight(lw.w_v, dev);
+            g.w_o = b200::StageWeight(lw.w_o, dev);
+            g.w_q_norm = b200::StageWeight(lw.w_q_norm, dev);
+            g.w_k_norm = b200::StageWeight(lw.w_k_norm, dev);
+            g.w_gate = b200::StageWeight(lw.w_gate, dev);
+            g.w_up = b200::StageWeight(lw.w_up, dev);
+            g.w_down = b200::StageWeight(lw.w_down, dev);
+            const torch::Tensor h = b200::StageActivation(hidden, dev);
+            const torch::Tensor pos = position_ids.to(dev);
+            torch::Tensor out = Forward(h, g, num_heads, num_kv_heads, head_dim, rope_theta, rms_norm_eps, use_qk_norm,
+                                        pos, kv_cache);
+            return out.to(hidden.device(), hidden.scalar_type());
+        }
+
+        // Tensor parallel (b200::SetTensorParallel): this rank's KV-head group of the layer, then
+        // the sum of the ranks' o_proj partials.  The layer is the reference's step sequence with
+        // the head counts of one group and the weight slices of its heads; the partial o_proj
+        // output is all-reduced before the residual add (decode graphs included: the collective
+        // is recorded with the layer).
+        static torch::Tensor HeadSharded(
+            const torch::Tensor& hidden,
+            const LayerWeights& lw,
+            int num_heads,
+            int num_kv_heads,
+            int head_dim,
+            double rope_theta,
+            double rms_norm_eps,
+            bool use_qk_norm,
+            const torch::Tensor& position_ids,
+            KVCache* kv_cache,
+            const b200::TensorParallel& tp)
+        {
+            if (num_heads % num_kv_heads != 0)
+            {
+                throw std::runtime_error("Attention: num_heads must be divisible by num_kv_heads.");
+            }
+            if (num_kv_heads % tp.world != 0)
+            {
+                throw std::runtime_error("TensorParallel: the kv heads do not split evenly over the ranks");
+            }
+            const int n_rep = num_heads / num_kv_heads;
+            const int kv_local = num_kv_heads / tp.world;
+            const int q_local = kv_local * n_rep;
+            const int64_t q0 = (int64_t)tp.rank * q_local * head_dim, q1 = q0 + (int64_t)q_local * head_dim;
+            const int64_t k0 = (int64_t)tp.rank * kv_local * head_dim, k1 = k0 + (int64_t)kv_local * head_dim;
+            LayerWeights s = lw;
+            s.w_q = b200::ShardWeight(lw.w_q, 0, q0, q1);
+            s.w_k = b200::ShardWeight(lw.w_k, 0, k0, k1);
+            s.w_v = b200::ShardWeight(lw.w_v, 0, k0, k1);
+            s.w_o = b200::ShardWeight(lw.w_o, 1, q0, q1);
+            torch::Tensor attn_in = RMSNorm::Forward(hidden, lw.input_layernorm, rms_norm_eps);
+            torch::Tensor attn_out;
+            if (use_qk_norm)
+            {
+                const auto B = attn_in.size(0);
+                const auto S = attn_in.size(1);
+                torch::Tensor q, k, v;
+                if (!b200::ProjectQKV(attn_in, s.w_q, s.w_k, s.w_v, q_local, kv_local, head_dim, &q, &k, &v))
+                {
+                    q = Linear::Forward(attn_in, s.w_q).view({B, S, q_local, head_dim}).transpose(1, 2);
+                    k = Linear::Forward(attn_in, s.w_k).view({B, S, kv_local, head_dim}).transpose(1, 2);
+                    v = Linear::Forward(attn_in, s.w_v).view({B, S, kv_local, head_dim}).transpose(1, 2);
+                }
+                attn_out = Attention::ForwardProjectedNormed(q, k, v, s.w_o, q_local, kv_local, head_dim, rope_theta,
+                                                             position_ids, kv_cache, lw.w_q_norm, lw.w_k_norm,
+                                                             rms_norm_eps);
+            }
+            else
+            {
+                attn_out = Attention::Forward(attn_in, s.w_q, s.w_k, s.w_v, s.w_o, q_local, kv_local, head_dim,
+                                              rope_theta, position_ids, kv_cache);
+            }
+            attn_out = attn_out.contiguous();
+            b200::RequireCudaBf16(attn_out, "TensorParallel");
+            b200::Check(mllm_comm_all_reduce_bf16(tp.comm, attn_out.data_ptr(), attn_out.data_ptr(),
+                                                  (size_t)attn_out.numel(), b200::CurrentStream()),
+                        "TensorParallel (o_proj all-reduce)");
+            torch::Tensor h = hidden + attn_out;
+            torch::Tensor mlp_in = RMSNorm::Forward(h, lw.post_attention_layernorm, rms_norm_eps);
+            return h + MLP::Forward(mlp_in, lw.w_gate, lw.w_up, lw.w_down);
+        }
+
         // The reference's step sequence (TransformerBlock.h:77-195), run kernel by kernel.
         static torch::Tensor Layer(
             const torch::Tensor& hidden,

@@ -78,9 +78,21 @@ Tensor block_forward(const Tensor& hidden, const std::map<std::string, Tensor>& 
                                            cache ? &cache->c : nullptr);
 }
 
+#ifdef MLLM_DROPIN
+// The drop-in's tensor-parallel mode: `comm` is an mllm_comm_t made by mllm_comm_init (passed as
+// an integer address); world 1 turns it off.
+void set_tensor_parallel(int64_t comm, int rank, int world) {
+    mllm::b200::SetTensorParallel(reinterpret_cast<mllm_comm_t>(comm), rank, world);
+}
+#endif
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+#ifdef MLLM_DROPIN
+    m.def("set_tensor_parallel", &set_tensor_parallel, pybind11::arg("comm"), pybind11::arg("rank"),
+          pybind11::arg("world"));
+#endif
     pybind11::class_<Runner>(m, "Runner")
         .def(pybind11::init<const std::string&>())
         .def("forward", &Runner::forward)

@@ -1,7 +1,8 @@
-"""Random-init Qwen3-architecture checkpoints in the HuggingFace layout the mLLM runners load
-(config.json + model.safetensors, tensor names of QwenRunner::LoadAllWeights).  Test helper:
-the tests and the end-to-end generation bench write one into a temporary directory on the GPU
-machine, then load it with both the reference runner and the drop-in runner."""
+"""Random-init Qwen3- and Llama-architecture checkpoints in the HuggingFace layout the mLLM
+runners load (config.json + model.safetensors, tensor names of QwenRunner::LoadAllWeights and
+LlamaRunner::LoadAllWeights, LlamaRunner.cpp:111-187).  Test helper: the tests and the
+end-to-end generation bench write one into a temporary directory on the GPU machine, then load
+it with both the reference runner and the drop-in runner."""
 from __future__ import annotations
 
 import json
@@ -49,21 +50,39 @@ def _tensor_names(s: QwenShape):
     return names
 
 
+def _llama_tensor_names(s: QwenShape):
+    """LlamaRunner's tensors: the Qwen3 list without the per-head q/k norm weights."""
+    return [(n, shape) for n, shape in _tensor_names(s) if not n.endswith(("q_norm.weight", "k_norm.weight"))]
+
+
+TINYLLAMA_LAYER = QwenShape(layers=2, hidden=2048, heads=32, kv_heads=4, head_dim=64, intermediate=1024, vocab=2048,
+                            rope_theta=1e4, eps=1e-5)
+
+
 def write_random_qwen3(path: str, s: QwenShape, seed: int = 0, device: str = "cuda", dtype: str = "bf16") -> None:
     """Weights N(0, 0.02) (norm weights 1 + N(0, 0.1)), rounded to bf16, generated with torch on
     `device` (a seeded torch generator) and streamed to model.safetensors tensor by tensor.
     dtype="f32" stores the same bf16 values widened exactly to fp32 (a higher-precision run of
     the same model)."""
+    _write(path, "qwen3", s, _tensor_names(s), seed, device, dtype)
+
+
+def write_random_llama(path: str, s: QwenShape, seed: int = 0, device: str = "cuda", dtype: str = "bf16") -> None:
+    """The same for the Llama architecture (model_type "llama": no QK-norm; LlamaRunner keeps
+    these weights on the host)."""
+    _write(path, "llama", s, _llama_tensor_names(s), seed, device, dtype)
+
+
+def _write(path, model_type, s, names, seed, device, dtype):
     import torch
     os.makedirs(path, exist_ok=True)
-    cfg = {"model_type": "qwen3", "_name_or_path": "random-qwen3", "hidden_size": s.hidden,
+    cfg = {"model_type": model_type, "_name_or_path": f"random-{model_type}", "hidden_size": s.hidden,
            "num_hidden_layers": s.layers, "num_attention_heads": s.heads, "num_key_value_heads": s.kv_heads,
            "head_dim": s.head_dim, "intermediate_size": s.intermediate, "vocab_size": s.vocab,
            "max_position_embeddings": 40960, "rms_norm_eps": s.eps, "rope_theta": s.rope_theta,
            "tie_word_embeddings": False, "torch_dtype": "bfloat16"}
     with open(os.path.join(path, "config.json"), "w") as f:
         json.dump(cfg, f)
-    names = _tensor_names(s)
     header = {}
     off = 0
     es, st_name = (2, "BF16") if dtype == "bf16" else (4, "F32")
