@@ -468,6 +468,20 @@ def run_gpu(args, rank, world, device):
             "cublas_concat_us": graphed_us(lambda i: F.linear(hx, ring_cat[i % 4])),
             "bytes": (ring_cat[0].numel() + hx.numel() + B * ring_cat[0].shape[0]) * 2}
     del ring, ring_cat
+    # FP8 block-scaled weights (the FP8 checkpoint layout): the Qwen3-8B gate projection
+    # [12288 x 4096] at 32 tokens, one mllm_linear_fp8_bf16 launch against the reference's route
+    # for such weights on every step -- DequantizeFP8 (QwenRunner.cpp:103-122) then a cuBLAS GEMM --
+    # and against bf16 weights through cuBLAS; a ring of 4 weight sets (201 MB of fp8 > L2)
+    NF = 12288
+    ring8 = [rt.Fp8Weight.quantize((0.02 * torch.randn(NF, HIDDEN, device=device, generator=gen)).bfloat16())
+             for _ in range(4)]
+    ring16 = [w.dequantize() for w in ring8]
+    proj["fp8"] = {"ours_us": graphed_us(lambda i: rt.linear_fp8(hx, ring8[i % 4])),
+                   "reference_route_us": graphed_us(lambda i: F.linear(hx, ring8[i % 4].dequantize())),
+                   "cublas_bf16_weights_us": graphed_us(lambda i: F.linear(hx, ring16[i % 4])),
+                   "bytes": NF * HIDDEN + (NF // 128) * (HIDDEN // 128) * 4 + (B * HIDDEN + B * NF) * 2,
+                   "out_features": NF}
+    del ring8, ring16
 
     # ------------------------------- prefill workload -------------------------------
     pre = None
@@ -1277,6 +1291,21 @@ def main():
             "roofline": {"bound": "hbm", "kernel": "linear_kernel<32>", "achieved": q_gbs, "peak": hbm_peak,
                          "unit": "GB/s", "frac": q_gbs / hbm_peak, "peak_source": peak_src,
                          "algorithmic_bytes": pj["bytes"]}}
+        f8 = pj["fp8"]
+        f8_gbs = f8["bytes"] / (f8["ours_us"] * 1e-6) / 1e9
+        line["fp8_projection"] = {
+            "workload": f"Qwen3-8B gate projection with FP8 weights, {DEC_B} tokens: [{DEC_B}x{HIDDEN}] x "
+                        f"[{HIDDEN}x{f8['out_features']}] e4m3, 128 x 128 block scales",
+            "timing": "per launch, 40 launches in a CUDA graph over a ring of 4 weight sets (201 MB of fp8 > L2)",
+            "us": f8["ours_us"], "reference_route_us": f8["reference_route_us"],
+            "cublas_bf16_weights_us": f8["cublas_bf16_weights_us"],
+            "speedup_vs_reference_route": f8["reference_route_us"] / f8["ours_us"],
+            "note": "reference_route: DequantizeFP8 (w.to(bf16) * scale.to(bf16)) then a cuBLAS GEMM, what "
+                    "QwenRunner runs per layer per step; the outputs are the same bf16 GEMM of the same "
+                    "dequantized weight",
+            "roofline": {"bound": "hbm", "kernel": "linear_fp8_kernel<32>", "achieved": f8_gbs, "peak": hbm_peak,
+                         "unit": "GB/s", "frac": f8_gbs / hbm_peak, "peak_source": peak_src,
+                         "algorithmic_bytes": f8["bytes"]}}
     if res["pre"] is not None:
         p = res["pre"]
         fl = prefill_flops(PRE_B, H, D, PRE_S)

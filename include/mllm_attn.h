@@ -422,6 +422,30 @@ MLLM_API int mllm_linear_bf16(const void* x, int64_t x_stride, int tokens, int64
                               size_t workspace_bytes, mllm_stream_t stream);
 
 /* ----------------------------------------------------------------------------------------
+ * FP8 projections.  Replaces, for a weight stored as e4m3 with one fp32 scale per 128 x 128
+ * block (`weight_scale_inv`, the FP8 checkpoint layout QwenRunner loads, QwenRunner.cpp:148-283),
+ * the reference's dequantize-then-multiply: DequantizeFP8 (QwenRunner.cpp:103-122,
+ * bf16(fp8 * bf16(scale)), run on every layer of every step) followed by Linear::Forward
+ * (Linear.h:33-68).  The fp8 bytes are streamed from HBM (half the bf16 weight) and dequantized
+ * in shared memory with exactly that rounding; the tensor cores then multiply the same bf16
+ * operand (fp32 accumulation, one rounding per output, split-k partials added in a fixed order).
+ *   x: bf16 [tokens, in_features], row stride x_stride (multiple of 8, 16-byte aligned)
+ *   weight: e4m3 [out_features, in_features], row stride weight_stride bytes (multiple of 16,
+ *       16-byte aligned); in_features and out_features multiples of 128
+ *   weight_scale_inv: fp32 [out_features/128, >= in_features/128], row stride scale_stride
+ *   out: bf16 [tokens, out_stride], 16-byte aligned, out_stride a multiple of 8
+ *   workspace: mllm_linear_fp8_workspace_size(...) bytes (0 when no split is needed), 256-byte
+ *       aligned, with the same counter convention as mllm_linear_bf16's workspace (one workspace
+ *       may serve both)
+ * 0 <= tokens <= 128 (decode-sized batches; larger batches dequantize and call a GEMM). */
+MLLM_API size_t mllm_linear_fp8_workspace_size(int tokens, int64_t out_features, int64_t in_features);
+MLLM_API int mllm_linear_fp8_bf16(const void* x, int64_t x_stride, int tokens, int64_t in_features,
+                                  const void* weight, int64_t weight_stride, int64_t out_features,
+                                  const float* weight_scale_inv, int64_t scale_stride, void* out,
+                                  int64_t out_stride, void* workspace, size_t workspace_bytes,
+                                  mllm_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------
  * Peer-memory plumbing for the tensor-parallel o_proj exchange (no reference counterpart: the
  * reference runs on one device, QwenRunner.cpp:236,328).  mllm_b200/tp.py's PeerExchange
  * sums the ranks' o_proj partials with these: flags raised in a peer's memory, a bounded

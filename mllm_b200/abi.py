@@ -82,6 +82,8 @@ SIGNATURES = {
     "mllm_linear_workspace_size": (_sz, [_i, _i, C.POINTER(C.c_int64), _i64]),
     "mllm_linear_bf16": (_i, [_p, _i64, _i, _i64, _i, C.POINTER(C.c_void_p), C.POINTER(C.c_int64),
                               C.POINTER(C.c_int64), _p, _i64, _p, _sz, _p]),
+    "mllm_linear_fp8_workspace_size": (_sz, [_i, _i64, _i64]),
+    "mllm_linear_fp8_bf16": (_i, [_p, _i64, _i, _i64, _p, _i64, _i64, _p, _i64, _p, _i64, _p, _sz, _p]),
     "mllm_ipc_alloc": (_i, [_sz, C.POINTER(C.c_void_p)]),
     "mllm_ipc_free": (_i, [_p]),
     "mllm_ipc_get_handle": (_i, [_p, _p]),

@@ -99,6 +99,29 @@ int encode_kv_map(CUtensorMap* map, const void* base, int64_t d, int64_t rows, i
     return MLLM_OK;
 }
 
+int encode_u8_map(CUtensorMap* map, const void* base, int64_t cols, int64_t rows, int64_t stride_row,
+                  uint32_t box_cols, uint32_t box_rows) {
+    auto fn = get_encode_fn();
+    if (!fn) return fail(MLLM_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    if (!aligned(base, 16)) return fail(MLLM_ERR_INVALID_ARGUMENT, "TMA base address must be 16-byte aligned");
+    if (stride_row <= 0 || stride_row % 16 != 0)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "byte-matrix row stride must be a positive multiple of 16");
+    cuuint64_t dims[4] = {(cuuint64_t)cols, (cuuint64_t)rows, 1, 1};
+    cuuint64_t strides[3] = {(cuuint64_t)stride_row, (cuuint64_t)(stride_row * rows), (cuuint64_t)(stride_row * rows)};
+    cuuint32_t box[4] = {box_cols, box_rows, 1, 1};
+    cuuint32_t elem_strides[4] = {1, 1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box, elem_strides,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        char buf[160];
+        snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled (bytes) failed (%d) dims=%lld,%lld", (int)r,
+                 (long long)cols, (long long)rows);
+        return fail(MLLM_ERR_INVALID_ARGUMENT, buf);
+    }
+    return MLLM_OK;
+}
+
 }  // namespace mllm_b200
 
 using namespace mllm_b200;
@@ -125,10 +148,11 @@ extern "C" const char* mllm_attn_last_error(void) { return t_last_error.c_str();
 
 extern "C" int mllm_attn_device_status(mllm_stream_t stream) {
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    constexpr int kReaders = 4;
-    unsigned v[kReaders] = {0u, 0u, 0u, 0u};
+    constexpr int kReaders = 5;
+    unsigned v[kReaders] = {0u, 0u, 0u, 0u, 0u};
     int (*readers[kReaders])(cudaStream_t, unsigned*) = {read_clear_status_decode, read_clear_status_prefill,
-                                                         read_clear_status_epilogue, read_clear_status_peer};
+                                                         read_clear_status_epilogue, read_clear_status_peer,
+                                                         read_clear_status_linear};
     for (int i = 0; i < kReaders; ++i) {
         const int e = readers[i](s, &v[i]);
         if (e != 0) return check_cuda((cudaError_t)e, "read device status");
@@ -138,5 +162,6 @@ extern "C" int mllm_attn_device_status(mllm_stream_t stream) {
     for (int i = 0; i < kReaders; ++i) all |= v[i];
     if (all & kErrTimeout) return fail(MLLM_ERR_DEVICE_TIMEOUT, "a kernel's bounded wait expired");
     if (all & kErrBadLength) return fail(MLLM_ERR_DEVICE_LENGTH, "a device-side length exceeded its capacity");
+    if (all & kErrSmemAlign) return fail(MLLM_ERR_CUDA, "a kernel's dynamic shared memory was misaligned (no work done)");
     return ok();
 }

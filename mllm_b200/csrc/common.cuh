@@ -27,6 +27,7 @@ enum DeviceError : unsigned {
     kErrNone = 0u,
     kErrTimeout = 1u,       // a bounded wait ran out (pipeline logic error)
     kErrBadLength = 2u,     // a device-side length exceeded the capacity given by the host
+    kErrSmemAlign = 4u,     // a kernel found its dynamic shared memory less aligned than it needs
 };
 static __device__ unsigned g_tu_status = 0u;
 

@@ -59,6 +59,7 @@ int read_clear_status_decode(cudaStream_t s, unsigned* out);
 int read_clear_status_prefill(cudaStream_t s, unsigned* out);
 int read_clear_status_epilogue(cudaStream_t s, unsigned* out);
 int read_clear_status_peer(cudaStream_t s, unsigned* out);
+int read_clear_status_linear(cudaStream_t s, unsigned* out);
 
 // Encodes a 4-D bf16 tensor map {d (inner), rows, heads, batch} with 128-byte swizzle and a
 // {box_d, box_rows, box_heads, 1} box.  Strides are in elements and need not be ordered (a
@@ -67,5 +68,11 @@ int read_clear_status_peer(cudaStream_t s, unsigned* out);
 int encode_kv_map(CUtensorMap* map, const void* base, int64_t d, int64_t rows, int64_t heads, int64_t batch,
                   int64_t stride_row, int64_t stride_head, int64_t stride_batch, uint32_t box_d,
                   uint32_t box_rows, uint32_t box_heads = 1);
+
+// Encodes a 2-D byte tensor map {cols (inner), rows} with row stride `stride_row` bytes, no
+// swizzle and a {box_cols, box_rows} box (as a 4-D map with unit outer dimensions, so that the
+// 4-D load helper serves it).  Returns MLLM_OK or an error.
+int encode_u8_map(CUtensorMap* map, const void* base, int64_t cols, int64_t rows, int64_t stride_row,
+                  uint32_t box_cols, uint32_t box_rows);
 
 }  // namespace mllm_b200

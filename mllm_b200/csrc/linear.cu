@@ -19,6 +19,8 @@
 //     first: only about 33 clusters of 4 are resident at once, so a 48-tile q|k|v grid ran in
 //     two waves.)
 // Every mbarrier wait is bounded (common.cuh).
+#include <cuda_fp8.h>
+
 #include <algorithm>
 #include <cstring>
 
@@ -337,7 +339,328 @@ int launch_linear(const LinearMaps& maps, const LinearArgs& a, const LinearPlan&
                       "linear launch");
 }
 
+// ---------------------------------------------------------------------------------------------
+// FP8 weights with 128 x 128 block scales (e4m3, weight_scale_inv [N/128][K/128] fp32): the
+// reference dequantizes every such projection on every step (QwenRunner.cpp:103-122:
+// w.to(bf16) * scale.to(bf16), a bf16 tensor product) and multiplies in bf16 (Linear.h:33-68).
+// This kernel streams the fp8 bytes -- half the bf16 weight -- and dequantizes each 128-row x
+// 128-k block in shared memory with exactly that arithmetic: fp8 -> fp32 (exact), times the
+// bf16-rounded scale (an exact product of a 4-bit and an 8-bit significand), one rounding to bf16.
+// The tensor cores then see the same bf16 operand the reference's GEMM sees.
+//
+// Roles (256 threads, the k range of a 128-row tile split over CTAs):
+//   warp 0 (lane 0): TMA of the fp8 tile blocks, 128 rows x 128 bytes, into ring A;
+//   warp 2 (lane 0): TMA of the activations' two 64-k atoms of each block into ring B;
+//   warps 3-7: dequantize ring A's block into ring B in the K-major 128-byte-swizzled layout the
+//     MMA reads (8-row groups 2 KB apart, two atoms per group);
+//   warp 1 (lane 0): tcgen05.mma kind::f16 over ring B, fp32 accumulators in tensor memory;
+//   warps 4-7: the epilogue (tensor-memory lane quarters 0-3), split partials as linear_kernel.
+// ---------------------------------------------------------------------------------------------
+constexpr int kF8Unit = 128;                 // k per unit: one scale block, two bf16 atoms
+constexpr int kF8Threads = 256;
+constexpr int kF8ConvWarp0 = 3;
+constexpr int kF8ConvWarps = 5;
+constexpr int kF8MaxTokens = 128;
+
+// At 32 tokens two CTAs share an SM (two fp8 stages and two dequantized stages each, 112 KB,
+// at most 128 registers): the dequantizing warps of two tiles interleave and the tile x split
+// grid fits one wave.  Wider token tiles keep one CTA per SM with deeper rings.  (Measured on
+// the Qwen3-8B gate projection at 32 tokens: 21 us with this split; one CTA per SM with eight fp8
+// stages and nine dequantizing warps, 35 us; three per SM with one dequantized stage, 26 us.)
+constexpr int f8_ctas_per_sm(int nt) { return nt == 32 ? 2 : 1; }
+
+template <int NT>
+struct F8Cfg {
+    static constexpr int kABytes = kTileRows * kF8Unit;          // fp8 block
+    static constexpr int kBWBytes = kTileRows * kF8Unit * 2;     // dequantized block
+    static constexpr int kBXBytes = NT * kF8Unit * 2;            // activations
+    static constexpr int kBBytes = kBWBytes + kBXBytes;
+    static constexpr int kAStages = NT == 32 ? 2 : 4;
+    static constexpr int kBStages = NT == 32 ? 2 : (NT <= 64 ? 3 : 2);
+    static constexpr int kRings = kAStages * kABytes + kBStages * kBBytes;
+    static constexpr int kSmem = kRings + 256;   // + barriers; the kernel has no static shared memory
+};
+
+struct F8Args {
+    int units;                 // K / 128
+    int tokens;
+    __nv_bfloat16* out;
+    int64_t out_stride;
+    const float* scale;        // [N/128][scale_stride]
+    int64_t scale_stride;
+    unsigned* counters;
+    float* partial;
+};
+
+// 8 e4m3 bytes -> 8 bf16 (16 bytes), each bf16(float(w) * s)
+__device__ __forceinline__ uint4 dequant8(uint2 w, float s) {
+    const uint32_t in[2] = {w.x, w.y};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const __nv_fp8x2_storage_t pair = (__nv_fp8x2_storage_t)((in[i] >> (16 * h)) & 0xffffu);
+            const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
+            __half2 hv;
+            hv = *reinterpret_cast<const __half2*>(&hr);
+            const float2 f = __half22float2(hv);
+            o[2 * i + h] = pack_bf16x2(__fmul_rn(f.x, s), __fmul_rn(f.y, s));
+        }
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kF8Threads, f8_ctas_per_sm(NT))
+    linear_fp8_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                      const F8Args a) {
+    using Cfg = F8Cfg<NT>;
+    constexpr int SA = Cfg::kAStages;
+    constexpr int SB = Cfg::kBStages;
+    // All shared memory is dynamic, so that its base is the CTA's shared window (1024-aligned) and
+    // two CTAs fit per SM without alignment slack: ring B (swizzled, 1024-aligned stages), ring A,
+    // then the barriers.  A base found misaligned is recorded and the CTA leaves before it touches
+    // a barrier or tensor memory.
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    if ((smem_u32(smem_raw) & 1023u) != 0u) {
+        if (threadIdx.x == 0) record_error(kErrSmemAlign);
+        return;
+    }
+    uint8_t* smem = smem_raw;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kRings);
+    uint64_t* a_full = bars;
+    uint64_t* a_empty = a_full + SA;
+    uint64_t* b_full = a_empty + SA;
+    uint64_t* b_empty = b_full + SB;
+    uint64_t* done_bar = b_empty + SB;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+    int* last_slot = reinterpret_cast<int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int splits = (int)gridDim.x;
+    const int split = (int)blockIdx.x;
+    const int tile = (int)blockIdx.y;
+    const int wrow = tile * kTileRows;
+    const int u0 = (int)((int64_t)split * a.units / splits);
+    const int nk = (int)((int64_t)(split + 1) * a.units / splits) - u0;   // >= 1 (splits <= units)
+    // ring B first (1024-aligned swizzle blocks), then ring A
+    auto stage_bw = [&](int s) { return smem + s * Cfg::kBBytes; };
+    auto stage_bx = [&](int s) { return smem + s * Cfg::kBBytes + Cfg::kBWBytes; };
+    auto stage_a = [&](int s) { return smem + SB * Cfg::kBBytes + s * Cfg::kABytes; };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < SA; ++s) {
+            mbar_init(&a_full[s], 1);
+            mbar_init(&a_empty[s], kF8ConvWarps);
+        }
+        for (int s = 0; s < SB; ++s) {
+            mbar_init(&b_full[s], 1 + kF8ConvWarps);   // the activation load + every converter warp
+            mbar_init(&b_empty[s], 1);
+        }
+        mbar_init(done_bar, 1);
+        mbar_fence_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, NT);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------- fp8 weight blocks -------------------------------
+        // after the previous kernel in the stream: it may be the one that wrote the weights
+        tma_prefetch_desc(&wmap);
+        pdl_wait();
+        int i = 0;
+        for (; i < nk; ++i) {
+            const int s = i % SA;
+            if (i >= SA && !mbar_wait(&a_empty[s], ((i / SA) - 1) & 1)) break;
+            mbar_arrive_expect_tx(&a_full[s], Cfg::kABytes);
+            tma_load_4d(stage_a(s), &wmap, &a_full[s], (u0 + i) * kF8Unit, wrow, 0, 0);
+        }
+        for (int j = (i > SA ? i - SA : 0); j < i; ++j) mbar_wait(&a_full[j % SA], (j / SA) & 1);
+    } else if (warp == 2 && lane == 0) {
+        // ------------------------------- activations -------------------------------
+        tma_prefetch_desc(&xmap);
+        pdl_wait();   // the activations may be the previous kernel's output
+        int i = 0;
+        for (; i < nk; ++i) {
+            const int s = i % SB;
+            if (i >= SB && !mbar_wait(&b_empty[s], ((i / SB) - 1) & 1)) break;
+            mbar_arrive_expect_tx(&b_full[s], Cfg::kBXBytes);
+            tma_load_4d(stage_bx(s), &xmap, &b_full[s], 0, 0, (u0 + i) * 2, 0);
+        }
+        for (int j = (i > SB ? i - SB : 0); j < i; ++j) mbar_wait(&b_full[j % SB], (j / SB) & 1);
+    } else if (warp >= kF8ConvWarp0) {
+        // ------------------------------- dequantize -------------------------------
+        const int ct = threadIdx.x - kF8ConvWarp0 * 32;
+        const float* srow = a.scale + (int64_t)tile * a.scale_stride;
+        for (int i = 0; i < nk; ++i) {
+            const int sa = i % SA, sb = i % SB;
+            if (!mbar_wait(&a_full[sa], (i / SA) & 1)) break;
+            if (i >= SB && !mbar_wait(&b_empty[sb], ((i / SB) - 1) & 1)) break;
+            // QwenRunner.cpp:103-122: scale.to(bf16), then the bf16 product
+            const float sc = __bfloat162float(__float2bfloat16_rn(srow[u0 + i]));
+            const uint8_t* src = stage_a(sa);
+            uint8_t* dst = stage_bw(sb);
+            // chunk u: row u / 16, k 8 (u % 16) .. + 7; four chunks per round, loads first
+            constexpr int kStep = kF8ConvWarps * 32;
+            constexpr int kChunks = kTileRows * 16;
+            for (int u0c = ct; u0c < kChunks; u0c += 4 * kStep) {
+                uint2 w[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int u = u0c + q * kStep;
+                    if (u < kChunks) w[q] = *reinterpret_cast<const uint2*>(src + (u >> 4) * kF8Unit + 8 * (u & 15));
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int u = u0c + q * kStep;
+                    if (u >= kChunks) break;
+                    const int R = u >> 4, c16 = u & 15;
+                    const int g = R >> 3, r = R & 7, at = c16 >> 3, c = c16 & 7;
+                    *reinterpret_cast<uint4*>(dst + g * 2048 + at * 1024 + r * 128 + ((c ^ r) << 4)) =
+                        dequant8(w[q], sc);
+                }
+            }
+            fence_proxy_async_smem();   // generic writes, read next by the tensor cores
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&b_full[sb]);
+                mbar_arrive(&a_empty[sa]);
+            }
+        }
+    } else if (warp == 1 && lane == 0) {
+        // -------------------------------- MMA issuer --------------------------------
+        constexpr uint32_t idesc = idesc_bf16_f32(kTileRows, NT, false);
+        constexpr uint32_t w_hi = smem_desc_hi_sw128(2048);   // row groups 2 KB apart (two atoms)
+        constexpr uint32_t x_hi = smem_desc_hi_sw128(1024);
+        for (int i = 0; i < nk; ++i) {
+            const int s = i % SB;
+            if (!mbar_wait(&b_full[s], (i / SB) & 1)) break;
+            tc_fence_after();
+            const uint32_t wd = smem_desc_lo(smem_u32(stage_bw(s)), 16);
+            const uint32_t xd = smem_desc_lo(smem_u32(stage_bx(s)), 16);
+#pragma unroll
+            for (int at = 0; at < 2; ++at)
+#pragma unroll
+                for (int ks = 0; ks < kAtomK / 16; ++ks)
+                    tc_mma_ss_w2(tmem, wd + (uint32_t)((at * 1024 + ks * 32) >> 4), w_hi,
+                                 xd + (uint32_t)((at * NT * 128 + ks * 32) >> 4), x_hi, idesc,
+                                 (i > 0 || at > 0 || ks > 0) ? 1u : 0u);
+            tc_commit(&b_empty[s]);
+        }
+        tc_commit(done_bar);
+    }
+    __syncwarp();
+
+    // --------------------------- epilogue (warps 4-7) ---------------------------
+    if (warp >= 4 && warp < 8) {
+        const int ew = warp - 4;                 // tensor-memory lane quarter
+        mbar_wait(done_bar, 0);
+        tc_fence_after();
+        pdl_trigger();
+        const int T = a.tokens;
+        const int row = ew * 32 + lane;
+        const int64_t ostride = a.out_stride;
+        __nv_bfloat16* outp = a.out + wrow;
+        const uint32_t t_lane = tmem + ((uint32_t)(ew * 32) << 16);
+        float* mine = a.partial + ((size_t)(tile * splits + split) * T) * kTileRows;
+#pragma unroll 1
+        for (int c = 0; c < T; c += 32) {
+            float r[32];
+            tmem_ld32(t_lane + (uint32_t)c, r);
+            tmem_wait_ld();
+            if (splits == 1) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (c + j < T) outp[(int64_t)(c + j) * ostride + row] = __float2bfloat16_rn(r[j]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (c + j < T) mine[(c + j) * kTileRows + row] = r[j];
+            }
+        }
+        if (splits > 1) {
+            __threadfence();
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+            if (ew == 0 && lane == 0) *last_slot = atomicAdd(&a.counters[tile], 1u) == (unsigned)(splits - 1);
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+            if (*last_slot) {
+                __threadfence();
+                const float* base = a.partial + (size_t)tile * splits * T * kTileRows + 4 * lane;
+                __nv_bfloat16* orow = outp + 4 * lane;
+                // one token per batch keeps the kernel's registers low
+                reduce_partials<1, kMaxSplits>(base, orow, ostride, T, splits, ew);
+                if (ew == 0 && lane == 0) a.counters[tile] = 0u;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, NT);
+}
+
+struct F8Plan {
+    int tiles = 0, units = 0, splits = 1, nt = 32;
+    size_t partial_offset = 0, workspace_bytes = 0;
+};
+
+void plan_linear_fp8(int tokens, int64_t out_features, int64_t in_features, int num_sms, F8Plan* p) {
+    p->tiles = (int)(out_features / kTileRows);
+    p->nt = tokens <= 32 ? 32 : tokens <= 64 ? 64 : 128;
+    p->units = (int)(in_features / kF8Unit);
+    // splits: the fewest that minimise (waves of CTAs) x (units per CTA), at most 8, at most one
+    // per unit, and few enough that the partials stay below about a quarter of the weight bytes
+    const int64_t cap = std::max<int64_t>(1, std::min<int64_t>({(int64_t)kMaxSplits, (int64_t)p->units,
+                                                                in_features / (8 * (int64_t)std::max(1, tokens))}));
+    const int64_t slots = (int64_t)num_sms * f8_ctas_per_sm(p->nt);   // CTAs resident at once
+    double best = 1e30;
+    p->splits = 1;
+    for (int64_t sp = 1; sp <= cap; ++sp) {
+        const int64_t waves = ((int64_t)p->tiles * sp + slots - 1) / slots;
+        const double cost = (double)waves * (double)((p->units + sp - 1) / sp);
+        if (cost < best - 1e-9) {
+            best = cost;
+            p->splits = (int)sp;
+        }
+    }
+    if (p->tiles > kMaxCounters) p->splits = 1;
+    p->partial_offset = kMaxCounters * sizeof(unsigned);
+    p->workspace_bytes = p->splits > 1 ? p->partial_offset + (size_t)p->tiles * p->splits * tokens * kTileRows * 4 : 0;
+}
+
+int check_linear_fp8_args(int tokens, int64_t in_features, int64_t out_features) {
+    if (tokens < 0 || tokens > kF8MaxTokens)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "linear_fp8: tokens must be in [0, 128]");
+    if (in_features <= 0 || in_features % kF8Unit != 0 || in_features > (int64_t)1 << 30)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "linear_fp8: in_features must be a positive multiple of 128");
+    if (out_features <= 0 || out_features % kTileRows != 0 || out_features > (1 << 24))
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "linear_fp8: out_features must be a positive multiple of 128");
+    return MLLM_OK;
+}
+
+template <int NT>
+int launch_linear_fp8(const CUtensorMap& wmap, const CUtensorMap& xmap, const F8Args& a, const F8Plan& p,
+                      cudaStream_t s) {
+    using Cfg = F8Cfg<NT>;
+    auto kern = linear_fp8_kernel<NT>;
+    if (int st = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem),
+                            "linear_fp8: shared memory attribute"))
+        return st;
+    return check_cuda(launch_pdl(kern, dim3(p.splits, p.tiles, 1), dim3(kF8Threads, 1, 1), (size_t)Cfg::kSmem, s,
+                                 wmap, xmap, a),
+                      "linear_fp8 launch");
+}
+
 }  // namespace
+
+MLLM_DEFINE_STATUS_READER(linear)
+
 }  // namespace mllm_b200
 
 using namespace mllm_b200;
@@ -414,6 +737,67 @@ extern "C" int mllm_linear_bf16(const void* x, int64_t x_stride, int tokens, int
         case 64: st = launch_linear<64>(maps, a, p, s); break;
         case 128: st = launch_linear<128>(maps, a, p, s); break;
         default: st = launch_linear<256>(maps, a, p, s); break;
+    }
+    return st ? st : ok();
+}
+
+extern "C" size_t mllm_linear_fp8_workspace_size(int tokens, int64_t out_features, int64_t in_features) {
+    if (check_linear_fp8_args(tokens, in_features, out_features) != MLLM_OK) {
+        ok();
+        return 0;
+    }
+    F8Plan p;
+    plan_linear_fp8(tokens, out_features, in_features, sm_count_or_default(), &p);
+    return p.workspace_bytes;
+}
+
+extern "C" int mllm_linear_fp8_bf16(const void* x, int64_t x_stride, int tokens, int64_t in_features,
+                                    const void* weight, int64_t weight_stride, int64_t out_features,
+                                    const float* weight_scale_inv, int64_t scale_stride, void* out,
+                                    int64_t out_stride, void* workspace, size_t workspace_bytes,
+                                    mllm_stream_t stream) {
+    MLLM_NVTX_RANGE("mllm_linear_fp8_bf16");
+    if (int st = check_linear_fp8_args(tokens, in_features, out_features)) return st;
+    if (tokens == 0) return ok();
+    if (!x || !weight || !weight_scale_inv || !out)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "linear_fp8: null pointer");
+    if (x_stride < in_features || out_stride < out_features || weight_stride < in_features ||
+        scale_stride < in_features / kF8Unit)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "linear_fp8: a row stride is below the row length");
+    if (!aligned(out, 16) || out_stride % 8 != 0)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "linear_fp8: output must be 16-byte aligned with a stride multiple of 8");
+    if (!aligned(weight, 16) || weight_stride % 16 != 0)
+        return fail(MLLM_ERR_INVALID_ARGUMENT, "linear_fp8: weight rows must be 16-byte aligned");
+    int num_sms = 0;
+    if (int st = require_sm100(&num_sms)) return st;
+    F8Plan p;
+    plan_linear_fp8(tokens, out_features, in_features, num_sms, &p);
+    if (p.tiles > 65535) return fail(MLLM_ERR_INVALID_ARGUMENT, "linear_fp8: too many output rows");
+    if (p.workspace_bytes > 0 && (!workspace || workspace_bytes < p.workspace_bytes || !aligned(workspace, 256)))
+        return fail(MLLM_ERR_INVALID_ARGUMENT,
+                    "linear_fp8: workspace missing, not 256-byte aligned or smaller than mllm_linear_fp8_workspace_size");
+    CUtensorMap wmap, xmap;
+    if (int st = encode_u8_map(&wmap, weight, in_features, out_features, weight_stride, kF8Unit, kTileRows)) return st;
+    // activations {64 k, tokens, k-atoms}: box NT rows x 2 atoms (one 128-k unit)
+    if (int st = encode_kv_map(&xmap, x, kAtomK, tokens, in_features / kAtomK, 1, x_stride, kAtomK,
+                               x_stride * tokens, kAtomK, (uint32_t)p.nt, 2))
+        return st;
+    F8Args a = {};
+    a.units = p.units;
+    a.tokens = tokens;
+    a.out = static_cast<__nv_bfloat16*>(out);
+    a.out_stride = out_stride;
+    a.scale = weight_scale_inv;
+    a.scale_stride = scale_stride;
+    a.counters = static_cast<unsigned*>(workspace);
+    a.partial = p.workspace_bytes ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + p.partial_offset)
+                                  : nullptr;
+    cudaStream_t s = (cudaStream_t)stream;
+    int st;
+    switch (p.nt) {
+        case 32: st = launch_linear_fp8<32>(wmap, xmap, a, p, s); break;
+        case 64: st = launch_linear_fp8<64>(wmap, xmap, a, p, s); break;
+        default: st = launch_linear_fp8<128>(wmap, xmap, a, p, s); break;
     }
     return st ? st : ok();
 }

@@ -732,9 +732,89 @@ def _linear_workspace(device, nbytes: int):
     return ws
 
 
-def _linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+class Fp8Weight:
+    """A projection stored the way FP8 checkpoints hold it (QwenRunner.cpp:148-283 loads it with its
+    `weight_scale_inv`): e4m3 values w [out, in] and fp32 scales [out/128, in/128], one per
+    128 x 128 block.  The reference dequantizes it on every step (DequantizeFP8,
+    QwenRunner.cpp:103-122) and multiplies in bf16; `linear_fp8` multiplies it as stored."""
+
+    BLOCK = 128
+
+    def __init__(self, w: torch.Tensor, scale_inv: torch.Tensor):
+        if w.dtype != torch.float8_e4m3fn or w.dim() != 2:
+            raise RuntimeError("Fp8Weight: e4m3 [out, in] weights")
+        n, k = w.shape
+        if n % self.BLOCK or k % self.BLOCK or tuple(scale_inv.shape) != (n // self.BLOCK, k // self.BLOCK):
+            raise RuntimeError("Fp8Weight: 128 x 128 blocks, scales [out/128, in/128]")
+        self.w = w.contiguous()
+        self.scale_inv = scale_inv.float().contiguous()
+
+    @classmethod
+    def quantize(cls, w: torch.Tensor) -> "Fp8Weight":
+        """Block-wise e4m3 quantization of a weight (scale = block amax / 448), the format of
+        FP8 checkpoints; for building test and benchmark models."""
+        n, k = w.shape
+        b = cls.BLOCK
+        blocks = w.float().view(n // b, b, k // b, b)
+        amax = blocks.abs().amax(dim=(1, 3)).clamp_min(1e-12)
+        scale = amax / 448.0
+        q = (blocks / scale[:, None, :, None]).to(torch.float8_e4m3fn).view(n, k)
+        return cls(q, scale)
+
+    def size(self, dim: int) -> int:
+        return self.w.size(dim)
+
+    @property
+    def shape(self):
+        return self.w.shape
+
+    def dequantize(self, dtype=BF16) -> torch.Tensor:
+        """DequantizeFP8 (QwenRunner.cpp:103-122): w.to(dtype) * scale.to(dtype), block-broadcast,
+        in dtype -- the weights the reference's GEMM sees."""
+        n, k = self.w.shape
+        b = self.BLOCK
+        w_h = self.w.to(dtype).reshape(n // b, b, k // b, b)
+        s_h = self.scale_inv.to(dtype).unsqueeze(1).unsqueeze(3)
+        return (w_h * s_h).reshape(n, k)
+
+
+FP8_MAX_TOKENS = 128
+
+
+def linear_fp8(x: torch.Tensor, w: Fp8Weight) -> torch.Tensor:
+    """Linear::Forward(x, DequantizeFP8(w)) for bf16 x with at most 128 rows, by
+    mllm_linear_fp8_bf16: the fp8 bytes are streamed and dequantized in shared memory with the
+    reference's rounding, so the product equals a bf16 GEMM on the dequantized weight (fp32
+    accumulation, one rounding).  More rows: the reference's own route (dequantize, cuBLAS)."""
+    K = x.size(-1)
+    if K != w.size(1):
+        raise RuntimeError("Linear: last dim of x must match weight in_features.")
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, K)
+    T = x2.size(0)
+    if not (x.is_cuda and x.dtype == BF16) or T > FP8_MAX_TOKENS:
+        return torch.nn.functional.linear(x, w.dequantize(x.dtype))
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
+        x2 = x2.contiguous()
+    N = w.size(0)
+    out = torch.empty((T, N), dtype=BF16, device=x.device)
+    need = abi.load().mllm_linear_fp8_workspace_size(T, N, K)
+    if need and _capturing():
+        ws = _capture_scratch.get("linear", need, x.device)
+    else:
+        ws = _linear_workspace(x.device, need)
+    abi.call("mllm_linear_fp8_bf16", _ptr(x2), x2.stride(0), T, K, _ptr(w.w), w.w.stride(0), N, _ptr(w.scale_inv),
+             w.scale_inv.stride(0), _ptr(out), out.stride(0), _ptr(ws), ws.numel() if ws is not None else 0,
+             abi.stream_handle())
+    return out.view(*lead, N)
+
+
+def _linear(x: torch.Tensor, w) -> torch.Tensor:
     """Linear::Forward (Linear.h:33-68): x @ w.T in the input dtype, a cuBLAS GEMM as in the
-    reference (for one weight mllm_linear_bf16 is not faster than cuBLAS beyond a few tokens)."""
+    reference (for one weight mllm_linear_bf16 is not faster than cuBLAS beyond a few tokens);
+    an Fp8Weight goes through linear_fp8."""
+    if isinstance(w, Fp8Weight):
+        return linear_fp8(x, w)
     if x.size(-1) != w.size(1):
         raise RuntimeError("Linear: last dim of x must match weight in_features.")
     return torch.nn.functional.linear(x, w)
@@ -743,9 +823,10 @@ def _linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
 def _project_qkv(h: torch.Tensor, w_q, w_k, w_v, num_heads: int, num_kv_heads: int, head_dim: int):
     """The three attention projections (TransformerBlock.h:82-96, Attention.h:52-54) as q [B,H,S,D]
     and k/v [B,Hkv,S,D] views.  Up to 256 tokens: one mllm_linear_bf16 launch writes q | k | v side
-    by side and the views point into it; otherwise three cuBLAS GEMMs as in the reference."""
+    by side and the views point into it; otherwise three cuBLAS GEMMs as in the reference (FP8
+    weights: three linear_fp8 launches)."""
     B, S, E = h.shape
-    if linear_supported(h, [w_q, w_k, w_v]):
+    if not any(isinstance(w, Fp8Weight) for w in (w_q, w_k, w_v)) and linear_supported(h, [w_q, w_k, w_v]):
         qkv = linear(h, [w_q, w_k, w_v])          # [B, S, (H + 2 Hkv) D]
         hq, hk = num_heads * head_dim, num_kv_heads * head_dim
         q = qkv[..., :hq].view(B, S, num_heads, head_dim).transpose(1, 2)

@@ -40,10 +40,11 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 
 
 def swiglu_mlp(x, w_gate, w_up, w_down):
-    """MLP::Forward (MLP.h:31-43): down(gate * sigmoid(gate) * up)."""
-    gate = torch.nn.functional.linear(x, w_gate)
-    up = torch.nn.functional.linear(x, w_up)
-    return torch.nn.functional.linear(gate * torch.sigmoid(gate) * up, w_down)
+    """MLP::Forward (MLP.h:31-43): down(gate * sigmoid(gate) * up); FP8 weights through
+    runtime.linear_fp8."""
+    gate = rt._linear(x, w_gate)
+    up = rt._linear(x, w_up)
+    return rt._linear(gate * torch.sigmoid(gate) * up, w_down)
 
 
 @dataclass
@@ -63,7 +64,9 @@ class DecoderShape:
 class DecoderModel:
     """Random-init decoder (Qwen3 or Llama layout) whose attention step runs on the B200 path."""
 
-    def __init__(self, shape: DecoderShape, seed: int = 0, device="cuda"):
+    def __init__(self, shape: DecoderShape, seed: int = 0, device="cuda", fp8: bool = False):
+        """fp8: every projection (q/k/v/o and the MLP) held as e4m3 with 128 x 128 block scales,
+        the layout of FP8 checkpoints, and multiplied as stored (runtime.linear_fp8)."""
         self.s = shape
         g = torch.Generator(device=device).manual_seed(seed)
         E, H, Hkv, D, I = shape.hidden, shape.heads, shape.kv_heads, shape.head_dim, shape.intermediate
@@ -84,6 +87,19 @@ class DecoderModel:
                 "w_q": w(H * D, E), "w_k": w(Hkv * D, E), "w_v": w(Hkv * D, E), "w_o": w(E, H * D),
                 "q_norm": gamma(D) if shape.qk_norm else None, "k_norm": gamma(D) if shape.qk_norm else None,
                 "w_gate": w(I, E), "w_up": w(I, E), "w_down": w(E, I)})
+        if fp8:
+            for lw in self.layers:
+                for name in ("w_q", "w_k", "w_v", "w_o", "w_gate", "w_up", "w_down"):
+                    lw[name] = rt.Fp8Weight.quantize(lw[name])
+
+    def dequantized(self) -> "DecoderModel":
+        """The same model with every FP8 projection dequantized the reference's way
+        (DequantizeFP8, QwenRunner.cpp:103-122): what the reference runner multiplies."""
+        import copy
+        m = copy.copy(self)
+        m.layers = [{k: (v.dequantize() if isinstance(v, rt.Fp8Weight) else v) for k, v in lw.items()}
+                    for lw in self.layers]
+        return m
 
     def new_caches(self, num_blocks: int, block_size: int = 256, max_seqs: int = 64,
                    max_blocks_per_seq: int | None = None):

@@ -142,3 +142,15 @@ def test_varlen_argument_validation(lib):
     assert epi(batch=0) == 1
     assert epi(qn=16) == 1 and b"norm weights" in lib.mllm_attn_last_error()
     assert epi(total=0, cu_=None, batch=0) == 0
+
+
+def test_linear_fp8_argument_validation(lib):
+    """mllm_linear_fp8_bf16 rejects unsupported shapes on the host, before any device call."""
+    def call(tokens=32, K=4096, N=4096, wstride=4096):
+        return lib.mllm_linear_fp8_bf16(16, K, tokens, K, 16, wstride, N, 16, K // 128, 16, N, None, 0, None)
+    assert call(tokens=129) == 1 and b"tokens" in lib.mllm_attn_last_error()
+    assert call(K=4160) == 1 and b"multiple of 128" in lib.mllm_attn_last_error()
+    assert call(N=4000) == 1 and b"multiple of 128" in lib.mllm_attn_last_error()
+    assert call(wstride=4000) == 1
+    assert call(tokens=0) == 0          # nothing to do, no device needed
+    assert lib.mllm_linear_fp8_workspace_size(129, 4096, 4096) == 0
