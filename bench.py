@@ -634,8 +634,75 @@ def run_gpu(args, rank, world, device):
             layer_modes["seqpar_comm"] = lambda: sp_comm(attn2d, w_o_full)
             ex_l = PeerExchange(Bp * S, HIDDEN, sub=4)
             layer_modes["peer_exchange"] = lambda: ex_l(attn2d, w_o)
+        # The same layer in micro-batches of sequences: each micro-batch's o_proj + exchange runs
+        # on a high-priority side stream while the next micro-batch's epilogue + attention runs
+        # (mllm_b200.tp.run_micro_batches); Bp / M sequences per micro-batch.
+        from mllm_b200.tp import run_micro_batches
+
+        def epi_mb(b0, nb):
+            off = b0 * S * prow * 2
+            kv_off = b0 * psb * 2
+            st = lib.mllm_qkv_epilogue_bf16(
+                qkv_p.data_ptr() + off, S * prow, prow, D,
+                qkv_p.data_ptr() + off + Hr * D * 2, S * prow, prow, D,
+                qkv_p.data_ptr() + off + (Hr + Hkvr) * D * 2, S * prow, prow, D,
+                nb, S, Hr, Hkvr, D, pos_p.data_ptr(), 0, 1, THETA, None, None, 0, 0,
+                gq.data_ptr(), gk.data_ptr(), EPS, qp.data_ptr() + b0 * Hr * S * D * 2,
+                kp.data_ptr() + kv_off, vp.data_ptr() + kv_off, psb, psh, pst, S, start_p.data_ptr(), 0,
+                torch.cuda.current_stream().cuda_stream)
+            assert st == 0, lib.mllm_attn_last_error()
+
+        def attn_mb(b0, nb):
+            kv_off = b0 * psb * 2
+            st = lib.mllm_prefill_attention_bf16(qp.data_ptr() + b0 * Hr * S * D * 2, kp.data_ptr() + kv_off,
+                                                 vp.data_ptr() + kv_off, psb, psh, pst, nb, Hr, Hkvr, D, S, S, scale,
+                                                 op.data_ptr() + b0 * S * Hr * D * 2,
+                                                 torch.cuda.current_stream().cuda_stream)
+            assert st == 0, lib.mllm_attn_last_error()
+
+        pipelined = {}
+        if world > 1:
+            comm_side = torch.cuda.Stream(device=device, priority=-1)
+            for M in (2, 4):
+                nb = Bp // M
+                rows = nb * S
+
+                def compute(m, nb=nb):
+                    epi_mb(m * nb, nb)
+                    attn_mb(m * nb, nb)
+
+                def ex_allreduce(m, rows=rows):
+                    a, b = m * rows, (m + 1) * rows
+                    torch.matmul(attn2d[a:b], w_o.t(), out=o_part[a:b])
+                    comm.all_reduce(o_part[a:b])
+
+                sp_m = SeqParallelOProj(rows, HIDDEN, comm=comm)
+
+                def ex_seqpar(m, rows=rows, sp_m=sp_m):
+                    a, b = m * rows, (m + 1) * rows
+                    sp_m(attn2d[a:b], w_o_full)
+
+                pipelined[f"micro{M}_gemm_then_comm_allreduce"] = (compute, ex_allreduce, M)
+                pipelined[f"micro{M}_seqpar_comm"] = (compute, ex_seqpar, M)
+            for name, (compute, exch, M) in pipelined.items():
+                layer_modes[name] = (lambda compute=compute, exch=exch, M=M:
+                                     run_micro_batches(compute, exch, M, comm_side))
         layer_ms = {}
         for name, exch in layer_modes.items():
+            if name.startswith("micro"):
+                # the whole layer is the schedule itself
+                for _ in range(2):
+                    exch()
+                barrier()
+                torch.cuda.synchronize()
+                p0.record(stream)
+                for i in range(ksteps):
+                    exch()
+                p1.record(stream)
+                torch.cuda.synchronize()
+                barrier()
+                layer_ms[name] = max_over_ranks(p0.elapsed_time(p1)) / ksteps
+                continue
             for _ in range(2):
                 epi_p()
                 attn_p()
@@ -1343,7 +1410,9 @@ def main():
                     "the all-reduce of the [B*S, hidden] partial (torch NCCL, or the library's mllm_comm); "
                     "chunked_overlap: the GEMM in 4 pieces overlapping their all-reduces; seqpar_*: attention "
                     "rows all-to-all to their row's owner, full-K o_proj there, all-gather of the output rows "
-                    "(torch NCCL, or mllm_comm for the all-gather); peer_exchange: pull-sum-push over peer memory"}
+                    "(torch NCCL, or mllm_comm for the all-gather); peer_exchange: pull-sum-push over peer memory; "
+                    "microM_*: the 4 sequences in M micro-batches, each micro-batch's o_proj + exchange on a "
+                    "high-priority stream while the next micro-batch's epilogue + attention runs"}
     if res["rag"] is not None:
         r = res["rag"]
         ach = r["bytes_per_rank"] / (r["ms"] * 1e-3) / 1e9

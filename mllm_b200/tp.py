@@ -295,6 +295,32 @@ class SeqParallelOProj:
         return out
 
 
+def run_micro_batches(compute, exchange, count: int, comm_stream=None):
+    """Overlaps the o_proj exchange of one micro-batch with the attention of the next.
+
+    The prefill rows of a head-sharded layer are independent per sequence, so the layer can run
+    in `count` micro-batches (groups of sequences): compute(m) enqueues micro-batch m's epilogue
+    and attention on the current stream; exchange(m) -- its o_proj GEMM and collective -- is
+    enqueued on `comm_stream` (a high-priority stream, so its kernels take SMs as soon as the
+    attention grid frees them) after an event that marks compute(m).  The exchange of micro-batch
+    m therefore runs while micro-batch m + 1 computes, and only the last exchange is exposed.
+    The current stream waits for every exchange before it returns.  Every rank must call it with
+    the same count (the collectives are matched in order)."""
+    import torch
+    cur = torch.cuda.current_stream()
+    if comm_stream is None:
+        comm_stream = torch.cuda.Stream(device=cur.device, priority=-1)
+    for m in range(count):
+        compute(m)
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        comm_stream.wait_event(ev)
+        with torch.cuda.stream(comm_stream):
+            exchange(m)
+    cur.wait_stream(comm_stream)
+    return comm_stream
+
+
 def tp_attention_block(h, shard: HeadShard, head_dim: int, rope_theta: float, position_ids, kv_cache,
                        w_q, w_k, w_v, w_o, w_q_norm=None, w_k_norm=None, rms_norm_eps: float = 1e-6,
                        group=None, attention_fn=None, overlap_chunks: int = 4, exchange=None, comm=None):
