@@ -687,6 +687,32 @@ def run_gpu(args, rank, world, device):
             for name, (compute, exch, M) in pipelined.items():
                 layer_modes[name] = (lambda compute=compute, exch=exch, M=M:
                                      run_micro_batches(compute, exch, M, comm_side))
+        if world > 1:
+            # token rows in, token rows out (tp.UlyssesLayout): this rank's q/k/v projections of
+            # its T/N token rows (all heads), one all-to-all to the head owners, the epilogue and
+            # attention on this rank's heads, one all-to-all back, o_proj of its rows with the
+            # whole w_o.  The layer's input and output stay sharded by token rows.
+            from mllm_b200.tp import UlyssesLayout, shard_heads
+            uly = UlyssesLayout(shard_heads(H, HKV, world, rank), H, HKV, D)
+            # the projections of this rank's rows, as UlyssesLayout.project writes them: [N, T/N, cols]
+            qkv_send = (torch.randn(world, Bp * S // world, (Hr + 2 * Hkvr) * D, device=device, generator=gen)
+                        * 0.5).bfloat16()
+            out_tok = torch.empty(Bp * S // world, HIDDEN, dtype=torch.bfloat16, device=device)
+
+            def ulysses_layer():
+                qkv_h = uly.heads_from_tokens_packed(qkv_send)   # [B*S, (Hr + 2 Hkvr) D], qkv_p's layout
+                st = lib.mllm_qkv_epilogue_bf16(
+                    qkv_h.data_ptr(), S * prow, prow, D,
+                    qkv_h.data_ptr() + Hr * D * 2, S * prow, prow, D,
+                    qkv_h.data_ptr() + (Hr + Hkvr) * D * 2, S * prow, prow, D,
+                    Bp, S, Hr, Hkvr, D, pos_p.data_ptr(), 0, 1, THETA, None, None, 0, 0,
+                    gq.data_ptr(), gk.data_ptr(), EPS, qp.data_ptr(), kp.data_ptr(), vp.data_ptr(),
+                    psb, psh, pst, S, start_p.data_ptr(), 0, torch.cuda.current_stream().cuda_stream)
+                assert st == 0, lib.mllm_attn_last_error()
+                attn_p()
+                torch.matmul(uly.tokens_from_heads(attn2d), w_o_full.t(), out=out_tok)
+
+            layer_modes["micro1_ulysses_token_rows_io"] = ulysses_layer
         layer_ms = {}
         for name, exch in layer_modes.items():
             if name.startswith("micro"):
@@ -889,6 +915,34 @@ def tp_parity_leg(rank, world, device, comm, barrier):
     shard = tp.shard_heads(H, HKV, world, rank)
     wq, wk, wv, wo = tp.shard_weights(shard, D, w["w_q"], w["w_k"], w["w_v"], w["w_o"])
     modes = {}
+    # Ulysses layout (tp.UlyssesLayout): this rank's token rows projected with the whole weights,
+    # q/k/v to the head owners, attention on this rank's heads, rows back to their owners, o_proj
+    # with the whole w_o; this rank's output rows against the same rows of the unsharded layer.
+    # The decode steps (2 rows) run head-sharded with the all-reduce.
+    lay = tp.UlyssesLayout(shard, H, HKV, D)
+    c = rt.KVCache(TP_B, shard.num_kv_heads, D, TP_S + TP_STEPS)
+    T = TP_B * TP_S
+    Tn = T // world
+    rows = slice(rank * Tn, (rank + 1) * Tn)
+    w_packed = lay.pack_qkv_weights(w["w_q"], w["w_k"], w["w_v"])
+    qkv_h = lay.heads_from_tokens_packed(lay.project(xs[0].view(T, HIDDEN)[rows], w_packed))
+    Hr, Hkvr = shard.num_heads, shard.num_kv_heads
+    qh = qkv_h[:, :Hr * D].view(TP_B, TP_S, Hr, D).transpose(1, 2)
+    kh = qkv_h[:, Hr * D:(Hr + Hkvr) * D].view(TP_B, TP_S, Hkvr, D).transpose(1, 2)
+    vh = qkv_h[:, (Hr + Hkvr) * D:].view(TP_B, TP_S, Hkvr, D).transpose(1, 2)
+    att = rt.Attention.forward_projected(qh, kh, vh, None, Hr, Hkvr, D, THETA, pos(0), c, gq, gk, EPS)
+    out_rows = torch.nn.functional.linear(lay.tokens_from_heads(att.reshape(T, Hr * D)), w["w_o"]).float()
+    ref_rows = ref[0].view(T, HIDDEN)[rows]
+    excess = float((out_rows - ref_rows).abs().sub(2e-2 + 2e-2 * ref_rows.abs()).max())
+    for i in range(1, len(xs)):
+        out = tp.tp_attention_block(xs[i], shard, D, THETA, pos(i), c, wq, wk, wv, wo, gq, gk, EPS,
+                                    comm=comm).float()
+        excess = max(excess, float((out - ref[i]).abs().sub(2e-2 + 2e-2 * ref[i].abs()).max()))
+    torch.cuda.synchronize()
+    t = torch.tensor([excess], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    modes["ulysses"] = {"max_excess": float(t.item()), "ok": float(t.item()) <= 0.0}
+    barrier()
     for mode in ("nccl_chunked", "comm", "peer", "seqpar"):
         ex = {}
         if mode == "peer":
@@ -1412,7 +1466,10 @@ def main():
                     "rows all-to-all to their row's owner, full-K o_proj there, all-gather of the output rows "
                     "(torch NCCL, or mllm_comm for the all-gather); peer_exchange: pull-sum-push over peer memory; "
                     "microM_*: the 4 sequences in M micro-batches, each micro-batch's o_proj + exchange on a "
-                    "high-priority stream while the next micro-batch's epilogue + attention runs"}
+                    "high-priority stream while the next micro-batch's epilogue + attention runs; "
+                    "micro1_ulysses_token_rows_io: the layer's input and output sharded by token rows "
+                    "(mllm_b200.tp.UlyssesLayout: q/k/v all-to-all to the head owners, attention, all-to-all "
+                    "back, o_proj of the rank's rows with the whole w_o) -- no output is replicated"}
     if res["rag"] is not None:
         r = res["rag"]
         ach = r["bytes_per_rank"] / (r["ms"] * 1e-3) / 1e9

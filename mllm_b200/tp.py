@@ -295,6 +295,90 @@ class SeqParallelOProj:
         return out
 
 
+class UlyssesLayout:
+    """Head-parallel attention with token-parallel layer input and output.
+
+    Tensor parallelism replicates the layer's output: every rank ends with all T rows (an
+    all-reduce of partials, or an all-gather of rows), which moves about (N-1)/N of the whole
+    [T, hidden] output into every GPU per layer.  In this layout rank r owns token rows
+    [r T/N, (r+1) T/N) between attention blocks -- the norms, the q/k/v projections (whole
+    weights) and the MLP run on those rows only -- and attention still runs on its KV-head group
+    over all tokens:
+
+      heads_from_tokens: q/k/v of my token rows, all heads [T/N, (H + 2 Hkv) D]  ->  q/k/v of
+          all token rows, my heads [T, (Hr + 2 Hkvr) D]   (one all-to-all)
+      attention on my heads (epilogue + prefill, unchanged)
+      tokens_from_heads: attention output of my heads [T, Hr D]  ->  all heads' outputs of my
+          token rows [T/N, H D]   (one all-to-all), then o_proj with the whole w_o on those rows.
+
+    Per rank and layer that is (N-1)/N of [T/N, (H + 2 Hkv) D] and of [T, Hr D] -- for Qwen3-8B,
+    T = 32768 at 8 GPUs, 44 MB and 29 MB -- instead of 235 MB or more.  Every o_proj row is one
+    full-K GEMM, as on one GPU.  T must be a multiple of N; the heads' order is the ranks' order
+    (shard_heads), so rank q's columns are heads [q Hr, (q+1) Hr) of q, k and v."""
+
+    def __init__(self, shard: HeadShard, num_heads: int, num_kv_heads: int, head_dim: int, group=None):
+        import torch.distributed as dist
+        self.shard, self.group = shard, group
+        self.N = dist.get_world_size(group)
+        self.H, self.Hkv, self.D = num_heads, num_kv_heads, head_dim
+
+    def pack_qkv_weights(self, w_q, w_k, w_v):
+        """The q/k/v weights regrouped by destination rank: [N, (Hr + 2 Hkvr) D, hidden], rank q's
+        block its q heads, then its k heads, then its v heads.  project() with it writes the
+        all-to-all's send buffer directly."""
+        import torch
+        N, D = self.N, self.D
+        Hr, Hkvr = self.H // N, self.Hkv // N
+        blocks = []
+        for q in range(N):
+            blocks.append(torch.cat([w_q[q * Hr * D:(q + 1) * Hr * D], w_k[q * Hkvr * D:(q + 1) * Hkvr * D],
+                                     w_v[q * Hkvr * D:(q + 1) * Hkvr * D]], 0))
+        return torch.stack(blocks, 0).contiguous()
+
+    def project(self, h_tok, w_packed):
+        """q/k/v projections of this rank's token rows h_tok [T/N, hidden] with pack_qkv_weights'
+        weights: the send buffer [N, T/N, (Hr + 2 Hkvr) D] of heads_from_tokens_packed."""
+        import torch
+        return torch.matmul(h_tok.unsqueeze(0), w_packed.transpose(1, 2))
+
+    def heads_from_tokens_packed(self, send):
+        """send [N, T/N, (Hr + 2 Hkvr) D] (block q for rank q) -> [T, (Hr + 2 Hkvr) D], every token
+        row of this rank's heads, in token order: one all-to-all, no copy."""
+        import torch
+        import torch.distributed as dist
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=self.group)
+        return recv.view(-1, send.shape[2])
+
+    def heads_from_tokens(self, qkv_tok):
+        """qkv_tok [T/N, (H + 2 Hkv) D] (q | k | v of this rank's token rows) -> [T, (Hr + 2 Hkvr) D]
+        (q | k | v of this rank's heads for every token row, rows in token order)."""
+        import torch
+        import torch.distributed as dist
+        N, D = self.N, self.D
+        Hr, Hkvr = self.H // N, self.Hkv // N
+        Tn = qkv_tok.shape[0]
+        x = qkv_tok.view(Tn, -1)
+        q = x[:, :self.H * D].view(Tn, N, Hr * D)
+        k = x[:, self.H * D:(self.H + self.Hkv) * D].view(Tn, N, Hkvr * D)
+        v = x[:, (self.H + self.Hkv) * D:].view(Tn, N, Hkvr * D)
+        send = torch.cat([q, k, v], dim=2).transpose(0, 1).contiguous()   # [N, Tn, (Hr + 2 Hkvr) D]
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=self.group)
+        return recv.view(N * Tn, -1)
+
+    def tokens_from_heads(self, attn):
+        """attn [T, Hr D] (this rank's heads, every token row) -> [T/N, H D] (every head, this rank's
+        token rows)."""
+        import torch
+        import torch.distributed as dist
+        N = self.N
+        T, Hd = attn.shape
+        recv = torch.empty((N, T // N, Hd), dtype=attn.dtype, device=attn.device)
+        dist.all_to_all_single(recv, attn.contiguous(), group=self.group)
+        return recv.permute(1, 0, 2).reshape(T // N, N * Hd)
+
+
 def run_micro_batches(compute, exchange, count: int, comm_stream=None):
     """Overlaps the o_proj exchange of one micro-batch with the attention of the next.
 

@@ -172,3 +172,86 @@ def test_sequence_parallel_oproj_equals_unsharded():
         assert p.exitcode == 0
     for r, got, want in res:
         np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5, err_msg=f"rank {r}")
+
+
+def _ulysses_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        T, H, Hkv, D = 16, 8, 4, 8
+        g = torch.Generator().manual_seed(11)
+        qkv_all = torch.randn(T, (H + 2 * Hkv) * D, generator=g)     # every token's q | k | v
+        shard = tp.shard_heads(H, Hkv, world, rank)
+        lay = tp.UlyssesLayout(shard, H, Hkv, D)
+        Tn = T // world
+        mine = qkv_all[rank * Tn:(rank + 1) * Tn]
+        heads = lay.heads_from_tokens(mine)
+        # the expected rows: q | k | v columns of this rank's heads, every token
+        q0, q1 = shard.q_heads[0] * D, shard.q_heads[1] * D
+        k0, k1 = shard.kv_heads[0] * D, shard.kv_heads[1] * D
+        want = torch.cat([qkv_all[:, q0:q1], qkv_all[:, H * D + k0:H * D + k1],
+                          qkv_all[:, (H + Hkv) * D + k0:(H + Hkv) * D + k1]], 1)
+        attn_all = torch.randn(T, H * D, generator=g)                 # every head's attention rows
+        back = lay.tokens_from_heads(attn_all[:, q0:q1].contiguous())
+        q.put((rank, torch.equal(heads, want), torch.equal(back, attn_all[rank * Tn:(rank + 1) * Tn])))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ulysses_layout_moves_rows_between_token_and_head_owners():
+    """UlyssesLayout: q/k/v of token rows to the owners of their heads, and attention rows back to
+    the owners of their tokens, exactly (2 gloo ranks)."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ulysses_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r, heads_ok, back_ok in res:
+        assert heads_ok and back_ok, r
+
+
+def _ulysses_packed_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        T, E, H, Hkv, D = 16, 24, 8, 4, 8
+        g = torch.Generator().manual_seed(12)
+        h = torch.randn(T, E, generator=g)
+        w_q, w_k, w_v = (torch.randn(n * D, E, generator=g) for n in (H, Hkv, Hkv))
+        shard = tp.shard_heads(H, Hkv, world, rank)
+        lay = tp.UlyssesLayout(shard, H, Hkv, D)
+        Tn = T // world
+        got = lay.heads_from_tokens_packed(lay.project(h[rank * Tn:(rank + 1) * Tn],
+                                                       lay.pack_qkv_weights(w_q, w_k, w_v)))
+        q0, q1 = shard.q_heads[0] * D, shard.q_heads[1] * D
+        k0, k1 = shard.kv_heads[0] * D, shard.kv_heads[1] * D
+        want = torch.cat([h @ w_q[q0:q1].t(), h @ w_k[k0:k1].t(), h @ w_v[k0:k1].t()], 1)
+        q.put((rank, float((got - want).abs().max())))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ulysses_packed_projection_lands_on_the_head_owners():
+    """UlyssesLayout.project with pack_qkv_weights writes the all-to-all's send buffer directly;
+    after heads_from_tokens_packed every rank holds its heads' q/k/v for every token row."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ulysses_packed_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r, err in res:
+        assert err < 1e-5, (r, err)
