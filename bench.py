@@ -1450,7 +1450,7 @@ def main():
         epi_gbs = p["epi_bytes"] / (p["epi_ms"] * 1e-3) / 1e9
         line["prefill"]["qkv_epilogue"] = {
             "ms": p["epi_ms"], "tokens": PRE_B * PRE_S,
-            "roofline": {"bound": "hbm", "kernel": "qkv_epilogue_row_kernel<128>", "achieved": epi_gbs,
+            "roofline": {"bound": "hbm", "kernel": "qkv_epilogue_tma_kernel<128, 1>", "achieved": epi_gbs,
                          "peak": hbm_peak, "unit": "GB/s", "frac": epi_gbs / hbm_peak, "peak_source": peak_src,
                          "algorithmic_bytes": p["epi_bytes"],
                          "note": "q/k/v head rows read once, q rows and the K/V cache rows written once"}}

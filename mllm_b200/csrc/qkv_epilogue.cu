@@ -344,212 +344,353 @@ __global__ void __launch_bounds__(256, (D == 128 && RPQ >= 4) ? 2 : 3) qkv_epilo
 }
 
 // ---------------------------------------------------------------------------------------------
-// Many tokens, a thread per head row: each thread brings its whole row into registers with
-// 16-byte loads (D/8 of them), norms and rotates it there and writes it with 16-byte stores.
+// Many tokens: the rows of kStTokens consecutive tokens of one sequence (a "group") move between
+// HBM and shared memory as TMA tensor boxes, and a thread per q/k row transforms them in place.
+//
+// A persistent block takes groups in turn.  Per group:
+//   1. One thread loads the group's q, k and v rows: per tensor and 64-column half, one box of
+//      {64 columns, kStTokens tokens, all heads} (128-byte swizzle), all completing on the
+//      stage's mbarrier -- six copies for the whole group at head_dim 128.
+//   2. The block computes the group's RoPE angles once.
+//   3. A thread per q/k row norms and rotates its row in place: a first pass sums the squares,
+//      a second scales, rounds and rotates the pairs (d, d + D/2).  Row r of a box holds head
+//      r / kStTokens of token r % kStTokens, and its 16-byte chunk c sits at chunk c ^ (r % 8) of
+//      its 128 bytes, so the 32 rows a warp reads at once fall in different bank groups.
+//   4. One thread stores the boxes: q to q_out ([B, H, S, D], the same box shape, rows past the
+//      sequence end clipped by the TMA unit), k and v to the cache when the group's four cache rows
+//      are consecutive rows of one sequence or block.  Otherwise (a group that ends a sequence,
+//      crosses a packed sequence or a cache block, or holds a refused row) the threads write the
+//      group's valid cache rows with 16-byte stores.
+// Three or four blocks per SM overlap one another's copies with their arithmetic.  (Two stages per block,
+// the next group's copies issued before the current group is computed, measured slower: the
+// second stage's shared memory leaves room for two blocks per SM only.)
 //
 // One thread per row keeps the reference's reduction entirely in registers: element d of the row
 // belongs to accumulator P_k[j] with j = d % 8, k = (d / 8) % 4, visited in order of d / 32, then
 // acc_j = ((P0 + P1) + P2) + P3 and the total sums acc_0 .. acc_7 in order -- the order of the
 // quarter-warp and warp kernels (qkv_math.cuh), with no exchange between lanes.  Every fp32 step
-// is the same explicitly rounded operation (the two scaling products of the norm as one f32x2
-// instruction: a product feeding a product, nothing to contract), so the outputs are
-// bit-identical to theirs.
-//
-// A block takes kRowTokens consecutive tokens: their RoPE angles are computed once (position-
-// independent factors once per block) into shared memory, then thread t takes rows t, t + 256, ...
-// of the block's tokens x heads (three per thread for the Qwen3-8B geometry).  Preconditions
-// (checked on the host): every row 16-byte aligned.
+// is the same explicitly rounded operation: products two at a time (one f32x2 multiply rounds each
+// lane as the scalar multiply does), and every sum a scalar __fadd_rn / __fsub_rn, so that no
+// product is contracted into its sum.  The outputs are bit-identical to the other kernels'.
 // ---------------------------------------------------------------------------------------------
-constexpr int kRowTokens = 16;
-constexpr int kRowThreads = 256;
+constexpr int kStTokens = 4;
+constexpr int kStMaxThreads = 192;   // a thread per row up to 48 q+k heads; more heads loop
+constexpr int kStMinBlocks = 3;      // at least three blocks per SM: at most 113 registers a thread
 
-__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        f[2 * i] = __uint_as_float(w[i] << 16);
-        f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-    }
+// A pair of fp32 values in one 64-bit register, element 0 in the low half.
+typedef unsigned long long f32x2;
+
+__device__ __forceinline__ f32x2 f2_make(float lo, float hi) {
+    f32x2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
 }
-
-__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
-    uint4 v;
-    v.x = pack_bf16x2(f[0], f[1]);
-    v.y = pack_bf16x2(f[2], f[3]);
-    v.z = pack_bf16x2(f[4], f[5]);
-    v.w = pack_bf16x2(f[6], f[7]);
-    return v;
+__device__ __forceinline__ void f2_split(f32x2 v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
 }
-
-// 8 consecutive fp32 from 16-byte aligned shared memory
-__device__ __forceinline__ void load8f(const float* p, float (&f)[8]) {
-    const float4 u = reinterpret_cast<const float4*>(p)[0];
-    const float4 w = reinterpret_cast<const float4*>(p)[1];
-    f[0] = u.x; f[1] = u.y; f[2] = u.z; f[3] = u.w;
-    f[4] = w.x; f[5] = w.y; f[6] = w.z; f[7] = w.w;
-}
-
-// (d0, d1) = (a0 * b0, a1 * b1), each product rounded to nearest (one f32x2 instruction)
-__device__ __forceinline__ void mul2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-    unsigned long long a, b, d;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(b0), "f"(b1));
+__device__ __forceinline__ f32x2 f2_mul(f32x2 a, f32x2 b) {
+    f32x2 d;
     asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
+    return d;
+}
+// the two bf16 of a 32-bit word (element 0 in the low half), widened exactly
+__device__ __forceinline__ f32x2 f2_from_bf16x2(uint32_t w) {
+    return f2_make(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+// both rounded to bf16 (nearest even), element 0 in the low half
+__device__ __forceinline__ uint32_t f2_to_bf16x2(f32x2 v) {
+    float lo, hi;
+    f2_split(v, lo, hi);
+    return pack_bf16x2(lo, hi);
 }
 
-// both values rounded to bf16 precision (round to nearest even) and widened back, exactly as
-// __bfloat162float(__float2bfloat16_rn(x)) does for each
-__device__ __forceinline__ void round_bf16x2(float& x0, float& x1) {
-    const uint32_t w = pack_bf16x2(x0, x1);
-    x0 = __uint_as_float(w << 16);
-    x1 = __uint_as_float(w & 0xffff0000u);
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2,
+                                             int c3) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+                 : "memory");
 }
+
+// Shared memory of the TMA kernel for head dimension D, H q heads and Hkv kv heads: the boxes
+// (q, k, v; per tensor one region per 64-column half, each a multiple of 1 KB), then the angles,
+// gamma, inv_freq, the per-token cache rows (3 ints per token) and the mbarrier.
+template <int D>
+struct TmaEpiSmem {
+    static constexpr int kHalves = D / 64;
+    // floats per token in the angle table (cos | sin | 4 of padding): the rows a warp transforms
+    // belong to four tokens, whose table reads then fall in different bank groups
+    static constexpr int kAng = 2 * D + 4;
+    __host__ __device__ static uint32_t region(int heads) { return ((uint32_t)kStTokens * heads * 128 + 1023) & ~1023u; }
+    __host__ __device__ static uint32_t stage_bytes(int H, int Hkv) { return kHalves * (region(H) + 2 * region(Hkv)); }
+    __host__ __device__ static size_t bytes(int H, int Hkv) {
+        return 1024 + (size_t)stage_bytes(H, Hkv) + (size_t)kStTokens * kAng * 4 + 2 * D * 4 + (D / 2) * 4 +
+               kStTokens * 3 * 4 + 16;
+    }
+};
 
 template <int D>
-__global__ void __launch_bounds__(kRowThreads, 2) qkv_epilogue_row_kernel(EpilogueArgs a, int ntok) {
-    constexpr int NC = D / 8;            // 16-byte chunks per row
-    constexpr int AS = 2 * D + 4;        // floats per token in the angle table (cos, sin, pad)
-    __shared__ __align__(16) float s_ang[kRowTokens * AS];
-    __shared__ __align__(16) float s_gamma[2 * D];
-    __shared__ float s_inv_freq[D / 2];
+__global__ void __launch_bounds__(kStMaxThreads, kStMinBlocks) qkv_epilogue_tma_kernel(
+    const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmQo,
+    const __grid_constant__ CUtensorMap tmKc, const __grid_constant__ CUtensorMap tmVc, EpilogueArgs a) {
+    using L = TmaEpiSmem<D>;
+    constexpr int HALVES = L::kHalves;
+    constexpr int NC = D / 8;                     // 16-byte chunks per row
+    constexpr int KT = kStTokens;
+    extern __shared__ unsigned char tma_smem_raw[];
+    unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tma_smem_raw) + 1023) &
+                                                         ~uintptr_t(1023));
+    const int H = a.H, Hkv = a.Hkv, qk = H + Hkv;
+    const uint32_t rq = L::region(H), rkv = L::region(Hkv);
+    const uint32_t stage_bytes = L::stage_bytes(H, Hkv);
+    float* s_ang = reinterpret_cast<float*>(sm + stage_bytes);
+    float* s_gamma = s_ang + KT * L::kAng;
+    float* s_inv_freq = s_gamma + 2 * D;
+    int* s_rows = reinterpret_cast<int*>(s_inv_freq + D / 2);   // [KT][3]: seq, block, row (-1: none)
+    uint64_t* s_bar = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(s_rows + KT * 3) + 7) & ~uintptr_t(7));
 
     pdl_trigger();   // a decode launched next may start its set-up (it waits for this grid)
     const int tid = threadIdx.x;
-    const int th = a.H + 2 * a.Hkv;
-    const int t0 = blockIdx.x * kRowTokens;
-    const int nt = min(kRowTokens, ntok - t0);
+    const int nthr = blockDim.x;
+    const int groups_per_seq = (a.S + KT - 1) / KT;
+    const int ngroups = a.B * groups_per_seq;
     const bool norm = a.q_gamma != nullptr;
     const bool tables = a.rope_cos != nullptr;
+    // box base of tensor `ten` (0 q, 1 k, 2 v), 64-column half `x`
+    auto box = [&](int ten, int x) -> unsigned char* {
+        unsigned char* b = sm;
+        if (ten == 0) return b + x * rq;
+        b += HALVES * rq;
+        if (ten == 1) return b + x * rkv;
+        return b + HALVES * rkv + x * rkv;
+    };
+    auto group_of = [&](int g, int& b, int& s0, int& nt) {
+        b = g / groups_per_seq;
+        s0 = (g - b * groups_per_seq) * KT;
+        nt = min(KT, a.S - s0);
+    };
+    // cache rows of the group's tokens (-1 block: not written, the error recorded)
+    auto prep = [&](int g) {
+        int b, s0, nt;
+        group_of(g, b, s0, nt);
+        if (tid < KT) {
+            int* o = s_rows + tid * 3;
+            o[0] = -1; o[1] = -1; o[2] = -1;
+            if (tid < nt) {
+                int seq, blk, rw;
+                const int64_t slot = cache_slot(a, b, s0 + tid, seq);
+                if (slot < 0 || slot >= a.capacity || !kv_locate(a.lay, seq, slot, blk, rw)) {
+                    record_error(kErrBadLength);
+                } else {
+                    o[0] = seq; o[1] = blk; o[2] = rw;
+                }
+            }
+        }
+    };
+    // one thread: the group's boxes
+    auto issue = [&](int g) {
+        int b, s0, nt;
+        group_of(g, b, s0, nt);
+        mbar_arrive_expect_tx(s_bar, (uint32_t)(KT * (H + 2 * Hkv) * D * 2));
+#pragma unroll
+        for (int x = 0; x < HALVES; ++x) {
+            tma_load_4d(box(0, x), &tmQ, s_bar, x * 64, s0, 0, b);
+            tma_load_4d(box(1, x), &tmK, s_bar, x * 64, s0, 0, b);
+            tma_load_4d(box(2, x), &tmV, s_bar, x * 64, s0, 0, b);
+        }
+    };
 
+    if (tid == 0) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+        tma_prefetch_desc(&tmQo);
+        tma_prefetch_desc(&tmKc);
+        tma_prefetch_desc(&tmVc);
+        mbar_init(s_bar, 1);
+        mbar_fence_init();
+    }
     if (norm) {
-        for (int d = tid; d < D; d += kRowThreads) {
+        for (int d = tid; d < D; d += nthr) {
             s_gamma[d] = __bfloat162float(a.q_gamma[d]);
             s_gamma[D + d] = __bfloat162float(a.k_gamma[d]);
         }
     }
     if (!tables) {
-        for (int jc = tid; jc < D / 2; jc += kRowThreads) s_inv_freq[jc] = rope_angle(1, jc, D, a.log_theta);
+        for (int jc = tid; jc < D / 2; jc += nthr) s_inv_freq[jc] = rope_angle(1, jc, D, a.log_theta);
     }
-    __syncthreads();
-    if (tables) {
-        for (int idx = tid; idx < nt * D; idx += kRowThreads) {
-            const int tl = idx / D, col = idx - tl * D;
-            const int token = t0 + tl;
-            const int b = token / a.S, s = token - b * a.S;
-            const int64_t row = (int64_t)b * a.rope_row_sb + (int64_t)s * a.rope_row_ss;
-            s_ang[tl * AS + col] = a.rope_cos[row * D + col];
-            s_ang[tl * AS + D + col] = a.rope_sin[row * D + col];
-        }
-    } else {
-        // rope_angle: float(pos) * inv_freq[col], then cos / sin, for the first half only (the
-        // second half of a computed table equals the first)
-        for (int idx = tid; idx < nt * (D / 2); idx += kRowThreads) {
-            const int tl = idx / (D / 2), col = idx - tl * (D / 2);
-            const int token = t0 + tl;
-            const int b = token / a.S, s = token - b * a.S;
-            const float angle =
-                __fmul_rn((float)a.positions[(int64_t)b * a.pos_sb + (int64_t)s * a.pos_ss], s_inv_freq[col]);
-            s_ang[tl * AS + col] = cosf(angle);
-            s_ang[tl * AS + D + col] = sinf(angle);
-        }
-    }
-    __syncthreads();
+    __syncthreads();   // barriers initialised
 
-    const int rows = nt * th;
-#pragma unroll 1
-    for (int r = tid; r < rows; r += kRowThreads) {
-        const int tl = r / th, head = r - tl * th;
-        const int token = t0 + tl;
-        const int b = token / a.S, s = token - b * a.S;
-        const HeadRef hr = locate_head(a, head, b, s);
-        __nv_bfloat16* dst;
-        if (hr.kind == 0) {
-            dst = a.q_out + (((int64_t)b * a.H + hr.h) * a.S + s) * D;
+    int it = 0;
+    for (int g = blockIdx.x; g < ngroups; g += gridDim.x, ++it) {
+        int b, s0, nt;
+        group_of(g, b, s0, nt);
+        // shared memory is free once the previous group's stores have read it; then this group's
+        // copies go out
+        if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        __syncthreads();
+        prep(g);
+        if (tid == 0) issue(g);
+
+        // RoPE angles of this group's tokens
+        if (tables) {
+            for (int idx = tid; idx < nt * D; idx += nthr) {
+                const int tl = idx / D, col = idx - tl * D;
+                const int64_t row = (int64_t)b * a.rope_row_sb + (int64_t)(s0 + tl) * a.rope_row_ss;
+                s_ang[tl * L::kAng + col] = a.rope_cos[row * D + col];
+                s_ang[tl * L::kAng + D + col] = a.rope_sin[row * D + col];
+            }
         } else {
-            int seq, blk, rw;
-            const int64_t slot = cache_slot(a, b, s, seq);
-            if (slot < 0 || slot >= a.capacity || !kv_locate(a.lay, seq, slot, blk, rw)) {
-                record_error(kErrBadLength);
-                continue;
+            // rope_angle: float(pos) * inv_freq[col], then cos / sin, for the first half only (the
+            // second half of a computed table equals the first)
+            for (int idx = tid; idx < nt * (D / 2); idx += nthr) {
+                const int tl = idx / (D / 2), col = idx - tl * (D / 2);
+                const float angle = __fmul_rn(
+                    (float)a.positions[(int64_t)b * a.pos_sb + (int64_t)(s0 + tl) * a.pos_ss], s_inv_freq[col]);
+                s_ang[tl * L::kAng + col] = cosf(angle);
+                s_ang[tl * L::kAng + D + col] = sinf(angle);
             }
-            dst = (hr.kind == 1 ? a.k_cache : a.v_cache) + blk * a.c_sb + hr.h * a.c_sh + rw * a.c_st;
         }
-        const uint4* src = reinterpret_cast<const uint4*>(hr.src);
-        uint4* out = reinterpret_cast<uint4*>(dst);
-        uint4 v[NC];
-#pragma unroll
-        for (int c = 0; c < NC; ++c) v[c] = src[c];
-        if (hr.kind == 2) {
-#pragma unroll
-            for (int c = 0; c < NC; ++c) out[c] = v[c];
-            continue;
-        }
-        float rr_scale = 1.f;
-        if (norm) {
-            // P_k[j] over the row's chunks c (k = c % 4) in order of c / 4
-            float p[4][8];
-#pragma unroll
-            for (int c = 0; c < NC; ++c) {
-                float x[8];
-                unpack8(v[c], x);
-#pragma unroll
-                for (int jj = 0; jj < 8; ++jj) {
-                    const float sq = __fmul_rn(x[jj], x[jj]);
-                    p[c & 3][jj] = c < 4 ? sq : __fadd_rn(p[c & 3][jj], sq);
-                }
-            }
-            float total = 0.f;
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj)
-                total = __fadd_rn(total, __fadd_rn(__fadd_rn(__fadd_rn(p[0][jj], p[1][jj]), p[2][jj]), p[3][jj]));
-            rr_scale = rms_scale<D>(total, a.eps);
-        }
-        const float* gw = s_gamma + (hr.kind == 0 ? 0 : D);
-        const float* cs = s_ang + tl * AS;
-        const float* sn = cs + D;
-        // RoPE.h:77-88 on the pairs (d, d + D/2): chunks c and c + NC/2
-#pragma unroll
-        for (int c = 0; c < NC / 2; ++c) {
-            float xl[8], xh[8];
-            unpack8(v[c], xl);
-            unpack8(v[c + NC / 2], xh);
+        // this group's boxes landed (one thread waits; a timeout stops the whole block, its error
+        // recorded), and the angles and cache rows are visible
+        const bool landed = tid != 0 || mbar_wait(s_bar, it & 1);
+        if (!__syncthreads_and(landed)) break;
+
+        // a thread per q/k row, in place; rows r = head * KT + token of the q boxes, then the k boxes
+        for (int r = tid; r < KT * qk; r += nthr) {
+            const bool is_q = r < KT * H;
+            const int rr = is_q ? r : r - KT * H;
+            const int tl = rr % KT;
+            if (tl >= nt) continue;
+            unsigned char* base0 = box(is_q ? 0 : 1, 0);
+            const uint32_t region = is_q ? rq : rkv;
+            const uint32_t swz = (uint32_t)(rr & 7);
+            // chunk c of the row: half c / 8, physical chunk (c % 8) ^ (row % 8)
+            auto chunk = [&](int c) -> uint4* {
+                return reinterpret_cast<uint4*>(base0 + (c >> 3) * region + rr * 128 + ((((uint32_t)c & 7u) ^ swz) << 4));
+            };
+            f32x2 rr2 = f2_make(1.f, 1.f);
             if (norm) {
-                // RMSNorm.h:48-63: x * rsqrt(var + eps) * w, cast to bf16
-                float gl[8], gh[8];
-                load8f(gw + 8 * c, gl);
-                load8f(gw + 8 * c + D / 2, gh);
+                // P_k[j] over the row's chunks c (k = c % 4) in order of c / 4: the squares two
+                // at a time, each accumulated with a scalar add
+                float p[4][8];
 #pragma unroll
-                for (int jj = 0; jj < 8; jj += 2) {
-                    mul2(xl[jj], xl[jj + 1], xl[jj], xl[jj + 1], rr_scale, rr_scale);
-                    mul2(xl[jj], xl[jj + 1], xl[jj], xl[jj + 1], gl[jj], gl[jj + 1]);
-                    mul2(xh[jj], xh[jj + 1], xh[jj], xh[jj + 1], rr_scale, rr_scale);
-                    mul2(xh[jj], xh[jj + 1], xh[jj], xh[jj + 1], gh[jj], gh[jj + 1]);
-                    round_bf16x2(xl[jj], xl[jj + 1]);
-                    round_bf16x2(xh[jj], xh[jj + 1]);
+                for (int c = 0; c < NC; ++c) {
+                    const uint4 w = *chunk(c);
+                    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const f32x2 x = f2_from_bf16x2(ww[i]);
+                        float s0q, s1q;
+                        f2_split(f2_mul(x, x), s0q, s1q);
+                        p[c & 3][2 * i] = c < 4 ? s0q : __fadd_rn(p[c & 3][2 * i], s0q);
+                        p[c & 3][2 * i + 1] = c < 4 ? s1q : __fadd_rn(p[c & 3][2 * i + 1], s1q);
+                    }
+                }
+                float total = 0.f;
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj)
+                    total = __fadd_rn(total, __fadd_rn(__fadd_rn(__fadd_rn(p[0][jj], p[1][jj]), p[2][jj]), p[3][jj]));
+                const float rsc = rms_scale<D>(total, a.eps);
+                rr2 = f2_make(rsc, rsc);
+            }
+            const float* gw = s_gamma + (is_q ? 0 : D);
+            const float* cs = s_ang + tl * L::kAng;
+            const float* sn = cs + D;
+            // 8 consecutive fp32 of a table (16-byte aligned), as four pairs
+            auto pairs8 = [](const float* q, f32x2 (&o)[4]) {
+                const ulonglong2 u = reinterpret_cast<const ulonglong2*>(q)[0];
+                const ulonglong2 v = reinterpret_cast<const ulonglong2*>(q)[1];
+                o[0] = u.x; o[1] = u.y; o[2] = v.x; o[3] = v.y;
+            };
+            // RoPE.h:77-88 on the pairs (d, d + D/2): chunks c and c + NC/2
+#pragma unroll
+            for (int c = 0; c < NC / 2; ++c) {
+                uint4* pl = chunk(c);
+                uint4* ph = chunk(c + NC / 2);
+                const uint4 wl = *pl, wh = *ph;
+                const uint32_t wwl[4] = {wl.x, wl.y, wl.z, wl.w};
+                const uint32_t wwh[4] = {wh.x, wh.y, wh.z, wh.w};
+                f32x2 gl[4], gh[4], cl[4], sl[4], ch[4], sh[4];
+                if (norm) {
+                    pairs8(gw + 8 * c, gl);
+                    pairs8(gw + 8 * c + D / 2, gh);
+                }
+                pairs8(cs + 8 * c, cl);
+                pairs8(sn + 8 * c, sl);
+                if (tables) {
+                    pairs8(cs + 8 * c + D / 2, ch);
+                    pairs8(sn + 8 * c + D / 2, sh);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        ch[i] = cl[i];
+                        sh[i] = sl[i];
+                    }
+                }
+                uint32_t ol[4], oh[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    f32x2 xl = f2_from_bf16x2(wwl[i]);
+                    f32x2 xh = f2_from_bf16x2(wwh[i]);
+                    if (norm) {
+                        // RMSNorm.h:48-63: x * rsqrt(var + eps) * w, cast to bf16
+                        xl = f2_from_bf16x2(f2_to_bf16x2(f2_mul(f2_mul(xl, rr2), gl[i])));
+                        xh = f2_from_bf16x2(f2_to_bf16x2(f2_mul(f2_mul(xh, rr2), gh[i])));
+                    }
+                    // out[d] = x[d]*cos[d] + (-x[d+D/2])*sin[d], out[d+D/2] = x[d+D/2]*cos[d+D/2] +
+                    // x[d]*sin[d+D/2]
+                    float a0, a1, b0, b1, c0, c1, d0, d1;
+                    f2_split(f2_mul(xl, cl[i]), a0, a1);
+                    f2_split(f2_mul(xh, sl[i]), b0, b1);
+                    f2_split(f2_mul(xh, ch[i]), c0, c1);
+                    f2_split(f2_mul(xl, sh[i]), d0, d1);
+                    ol[i] = pack_bf16x2(__fsub_rn(a0, b0), __fsub_rn(a1, b1));
+                    oh[i] = pack_bf16x2(__fadd_rn(c0, d0), __fadd_rn(c1, d1));
+                }
+                *pl = make_uint4(ol[0], ol[1], ol[2], ol[3]);
+                *ph = make_uint4(oh[0], oh[1], oh[2], oh[3]);
+            }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the rows, for the TMA stores
+        __syncthreads();
+
+        // the group's cache rows: one box per half when they are KT consecutive rows of one block
+        const int* crow = s_rows;
+        bool boxed = nt == KT;
+        for (int t = 0; t < KT && boxed; ++t)
+            boxed = crow[3 * t + 1] >= 0 && crow[3 * t] == crow[0] && crow[3 * t + 1] == crow[1] &&
+                    crow[3 * t + 2] == crow[2] + t;
+        if (tid == 0) {
+#pragma unroll
+            for (int x = 0; x < HALVES; ++x) {
+                tma_store_4d(&tmQo, box(0, x), x * 64, s0, 0, b);
+                if (boxed) {
+                    tma_store_4d(&tmKc, box(1, x), x * 64, crow[2], 0, crow[1]);
+                    tma_store_4d(&tmVc, box(2, x), x * 64, crow[2], 0, crow[1]);
                 }
             }
-            float cl[8], sl[8], ch[8], sh[8];
-            load8f(cs + 8 * c, cl);
-            load8f(sn + 8 * c, sl);
-            if (tables) {
-                load8f(cs + 8 * c + D / 2, ch);
-                load8f(sn + 8 * c + D / 2, sh);
-            } else {
-#pragma unroll
-                for (int jj = 0; jj < 8; ++jj) {
-                    ch[jj] = cl[jj];
-                    sh[jj] = sl[jj];
-                }
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+        if (!boxed) {
+            // 16-byte stores of the valid rows: index = ((ten * Hkv + h) * KT + t) * NC + c
+            const int total = 2 * Hkv * KT * NC;
+            for (int i = tid; i < total; i += nthr) {
+                const int c = i % NC, t = (i / NC) % KT, hrow = i / (NC * KT);   // hrow = ten * Hkv + h
+                const int ten = hrow >= Hkv ? 1 : 0, h = hrow - ten * Hkv;
+                if (t >= nt || crow[3 * t + 1] < 0) continue;
+                const int rr = h * KT + t;
+                const uint4 val = *reinterpret_cast<const uint4*>(box(1 + ten, c >> 3) + rr * 128 +
+                                                                   ((((uint32_t)c & 7u) ^ (uint32_t)(rr & 7)) << 4));
+                __nv_bfloat16* dst = (ten == 0 ? a.k_cache : a.v_cache) + (int64_t)crow[3 * t + 1] * a.c_sb +
+                                     (int64_t)h * a.c_sh + (int64_t)crow[3 * t + 2] * a.c_st + 8 * c;
+                *reinterpret_cast<uint4*>(dst) = val;
             }
-            float lo[8], hi[8];
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj)
-                rope_rotate_pair(xl[jj], xh[jj], cl[jj], sl[jj], ch[jj], sh[jj], lo[jj], hi[jj]);
-            out[c] = pack8(lo);
-            out[c + NC / 2] = pack8(hi);
         }
     }
+    if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");   // smem stays until read
+    __syncthreads();
 }
 
 }  // namespace
@@ -624,17 +765,62 @@ int epilogue_entry(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh, cons
     const int total_heads = num_heads + 2 * num_kv_heads;
     const int64_t tokens = (int64_t)batch * seq_len;
     cudaStream_t st = (cudaStream_t)stream;
-    // Many tokens, every row 16-byte aligned: a thread per head row.
-    if (tokens >= 1024) {
+    // Many tokens, every row 16-byte aligned: TMA boxes of kStTokens tokens x all heads.
+    if (tokens >= 1024 && num_heads <= 256) {
         bool al = aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(q_out, 16) && aligned(k_cache, 16) &&
                   aligned(v_cache, 16);
-        for (int64_t st8 : {q_sb, q_ss, q_sh, k_sb, k_ss, k_sh, v_sb, v_ss, v_sh, cache_sb, cache_sh, cache_st})
-            al = al && (st8 % 8 == 0);
-        if (al) {
-            const unsigned blocks = (unsigned)((tokens + kRowTokens - 1) / kRowTokens);
-            if (head_dim == 128) qkv_epilogue_row_kernel<128><<<blocks, kRowThreads, 0, st>>>(a, (int)tokens);
-            else qkv_epilogue_row_kernel<64><<<blocks, kRowThreads, 0, st>>>(a, (int)tokens);
-            if (int e = check_cuda(cudaGetLastError(), "qkv_epilogue launch")) return e;
+        for (int64_t st8 : {q_ss, q_sh, k_ss, k_sh, v_ss, v_sh, cache_sb, cache_sh, cache_st})
+            al = al && st8 > 0 && (st8 % 8 == 0);
+        for (int64_t st8 : {q_sb, k_sb, v_sb}) al = al && (batch == 1 || (st8 > 0 && st8 % 8 == 0));
+        int sms = 0;
+        if (int e = require_sm100(&sms)) return e;
+        const size_t smem = head_dim == 128 ? TmaEpiSmem<128>::bytes(num_heads, num_kv_heads)
+                                            : TmaEpiSmem<64>::bytes(num_heads, num_kv_heads);
+        const int64_t cache_rows = lay.table ? lay.block_size : cache_capacity;
+        if (al && smem <= 200 * 1024 && seq_len >= kStTokens && cache_rows >= kStTokens) {
+            // tensor maps {D, rows, heads, batch}: q/k/v by token (batch stride arbitrary for B = 1),
+            // q_out [B, H, S, D], the cache by (sequence or block, kv head, row)
+            const int64_t S = seq_len, D = head_dim;
+            auto bstride = [&](int64_t sb, int64_t ss) { return batch == 1 ? S * ss : sb; };
+            const int64_t cache_batch = lay.table ? lay.num_blocks : (cu_seqlens ? n_seqs : batch);
+            CUtensorMap mq, mk, mv, mqo, mkc, mvc;
+            const uint32_t kt = kStTokens;
+            if (int e = encode_kv_map(&mq, q, D, S, num_heads, batch, q_ss, q_sh, bstride(q_sb, q_ss), 64, kt,
+                                      (uint32_t)num_heads))
+                return e;
+            if (int e = encode_kv_map(&mk, k, D, S, num_kv_heads, batch, k_ss, k_sh, bstride(k_sb, k_ss), 64, kt,
+                                      (uint32_t)num_kv_heads))
+                return e;
+            if (int e = encode_kv_map(&mv, v, D, S, num_kv_heads, batch, v_ss, v_sh, bstride(v_sb, v_ss), 64, kt,
+                                      (uint32_t)num_kv_heads))
+                return e;
+            if (int e = encode_kv_map(&mqo, q_out, D, S, num_heads, batch, D, S * D, (int64_t)num_heads * S * D, 64,
+                                      kt, (uint32_t)num_heads))
+                return e;
+            if (int e = encode_kv_map(&mkc, k_cache, D, cache_rows, num_kv_heads, cache_batch, cache_st, cache_sh,
+                                      cache_sb, 64, kt, (uint32_t)num_kv_heads))
+                return e;
+            if (int e = encode_kv_map(&mvc, v_cache, D, cache_rows, num_kv_heads, cache_batch, cache_st, cache_sh,
+                                      cache_sb, 64, kt, (uint32_t)num_kv_heads))
+                return e;
+            const int threads = std::min(kStMaxThreads, (kStTokens * (num_heads + num_kv_heads) + 31) / 32 * 32);
+            const int64_t groups = (int64_t)batch * ((seq_len + kStTokens - 1) / kStTokens);
+            auto launch = [&](auto kern) {
+                if (int e = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                            (int)smem),
+                                       "qkv_epilogue smem"))
+                    return e;
+                // persistent: as many blocks as fit on the GPU at once (registers and shared memory)
+                int per_sm = 0;
+                if (int e = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem),
+                                       "qkv_epilogue occupancy"))
+                    return e;
+                const unsigned blocks = (unsigned)std::min<int64_t>(groups, (int64_t)sms * std::max(per_sm, 1));
+                kern<<<blocks, threads, smem, st>>>(mq, mk, mv, mqo, mkc, mvc, a);
+                return check_cuda(cudaGetLastError(), "qkv_epilogue launch");
+            };
+            const int e = head_dim == 128 ? launch(qkv_epilogue_tma_kernel<128>) : launch(qkv_epilogue_tma_kernel<64>);
+            if (e) return e;
             return ok();
         }
     }

@@ -167,6 +167,38 @@ def test_epilogue_rejects_bad_slots(rt):
     assert lib.mllm_attn_device_status(None) == 0  # cleared
 
 
+def test_epilogue_many_tokens_rejects_bad_slots(rt):
+    """The many-token kernel refuses the same way: tokens whose cache row is past the capacity
+    get no K/V row and raise the device status, every other row is written as in a call that fits."""
+    from mllm_b200 import abi
+    lib = abi.load()
+    B, H, Hkv, S, D, start = 1, 4, 2, 1200, 128, 100
+    g = torch.Generator(device="cuda").manual_seed(5)
+    q = torch.randn(B, H, S, D, device="cuda", generator=g).bfloat16()
+    k = torch.randn(B, Hkv, S, D, device="cuda", generator=g).bfloat16()
+    v = torch.randn(B, Hkv, S, D, device="cuda", generator=g).bfloat16()
+    pos = torch.arange(S, device="cuda")
+
+    def run(capacity):
+        cache = rt.KVCache(B, Hkv, D, capacity)
+        cache.set_lengths([start])
+        q_out = torch.empty_like(q)
+        abi.call("mllm_qkv_epilogue_bf16", q.data_ptr(), q.stride(0), q.stride(2), q.stride(1),
+                 k.data_ptr(), k.stride(0), k.stride(2), k.stride(1), v.data_ptr(), v.stride(0), v.stride(2),
+                 v.stride(1), B, S, H, Hkv, D, pos.data_ptr(), 0, 1, 1e4, None, None, 0, 0, None, None, 1e-6,
+                 q_out.data_ptr(), cache.key_buf.data_ptr(), cache.value_buf.data_ptr(), *cache.strides,
+                 capacity, cache.lengths.data_ptr(), 0, None)
+        return q_out, cache, lib.mllm_attn_device_status(None)
+
+    q_fit, fit, st_fit = run(start + S)
+    q_cut, cut, st_cut = run(S)          # rows S .. start + S - 1 do not exist
+    assert st_fit == 0 and st_cut == 7   # MLLM_ERR_DEVICE_LENGTH
+    assert torch.equal(q_cut, q_fit)
+    assert torch.equal(cut.key_buf[:, :, start:S], fit.key_buf[:, :, start:S])
+    assert torch.equal(cut.value_buf[:, :, start:S], fit.value_buf[:, :, start:S])
+    assert lib.mllm_attn_device_status(None) == 0
+
+
 # ---------------------------------------------------------------------------------------
 # Decode
 # ---------------------------------------------------------------------------------------
