@@ -115,13 +115,16 @@ def test_epilogue_kv_cache_bit_exact(rt, c):
         np.testing.assert_array_equal(torch_to_bits(qr), O.bf16_bits(q_ref), err_msg=tag)
 
 
-@pytest.mark.parametrize("H,Hkv,D,qk_norm,table", [(32, 8, 128, True, False), (40, 8, 128, True, True),
-                                                   (32, 4, 64, False, False)])
-def test_epilogue_many_tokens_equals_chunked(rt, H, Hkv, D, qk_norm, table):
-    """A call over many tokens (the quarter-warp kernel) writes bit-identical q rows and cache rows to
+@pytest.mark.parametrize("H,Hkv,D,qk_norm,table,S", [(32, 8, 128, True, False, 1536), (40, 8, 128, True, True, 1536),
+                                                     (32, 4, 64, False, False, 1536), (4, 1, 128, True, False, 1539),
+                                                     (16, 4, 128, True, True, 1536), (8, 2, 64, True, False, 1539)])
+def test_epilogue_many_tokens_equals_chunked(rt, H, Hkv, D, qk_norm, table, S):
+    """A call over many tokens (the TMA-box kernel) writes bit-identical q rows and cache rows to
     the same tokens epilogued in small chunks (the warp-per-row kernel, pinned bit-exact to the
-    reference above): Qwen3-8B, Qwen3-14B with a RoPE table, TinyLlama geometry."""
-    B, S, chunk = 2, 1536, 256
+    reference above): Qwen3-8B, Qwen3-14B with a RoPE table, TinyLlama geometry, and the per-rank
+    head counts of Qwen3-8B split over 8 and 2 GPUs (1539 tokens per sequence: each sequence ends in a
+    partial group of tokens)."""
+    B, chunk = 2, 256
     g = torch.Generator(device="cuda").manual_seed(H + D)
     proj = (torch.randn(B, S, (H + 2 * Hkv) * D, device="cuda", generator=g) * 0.7).bfloat16()
     q = proj[..., : H * D].view(B, S, H, D).transpose(1, 2)
