@@ -10,7 +10,9 @@ Cases (Qwen3-8B attention geometry: 32 q heads, 8 kv heads, head_dim 128, hidden
   linear_fp8 the same with e4m3 weights and 128 x 128 block scales (linear_fp8_kernel)
 
 Prints one line: the case, its sizes and the mean milliseconds per launch over --iters launches
-(after --warmup).  Inputs are seeded random data; every launch goes through the C-ABI."""
+(after --warmup).  Inputs are seeded random data; every launch goes through the C-ABI.  With --graph
+(the default for the projections, whose launches last about as long as a host call) the --iters
+launches are recorded once in a CUDA graph and the graph is timed."""
 import argparse
 import json
 
@@ -73,19 +75,28 @@ def _decode(args, dev, g):
 
 
 def _linear(args, dev, g, fp8):
+    """Launches cycle through a ring of weight sets larger than L2 (126 MB), so that every launch
+    streams its weights from HBM."""
     T = args.tokens
     x = torch.randn(T, HIDDEN, device=dev, generator=g).bfloat16()
     ws = [torch.randn(n, HIDDEN, device=dev, generator=g).mul_(0.02).bfloat16() for n in (H * D, HKV * D, HKV * D)]
+    count = [0]
     if fp8:
-        w = rt.Fp8Weight.quantize(torch.cat(ws))
+        w0 = rt.Fp8Weight.quantize(torch.cat(ws))
+        nbytes = w0.w.numel() + w0.scale_inv.numel() * 4
+        ring = [w0] + [rt.Fp8Weight(w0.w.clone(), w0.scale_inv.clone()) for _ in range(-(-256 * 2**20 // nbytes) - 1)]
 
         def launch():
-            rt.linear_fp8(x, w)
-        return launch, {"tokens": T, "bytes": w.w.numel() + w.scale_inv.numel() * 4}
+            rt.linear_fp8(x, ring[count[0] % len(ring)])
+            count[0] += 1
+        return launch, {"tokens": T, "bytes": nbytes, "ring": len(ring)}
+    nbytes = sum(t.numel() for t in ws) * 2
+    ring = [ws] + [[t.clone() for t in ws] for _ in range(-(-256 * 2**20 // nbytes) - 1)]
 
     def launch():
-        rt.linear(x, ws)
-    return launch, {"tokens": T, "bytes": sum(t.numel() for t in ws) * 2}
+        rt.linear(x, ring[count[0] % len(ring)])
+        count[0] += 1
+    return launch, {"tokens": T, "bytes": nbytes, "ring": len(ring)}
 
 
 def main(argv=None):
@@ -97,7 +108,11 @@ def main(argv=None):
     ap.add_argument("--tokens", type=int, default=32)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--graph", action=argparse.BooleanOptionalAction, default=None,
+                    help="time the launches as one CUDA graph (default: on for linear and linear_fp8)")
     args = ap.parse_args(argv)
+    if args.graph is None:
+        args.graph = args.case in ("linear", "linear_fp8")
     if args.batch is None:
         args.batch = 32 if args.case == "decode" else 4
     if not torch.cuda.is_available():
@@ -116,14 +131,28 @@ def main(argv=None):
     for _ in range(args.warmup):
         launch()
     torch.cuda.synchronize()
+    run = lambda: [launch() for _ in range(args.iters)]
+    if args.graph:
+        graph = torch.cuda.CUDAGraph()
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        scratch = rt.GraphScratch()   # the graph's workspaces: alive as long as the graph
+        with torch.cuda.stream(stream):
+            with rt.graph_scratch(scratch):
+                graph.capture_begin()
+                run()
+                graph.capture_end()
+        torch.cuda.current_stream().wait_stream(stream)
+        graph.replay()
+        torch.cuda.synchronize()
+        run = graph.replay
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.iters):
-        launch()
+    run()
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.iters
-    info.update(case=args.case, ms=ms)
+    info.update(case=args.case, ms=ms, graph=args.graph)
     if "bytes" in info:
         info["gb_s"] = info["bytes"] / ms / 1e6
     if "flop" in info:
