@@ -810,11 +810,23 @@ int epilogue_entry(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh, cons
                                                             (int)smem),
                                        "qkv_epilogue smem"))
                     return e;
-                // persistent: as many blocks as fit on the GPU at once (registers and shared memory)
+                // persistent: as many blocks as fit on the GPU at once (registers and shared memory),
+                // queried once per device, head dimension, block size and shared-memory size
+                struct Fit { int dev = -1, d = 0, threads = 0; size_t smem = 0; int per_sm = 0; };
+                static thread_local Fit fits[8];
+                int dev = 0;
+                if (int e = check_cuda(cudaGetDevice(&dev), "qkv_epilogue device")) return e;
                 int per_sm = 0;
-                if (int e = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem),
-                                       "qkv_epilogue occupancy"))
-                    return e;
+                for (const Fit& f : fits)
+                    if (f.dev == dev && f.d == head_dim && f.threads == threads && f.smem == smem) per_sm = f.per_sm;
+                if (per_sm == 0) {
+                    if (int e = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem),
+                                           "qkv_epilogue occupancy"))
+                        return e;
+                    static thread_local int next = 0;
+                    fits[next] = Fit{dev, head_dim, threads, smem, per_sm};
+                    next = (next + 1) % 8;
+                }
                 const unsigned blocks = (unsigned)std::min<int64_t>(groups, (int64_t)sms * std::max(per_sm, 1));
                 kern<<<blocks, threads, smem, st>>>(mq, mk, mv, mqo, mkc, mvc, a);
                 return check_cuda(cudaGetLastError(), "qkv_epilogue launch");
