@@ -713,6 +713,35 @@ def run_gpu(args, rank, world, device):
                 torch.matmul(uly.tokens_from_heads(attn2d), w_o_full.t(), out=out_tok)
 
             layer_modes["micro1_ulysses_token_rows_io"] = ulysses_layer
+
+            # the same layout one sequence at a time (rank r owns rows [r S/N, (r+1) S/N) of every
+            # sequence), pipelined by UlyssesLayout.run_sequences: sequence b+1's input all-to-all
+            # and sequence b-1's output all-to-all + o_proj run on a side stream under sequence b's
+            # epilogue + attention
+            seq_send = [(torch.randn(world, S // world, prow, device=device, generator=gen) * 0.5).bfloat16()
+                        for _ in range(Bp)]
+            out_seq = torch.empty(Bp, S // world, HIDDEN, dtype=torch.bfloat16, device=device)
+            side_u = torch.cuda.Stream(device=device, priority=-1)
+
+            def attend_seq(b, qkv_h):
+                kv_off = b * psb * 2
+                st = lib.mllm_qkv_epilogue_bf16(
+                    qkv_h.data_ptr(), S * prow, prow, D,
+                    qkv_h.data_ptr() + Hr * D * 2, S * prow, prow, D,
+                    qkv_h.data_ptr() + (Hr + Hkvr) * D * 2, S * prow, prow, D,
+                    1, S, Hr, Hkvr, D, pos_p.data_ptr(), 0, 1, THETA, None, None, 0, 0,
+                    gq.data_ptr(), gk.data_ptr(), EPS, qp.data_ptr() + b * Hr * S * D * 2,
+                    kp.data_ptr() + kv_off, vp.data_ptr() + kv_off, psb, psh, pst, S, start_p.data_ptr(), 0,
+                    torch.cuda.current_stream().cuda_stream)
+                assert st == 0, lib.mllm_attn_last_error()
+                attn_mb(b, 1)
+                return attn2d[b * S:(b + 1) * S]
+
+            def finish_seq(b, rows):
+                torch.matmul(rows, w_o_full.t(), out=out_seq[b])
+
+            layer_modes["micro4_ulysses_per_sequence"] = lambda: uly.run_sequences(
+                lambda b: seq_send[b], attend_seq, finish_seq, Bp, side_u)
         layer_ms = {}
         for name, exch in layer_modes.items():
             if name.startswith("micro"):
@@ -942,6 +971,32 @@ def tp_parity_leg(rank, world, device, comm, barrier):
     t = torch.tensor([excess], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     modes["ulysses"] = {"max_excess": float(t.item()), "ok": float(t.item()) <= 0.0}
+    barrier()
+    # the same layout one sequence at a time (UlyssesLayout.run_sequences on a side stream): rank r
+    # owns rows [r S/N, (r+1) S/N) of every sequence; its prefill rows against the same rows of
+    # the unsharded layer
+    Sn = TP_S // world
+    out_seq = torch.empty(TP_B, Sn, HIDDEN, dtype=torch.bfloat16, device=device)
+    seq_caches = [rt.KVCache(1, Hkvr, D, TP_S) for _ in range(TP_B)]
+
+    def attend_p(b, qkv):
+        qs = qkv[:, :Hr * D].view(1, TP_S, Hr, D).transpose(1, 2)
+        ks = qkv[:, Hr * D:(Hr + Hkvr) * D].view(1, TP_S, Hkvr, D).transpose(1, 2)
+        vs = qkv[:, (Hr + Hkvr) * D:].view(1, TP_S, Hkvr, D).transpose(1, 2)
+        return rt.Attention.forward_projected(qs, ks, vs, None, Hr, Hkvr, D, THETA, pos(0), seq_caches[b], gq, gk,
+                                              EPS).reshape(TP_S, Hr * D)
+
+    def finish_p(b, rows):
+        out_seq[b] = torch.nn.functional.linear(rows, w["w_o"])
+
+    lay.run_sequences(lambda b: lay.project(xs[0][b, rank * Sn:(rank + 1) * Sn], w_packed), attend_p, finish_p,
+                      TP_B, torch.cuda.Stream(device=device, priority=-1))
+    torch.cuda.synchronize()
+    ref_seq = ref[0][:, rank * Sn:(rank + 1) * Sn]
+    t = torch.tensor([float((out_seq.float() - ref_seq).abs().sub(2e-2 + 2e-2 * ref_seq.abs()).max())],
+                     dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    modes["ulysses_seq"] = {"max_excess": float(t.item()), "ok": float(t.item()) <= 0.0}
     barrier()
     for mode in ("nccl_chunked", "comm", "peer", "seqpar"):
         ex = {}
@@ -1469,7 +1524,11 @@ def main():
                     "high-priority stream while the next micro-batch's epilogue + attention runs; "
                     "micro1_ulysses_token_rows_io: the layer's input and output sharded by token rows "
                     "(mllm_b200.tp.UlyssesLayout: q/k/v all-to-all to the head owners, attention, all-to-all "
-                    "back, o_proj of the rank's rows with the whole w_o) -- no output is replicated"}
+                    "back, o_proj of the rank's rows with the whole w_o) -- no output is replicated; "
+                    "micro4_ulysses_per_sequence: the same layout one sequence at a time (rank r owns rows "
+                    "[r S/N, (r+1) S/N) of every sequence), sequence b+1's input all-to-all and sequence "
+                    "b-1's output all-to-all + o_proj on a side stream under sequence b's attention "
+                    "(UlyssesLayout.run_sequences)"}
     if res["rag"] is not None:
         r = res["rag"]
         ach = r["bytes_per_rank"] / (r["ms"] * 1e-3) / 1e9

@@ -378,6 +378,54 @@ class UlyssesLayout:
         dist.all_to_all_single(recv, attn.contiguous(), group=self.group)
         return recv.permute(1, 0, 2).reshape(T // N, N * Hd)
 
+    def run_sequences(self, send_of, attend, finish, count: int, side_stream=None):
+        """The layer in this layout one sequence at a time, pipelined.  Here rank r owns rows
+        [r S/N, (r+1) S/N) of EVERY sequence, so the moves of one sequence involve every rank
+        evenly and heads_from_tokens_packed / tokens_from_heads apply to it unchanged (T = S).
+
+          send_of(b) -> [N, S/N, (Hr + 2 Hkvr) D]: this rank's q/k/v projections of its rows of
+              sequence b, grouped by destination (project() with pack_qkv_weights' weights); ready
+              on the current stream when run_sequences is called;
+          attend(b, qkv [S, (Hr + 2 Hkvr) D]) -> [S, Hr D]: epilogue + attention of this rank's heads
+              over sequence b, on the current stream;
+          finish(b, rows [S/N, H D]): this rank's rows of sequence b after attention (o_proj).
+
+        With a side stream, sequence b+1's input all-to-all and sequence b-1's output all-to-all
+        and finish run on it while sequence b is attended on the current stream; only the first
+        input move and the last output move are exposed.  The current stream waits for the side
+        stream before this returns.  Without one (CPU ranks) the steps run in order.  Every rank
+        must call it with the same count (the collectives are matched in order)."""
+        import torch
+        if side_stream is None:
+            for b in range(count):
+                finish(b, self.tokens_from_heads(attend(b, self.heads_from_tokens_packed(send_of(b)))))
+            return
+        cur = torch.cuda.current_stream()
+        side_stream.wait_stream(cur)
+        recv, ev_in = [None] * count, [None] * count
+
+        def move_in(b):
+            with torch.cuda.stream(side_stream):
+                recv[b] = self.heads_from_tokens_packed(send_of(b))
+                ev_in[b] = torch.cuda.Event()
+                ev_in[b].record(side_stream)
+
+        move_in(0)
+        for b in range(count):
+            cur.wait_event(ev_in[b])
+            recv[b].record_stream(cur)
+            att = attend(b, recv[b])
+            ev_att = torch.cuda.Event()
+            ev_att.record(cur)
+            if b + 1 < count:
+                move_in(b + 1)
+            side_stream.wait_event(ev_att)
+            att.record_stream(side_stream)
+            with torch.cuda.stream(side_stream):
+                finish(b, self.tokens_from_heads(att))
+            recv[b] = None
+        cur.wait_stream(side_stream)
+
 
 def run_micro_batches(compute, exchange, count: int, comm_stream=None):
     """Overlaps the o_proj exchange of one micro-batch with the attention of the next.

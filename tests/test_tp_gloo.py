@@ -255,3 +255,66 @@ def test_ulysses_packed_projection_lands_on_the_head_owners():
         assert p.exitcode == 0
     for r, err in res:
         assert err < 1e-5, (r, err)
+
+
+def _ulysses_seq_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        B, S, E, H, Hkv, D = 3, 8, 24, 8, 4, 8
+        g = torch.Generator().manual_seed(13)
+        h = torch.randn(B, S, E, generator=g)
+        w_q, w_k, w_v = (torch.randn(n * D, E, generator=g) for n in (H, Hkv, Hkv))
+        w_o = torch.randn(E, H * D, generator=g)
+        shard = tp.shard_heads(H, Hkv, world, rank)
+        lay = tp.UlyssesLayout(shard, H, Hkv, D)
+        Sn = S // world
+        w_packed = lay.pack_qkv_weights(w_q, w_k, w_v)
+        q0, q1 = shard.q_heads[0] * D, shard.q_heads[1] * D
+        k0, k1 = shard.kv_heads[0] * D, shard.kv_heads[1] * D
+        # a stand-in for attention that mixes every row of the sequence (so that a row taken from
+        # the wrong sequence or position shows): q * (row-sum of k) + cumulative sum of v per head
+        def attend(b, qkv):
+            Hr, Hkvr = shard.num_heads, shard.num_kv_heads
+            qq = qkv[:, :Hr * D].view(S, Hr, D)
+            kk = qkv[:, Hr * D:(Hr + Hkvr) * D].view(S, Hkvr, D).repeat_interleave(Hr // Hkvr, 1)
+            vv = qkv[:, (Hr + Hkvr) * D:].view(S, Hkvr, D).repeat_interleave(Hr // Hkvr, 1)
+            return (qq * kk.sum(0, keepdim=True) + vv.cumsum(0)).reshape(S, Hr * D)
+        out = torch.empty(B, Sn, E)
+
+        def finish(b, rows):
+            out[b] = rows @ w_o.t()
+        lay.run_sequences(lambda b: lay.project(h[b, rank * Sn:(rank + 1) * Sn], w_packed), attend, finish, B)
+        # the same on one process: every head, every sequence
+        want = torch.empty(B, Sn, E)
+        for b in range(B):
+            qa, ka, va = h[b] @ w_q.t(), h[b] @ w_k.t(), h[b] @ w_v.t()
+            qq = qa.view(S, H, D)
+            kk = ka.view(S, Hkv, D).repeat_interleave(H // Hkv, 1)
+            vv = va.view(S, Hkv, D).repeat_interleave(H // Hkv, 1)
+            att = (qq * kk.sum(0, keepdim=True) + vv.cumsum(0)).reshape(S, H * D)
+            want[b] = (att @ w_o.t())[rank * Sn:(rank + 1) * Sn]
+        q.put((rank, float((out - want).abs().max() / want.abs().max())))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ulysses_per_sequence_pipeline_gives_each_rank_its_rows():
+    """UlyssesLayout.run_sequences (rank r owns rows [r S/N, (r+1) S/N) of every sequence): each
+    sequence's q/k/v reach the head owners, the per-head results come back to the row owners and
+    every rank ends with its rows of every sequence, as one process computing all heads would
+    (2 gloo ranks, 3 sequences)."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ulysses_seq_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r, err in res:
+        assert err < 1e-5, (r, err)
