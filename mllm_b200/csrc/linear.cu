@@ -516,18 +516,19 @@ __global__ void __launch_bounds__(kF8Threads, f8_ctas_per_sm(NT))
             const float sc = __bfloat162float(__float2bfloat16_rn(srow[u0 + i]));
             const uint8_t* src = stage_a(sa);
             uint8_t* dst = stage_bw(sb);
-            // chunk u: row u / 16, k 8 (u % 16) .. + 7; four chunks per round, loads first
+            // chunk u: row u / 16, k 8 (u % 16) .. + 7; kConvBatch chunks per round, loads first
             constexpr int kStep = kF8ConvWarps * 32;
+            constexpr int kConvBatch = 8;   // chunks per thread per round: loads first, then conversions
             constexpr int kChunks = kTileRows * 16;
-            for (int u0c = ct; u0c < kChunks; u0c += 4 * kStep) {
-                uint2 w[4];
+            for (int u0c = ct; u0c < kChunks; u0c += kConvBatch * kStep) {
+                uint2 w[kConvBatch];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
+                for (int q = 0; q < kConvBatch; ++q) {
                     const int u = u0c + q * kStep;
                     if (u < kChunks) w[q] = *reinterpret_cast<const uint2*>(src + (u >> 4) * kF8Unit + 8 * (u & 15));
                 }
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
+                for (int q = 0; q < kConvBatch; ++q) {
                     const int u = u0c + q * kStep;
                     if (u >= kChunks) break;
                     const int R = u >> 4, c16 = u & 15;
