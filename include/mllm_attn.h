@@ -412,7 +412,11 @@ MLLM_API int mllm_sample(void* logits, int logits_bf16, int64_t row_stride, int 
  *       any shapes in one stream (not concurrent calls); the rest needs no initialisation
  * fp32 accumulation on the tensor cores, one rounding to bf16 per output.  The k range of a
  * 128-row tile may be split over up to 8 CTAs whose fp32 partials are added in split order,
- * so results are deterministic.  0 <= tokens <= 256. */
+ * so results are deterministic.  0 <= tokens <= 256.
+ * The launch may start while the previous kernel in the stream is finishing (programmatic
+ * dependent launch) and streams its first weight tiles before it waits for that kernel: the
+ * weights must not be written by the kernel launched just before this call in the same stream
+ * (x may be).  The same holds for mllm_linear_fp8_bf16. */
 MLLM_API size_t mllm_linear_workspace_size(int tokens, int num_weights, const int64_t* out_features,
                                            int64_t in_features);
 

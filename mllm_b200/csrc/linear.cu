@@ -481,10 +481,15 @@ __global__ void __launch_bounds__(kF8Threads, f8_ctas_per_sm(NT))
 
     if (warp == 0 && lane == 0) {
         // ------------------------------- fp8 weight blocks -------------------------------
-        // after the previous kernel in the stream: it may be the one that wrote the weights
+        // The first SA blocks stream before this grid waits for the previous kernel in the stream
+        // (as linear_kernel does): the weights must not be that kernel's output.
         tma_prefetch_desc(&wmap);
-        pdl_wait();
         int i = 0;
+        for (; i < nk && i < SA; ++i) {
+            mbar_arrive_expect_tx(&a_full[i], Cfg::kABytes);
+            tma_load_4d(stage_a(i), &wmap, &a_full[i], (u0 + i) * kF8Unit, wrow, 0, 0);
+        }
+        pdl_wait();
         for (; i < nk; ++i) {
             const int s = i % SA;
             if (i >= SA && !mbar_wait(&a_empty[s], ((i / SA) - 1) & 1)) break;
