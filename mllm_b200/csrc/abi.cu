@@ -100,7 +100,7 @@ int encode_kv_map(CUtensorMap* map, const void* base, int64_t d, int64_t rows, i
 }
 
 int encode_u8_map(CUtensorMap* map, const void* base, int64_t cols, int64_t rows, int64_t stride_row,
-                  uint32_t box_cols, uint32_t box_rows) {
+                  uint32_t box_cols, uint32_t box_rows, bool swizzle128) {
     auto fn = get_encode_fn();
     if (!fn) return fail(MLLM_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
     if (!aligned(base, 16)) return fail(MLLM_ERR_INVALID_ARGUMENT, "TMA base address must be 16-byte aligned");
@@ -111,7 +111,8 @@ int encode_u8_map(CUtensorMap* map, const void* base, int64_t cols, int64_t rows
     cuuint32_t box[4] = {box_cols, box_rows, 1, 1};
     cuuint32_t elem_strides[4] = {1, 1, 1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box, elem_strides,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         char buf[160];

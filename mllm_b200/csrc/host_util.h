@@ -69,10 +69,11 @@ int encode_kv_map(CUtensorMap* map, const void* base, int64_t d, int64_t rows, i
                   int64_t stride_row, int64_t stride_head, int64_t stride_batch, uint32_t box_d,
                   uint32_t box_rows, uint32_t box_heads = 1);
 
-// Encodes a 2-D byte tensor map {cols (inner), rows} with row stride `stride_row` bytes, no
-// swizzle and a {box_cols, box_rows} box (as a 4-D map with unit outer dimensions, so that the
-// 4-D load helper serves it).  Returns MLLM_OK or an error.
+// Encodes a 2-D byte tensor map {cols (inner), rows} with row stride `stride_row` bytes and a
+// {box_cols, box_rows} box (as a 4-D map with unit outer dimensions, so that the 4-D load helper
+// serves it); with swizzle128 the box rows (box_cols <= 128) land with the 128-byte swizzle: 16-byte
+// chunk c of box row r at chunk c ^ (r % 8).  Returns MLLM_OK or an error.
 int encode_u8_map(CUtensorMap* map, const void* base, int64_t cols, int64_t rows, int64_t stride_row,
-                  uint32_t box_cols, uint32_t box_rows);
+                  uint32_t box_cols, uint32_t box_rows, bool swizzle128 = false);
 
 }  // namespace mllm_b200

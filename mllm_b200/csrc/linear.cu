@@ -349,37 +349,44 @@ int launch_linear(const LinearMaps& maps, const LinearArgs& a, const LinearPlan&
 // The tensor cores then see the same bf16 operand the reference's GEMM sees.
 //
 // Roles (384 threads, the k range of a 128-row tile split over CTAs):
-//   warp 0 (lane 0): TMA of the fp8 tile blocks, 128 rows x 128 bytes, into ring A;
-//   warp 2 (lane 0): TMA of the activations' two 64-k atoms of each block into ring B;
-//   warps 3-11: dequantize ring A's block into ring B in the K-major 128-byte-swizzled layout the
-//     MMA reads (8-row groups 2 KB apart, two atoms per group);
-//   warp 1 (lane 0): tcgen05.mma kind::f16 over ring B, fp32 accumulators in tensor memory;
+//   warp 0 (lane 0): TMA of the fp8 tile blocks, 128 rows x 128 bytes (128-byte swizzle), into
+//     ring A in shared memory;
+//   warp 2 (lane 0): TMA of the activations' two 64-k atoms of each block into ring X;
+//   warps 4-11: dequantize -- thread (warp % 4, lane) owns tile row 32 * (warp % 4) + lane (its
+//     tensor-memory lane), warps 4-7 the block's first 64 k, warps 8-11 the last 64; each writes its
+//     row's bf16 values into a tensor-memory stage with tcgen05.st;
+//   warp 1 (lane 0): tensor-memory allocation and tcgen05.mma kind::f16 with A = the dequantized
+//     block in tensor memory (TS form) and B = the activations in shared memory, fp32 accumulators
+//     in tensor memory columns [0, NT);
 //   warps 4-7: the epilogue (tensor-memory lane quarters 0-3), split partials as linear_kernel.
 // ---------------------------------------------------------------------------------------------
 constexpr int kF8Unit = 128;                 // k per unit: one scale block, two bf16 atoms
 constexpr int kF8Threads = 384;
-constexpr int kF8ConvWarp0 = 3;
-constexpr int kF8ConvWarps = 9;
+constexpr int kF8ConvWarp0 = 4;
+constexpr int kF8ConvWarps = 8;
 constexpr int kF8MaxTokens = 128;
 
-// At 32 tokens two CTAs share an SM (two fp8 stages and two dequantized stages each, 112 KB,
-// at most 85 registers at 384 threads): the dequantizing warps of two tiles interleave and the
-// tile x split grid fits one wave.  The dequantizing issue, not the fp8 stream, sets the pace:
-// nine dequantizing warps per CTA run 3-7 % faster than five.  Wider token tiles keep one CTA per SM with deeper rings.  (Measured on
-// the Qwen3-8B gate projection at 32 tokens: 21 us with this split; one CTA per SM with eight fp8
-// stages and nine dequantizing warps, 35 us; three per SM with one dequantized stage, 26 us.)
+// At 32 tokens two CTAs share an SM (five fp8 stages and three dequantized stages each, 105 KB of
+// shared memory and 256 tensor-memory columns; at most 85 registers at 384 threads): the
+// dequantizing warps of two tiles interleave and the tile x split grid fits one wave.  Wider token
+// tiles keep one CTA per SM.  The dequantizing issue, not the fp8 stream, sets the pace.
 constexpr int f8_ctas_per_sm(int nt) { return nt == 32 ? 2 : 1; }
 
 template <int NT>
 struct F8Cfg {
     static constexpr int kABytes = kTileRows * kF8Unit;          // fp8 block
-    static constexpr int kBWBytes = kTileRows * kF8Unit * 2;     // dequantized block
-    static constexpr int kBXBytes = NT * kF8Unit * 2;            // activations
-    static constexpr int kBBytes = kBWBytes + kBXBytes;
-    static constexpr int kAStages = NT == 32 ? 2 : 4;
-    static constexpr int kBStages = NT == 32 ? 2 : (NT <= 64 ? 3 : 2);
-    static constexpr int kRings = kAStages * kABytes + kBStages * kBBytes;
+    static constexpr int kBXBytes = NT * kF8Unit * 2;            // activations of one block
+    static constexpr int kAStages = NT == 32 ? 5 : (NT == 64 ? 8 : 6);
+    static constexpr int kBStages = 3;                           // dequantized (tensor memory) + activations
+    static constexpr int kRings = kBStages * kBXBytes + kAStages * kABytes;
     static constexpr int kSmem = kRings + 256;   // + barriers; the kernel has no static shared memory
+    // tensor memory: accumulators [0, NT), then kBStages dequantized blocks of 64 columns (128 bf16
+    // of k per row); the allocation is the next power of two
+    static constexpr uint32_t kACol = NT;
+    static constexpr uint32_t kTmemUsed = NT + kBStages * 64;
+    static constexpr uint32_t kTmemCols = kTmemUsed <= 256 ? 256 : 512;
+    static_assert(f8_ctas_per_sm(NT) * kTmemCols <= 512, "tensor memory of the resident CTAs");
+    static_assert(f8_ctas_per_sm(NT) * (kSmem + 1024) <= 228 * 1024, "shared memory of the resident CTAs");
 };
 
 struct F8Args {
@@ -428,8 +435,8 @@ __global__ void __launch_bounds__(kF8Threads, f8_ctas_per_sm(NT))
     constexpr int SA = Cfg::kAStages;
     constexpr int SB = Cfg::kBStages;
     // All shared memory is dynamic, so that its base is the CTA's shared window (1024-aligned) and
-    // two CTAs fit per SM without alignment slack: ring B (swizzled, 1024-aligned stages), ring A,
-    // then the barriers.  A base found misaligned is recorded and the CTA leaves before it touches
+    // two CTAs fit per SM without alignment slack: ring X (swizzled, 1024-aligned stages), ring A
+    // (swizzled), then the barriers.  A base found misaligned is recorded and the CTA leaves before it touches
     // a barrier or tensor memory.
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     if ((smem_u32(smem_raw) & 1023u) != 0u) {
@@ -453,10 +460,9 @@ __global__ void __launch_bounds__(kF8Threads, f8_ctas_per_sm(NT))
     const int wrow = tile * kTileRows;
     const int u0 = (int)((int64_t)split * a.units / splits);
     const int nk = (int)((int64_t)(split + 1) * a.units / splits) - u0;   // >= 1 (splits <= units)
-    // ring B first (1024-aligned swizzle blocks), then ring A
-    auto stage_bw = [&](int s) { return smem + s * Cfg::kBBytes; };
-    auto stage_bx = [&](int s) { return smem + s * Cfg::kBBytes + Cfg::kBWBytes; };
-    auto stage_a = [&](int s) { return smem + SB * Cfg::kBBytes + s * Cfg::kABytes; };
+    // ring X first (1024-aligned swizzle blocks), then ring A
+    auto stage_bx = [&](int s) { return smem + s * Cfg::kBXBytes; };
+    auto stage_a = [&](int s) { return smem + SB * Cfg::kBXBytes + s * Cfg::kABytes; };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < SA; ++s) {
@@ -464,14 +470,14 @@ __global__ void __launch_bounds__(kF8Threads, f8_ctas_per_sm(NT))
             mbar_init(&a_empty[s], kF8ConvWarps);
         }
         for (int s = 0; s < SB; ++s) {
-            mbar_init(&b_full[s], 1 + kF8ConvWarps);   // the activation load + every converter warp
+            mbar_init(&b_full[s], 1 + kF8ConvWarps);   // the activation load + every dequantizing warp
             mbar_init(&b_empty[s], 1);
         }
         mbar_init(done_bar, 1);
         mbar_fence_init();
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, NT);
+        tmem_alloc(tmem_slot, Cfg::kTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -511,7 +517,11 @@ __global__ void __launch_bounds__(kF8Threads, f8_ctas_per_sm(NT))
         for (int j = (i > SB ? i - SB : 0); j < i; ++j) mbar_wait(&b_full[j % SB], (j / SB) & 1);
     } else if (warp >= kF8ConvWarp0) {
         // ------------------------------- dequantize -------------------------------
-        const int ct = threadIdx.x - kF8ConvWarp0 * 32;
+        // thread (warp % 4, lane): tile row r = 32 * (warp % 4) + lane, which is its tensor-memory
+        // lane; warps 4-7 take k [0, 64) of each block, warps 8-11 k [64, 128)
+        const int quad = warp & 3, khalf = (warp - kF8ConvWarp0) >> 2;
+        const int r = quad * 32 + lane;
+        const uint32_t t_row = tmem + ((uint32_t)(quad * 32) << 16) + Cfg::kACol + (uint32_t)(khalf * 32);
         const float* srow = a.scale + (int64_t)tile * a.scale_stride;
         for (int i = 0; i < nk; ++i) {
             const int sa = i % SA, sb = i % SB;
@@ -519,30 +529,27 @@ __global__ void __launch_bounds__(kF8Threads, f8_ctas_per_sm(NT))
             if (i >= SB && !mbar_wait(&b_empty[sb], ((i / SB) - 1) & 1)) break;
             // QwenRunner.cpp:103-122: scale.to(bf16), then the bf16 product
             const float sc = __bfloat162float(__float2bfloat16_rn(srow[u0 + i]));
-            const uint8_t* src = stage_a(sa);
-            uint8_t* dst = stage_bw(sb);
-            // chunk u: row u / 16, k 8 (u % 16) .. + 7; kConvBatch chunks per round, loads first
-            constexpr int kStep = kF8ConvWarps * 32;
-            constexpr int kConvBatch = 8;   // chunks per thread per round: loads first, then conversions
-            constexpr int kChunks = kTileRows * 16;
-            for (int u0c = ct; u0c < kChunks; u0c += kConvBatch * kStep) {
-                uint2 w[kConvBatch];
+            // the row's 64 fp8 bytes: 16-byte chunks 4 khalf .. + 3, chunk c at (c ^ (r % 8)) in
+            // the swizzled block (the 32 rows a warp reads fall in 8 different bank groups)
+            const uint8_t* src = stage_a(sa) + r * kF8Unit;
+            uint4 w[4];
 #pragma unroll
-                for (int q = 0; q < kConvBatch; ++q) {
-                    const int u = u0c + q * kStep;
-                    if (u < kChunks) w[q] = *reinterpret_cast<const uint2*>(src + (u >> 4) * kF8Unit + 8 * (u & 15));
-                }
+            for (int q = 0; q < 4; ++q)
+                w[q] = *reinterpret_cast<const uint4*>(src + ((((uint32_t)(4 * khalf + q)) ^ (uint32_t)(r & 7)) << 4));
+            float o[32];   // 64 bf16 of k, two per tensor-memory column
 #pragma unroll
-                for (int q = 0; q < kConvBatch; ++q) {
-                    const int u = u0c + q * kStep;
-                    if (u >= kChunks) break;
-                    const int R = u >> 4, c16 = u & 15;
-                    const int g = R >> 3, r = R & 7, at = c16 >> 3, c = c16 & 7;
-                    *reinterpret_cast<uint4*>(dst + g * 2048 + at * 1024 + r * 128 + ((c ^ r) << 4)) =
-                        dequant8(w[q], sc);
-                }
+            for (int q = 0; q < 4; ++q) {
+                const uint4 lo = dequant8(make_uint2(w[q].x, w[q].y), sc);
+                const uint4 hi = dequant8(make_uint2(w[q].z, w[q].w), sc);
+                o[8 * q + 0] = __uint_as_float(lo.x); o[8 * q + 1] = __uint_as_float(lo.y);
+                o[8 * q + 2] = __uint_as_float(lo.z); o[8 * q + 3] = __uint_as_float(lo.w);
+                o[8 * q + 4] = __uint_as_float(hi.x); o[8 * q + 5] = __uint_as_float(hi.y);
+                o[8 * q + 6] = __uint_as_float(hi.z); o[8 * q + 7] = __uint_as_float(hi.w);
             }
-            fence_proxy_async_smem();   // generic writes, read next by the tensor cores
+            tc_fence_after();   // after the MMA that read this stage (b_empty) completed
+            tmem_st32(t_row + (uint32_t)(sb * 64), o);
+            tmem_wait_st();
+            tc_fence_before();
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&b_full[sb]);
@@ -551,22 +558,19 @@ __global__ void __launch_bounds__(kF8Threads, f8_ctas_per_sm(NT))
         }
     } else if (warp == 1 && lane == 0) {
         // -------------------------------- MMA issuer --------------------------------
+        // D [128 rows, NT] += A [128 rows, 128 k] (tensor memory, stage sb) x B [128 k, NT tokens]
         constexpr uint32_t idesc = idesc_bf16_f32(kTileRows, NT, false);
-        constexpr uint32_t w_hi = smem_desc_hi_sw128(2048);   // row groups 2 KB apart (two atoms)
         constexpr uint32_t x_hi = smem_desc_hi_sw128(1024);
         for (int i = 0; i < nk; ++i) {
             const int s = i % SB;
             if (!mbar_wait(&b_full[s], (i / SB) & 1)) break;
             tc_fence_after();
-            const uint32_t wd = smem_desc_lo(smem_u32(stage_bw(s)), 16);
             const uint32_t xd = smem_desc_lo(smem_u32(stage_bx(s)), 16);
 #pragma unroll
-            for (int at = 0; at < 2; ++at)
-#pragma unroll
-                for (int ks = 0; ks < kAtomK / 16; ++ks)
-                    tc_mma_ss_w2(tmem, wd + (uint32_t)((at * 1024 + ks * 32) >> 4), w_hi,
-                                 xd + (uint32_t)((at * NT * 128 + ks * 32) >> 4), x_hi, idesc,
-                                 (i > 0 || at > 0 || ks > 0) ? 1u : 0u);
+            for (int ks = 0; ks < kF8Unit / 16; ++ks)
+                tc_mma_ts_w(tmem, tmem + Cfg::kACol + (uint32_t)(s * 64 + ks * 8),
+                            xd + (uint32_t)((((ks >> 2) * NT * 128) + (ks & 3) * 32) >> 4), x_hi, idesc,
+                            (i > 0 || ks > 0) ? 1u : 0u);
             tc_commit(&b_empty[s]);
         }
         tc_commit(done_bar);
@@ -617,7 +621,7 @@ __global__ void __launch_bounds__(kF8Threads, f8_ctas_per_sm(NT))
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) tmem_dealloc(tmem, NT);
+    if (warp == 1) tmem_dealloc(tmem, Cfg::kTmemCols);
 }
 
 struct F8Plan {
@@ -792,7 +796,8 @@ extern "C" int mllm_linear_fp8_bf16(const void* x, int64_t x_stride, int tokens,
         return fail(MLLM_ERR_INVALID_ARGUMENT,
                     "linear_fp8: workspace missing, not 256-byte aligned or smaller than mllm_linear_fp8_workspace_size");
     CUtensorMap wmap, xmap;
-    if (int st = encode_u8_map(&wmap, weight, in_features, out_features, weight_stride, kF8Unit, kTileRows)) return st;
+    if (int st = encode_u8_map(&wmap, weight, in_features, out_features, weight_stride, kF8Unit, kTileRows, true))
+        return st;
     // activations {64 k, tokens, k-atoms}: box NT rows x 2 atoms (one 128-k unit)
     if (int st = encode_kv_map(&xmap, x, kAtomK, tokens, in_features / kAtomK, 1, x_stride, kAtomK,
                                x_stride * tokens, kAtomK, (uint32_t)p.nt, 2))
