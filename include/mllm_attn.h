@@ -431,7 +431,7 @@ MLLM_API int mllm_linear_bf16(const void* x, int64_t x_stride, int tokens, int64
  * the reference's dequantize-then-multiply: DequantizeFP8 (QwenRunner.cpp:103-122,
  * bf16(fp8 * bf16(scale)), run on every layer of every step) followed by Linear::Forward
  * (Linear.h:33-68).  The fp8 bytes are streamed from HBM (half the bf16 weight) and dequantized
- * in shared memory with exactly that rounding; the tensor cores then multiply the same bf16
+ * on chip with exactly that rounding; the tensor cores then multiply the same bf16
  * operand (fp32 accumulation, one rounding per output, split-k partials added in a fixed order).
  *   x: bf16 [tokens, in_features], row stride x_stride (multiple of 8, 16-byte aligned)
  *   weight: e4m3 [out_features, in_features], row stride weight_stride bytes (multiple of 16,

@@ -344,7 +344,7 @@ int launch_linear(const LinearMaps& maps, const LinearArgs& a, const LinearPlan&
 // reference dequantizes every such projection on every step (QwenRunner.cpp:103-122:
 // w.to(bf16) * scale.to(bf16), a bf16 tensor product) and multiplies in bf16 (Linear.h:33-68).
 // This kernel streams the fp8 bytes -- half the bf16 weight -- and dequantizes each 128-row x
-// 128-k block in shared memory with exactly that arithmetic: fp8 -> fp32 (exact), times the
+// 128-k block on chip (from shared memory into tensor memory) with exactly that arithmetic: fp8 -> fp32 (exact), times the
 // bf16-rounded scale (an exact product of a 4-bit and an 8-bit significand), one rounding to bf16.
 // The tensor cores then see the same bf16 operand the reference's GEMM sees.
 //

@@ -783,7 +783,7 @@ FP8_MAX_TOKENS = 128
 
 def linear_fp8(x: torch.Tensor, w: Fp8Weight) -> torch.Tensor:
     """Linear::Forward(x, DequantizeFP8(w)) for bf16 x with at most 128 rows, by
-    mllm_linear_fp8_bf16: the fp8 bytes are streamed and dequantized in shared memory with the
+    mllm_linear_fp8_bf16: the fp8 bytes are streamed and dequantized on chip (into tensor memory) with the
     reference's rounding, so the product equals a bf16 GEMM on the dequantized weight (fp32
     accumulation, one rounding).  More rows: the reference's own route (dequantize, cuBLAS)."""
     K = x.size(-1)
