@@ -484,6 +484,11 @@ __global__ void __launch_bounds__(kF8Threads, f8_ctas_per_sm(NT))
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // The next kernel in the stream may launch once every CTA of this grid has started: its CTAs
+    // take the SMs this grid's CTAs leave, and it waits (griddepcontrol.wait) for this grid to
+    // complete before it reads anything this grid writes.  (linear_kernel, one CTA per SM and a
+    // shorter ramp, measured 1 % slower with this and triggers in its epilogue instead.)
+    pdl_trigger();
 
     if (warp == 0 && lane == 0) {
         // ------------------------------- fp8 weight blocks -------------------------------
@@ -582,7 +587,6 @@ __global__ void __launch_bounds__(kF8Threads, f8_ctas_per_sm(NT))
         const int ew = warp - 4;                 // tensor-memory lane quarter
         mbar_wait(done_bar, 0);
         tc_fence_after();
-        pdl_trigger();
         const int T = a.tokens;
         const int row = ew * 32 + lane;
         const int64_t ostride = a.out_stride;
