@@ -562,99 +562,98 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 2)
 }
 
 // Merges the per-chunk partials of every (sequence, query head) whose cache spans more
-// than one chunk.  One CTA per (kv head, sequence); thread d owns column d of every head.
-// By the time this runs the partials have usually left L2 (the split kernel streamed the
-// whole cache through it after writing them), so every load of a CTA goes out in one round:
-// thread d first issues its column's loads for all heads and chunks, then the (m, l) pairs are
-// staged and turned into chunk weights exp2(m_c - M) and 1/L while those loads are in flight,
-// and only then are the columns summed, in chunk order.
+// than one chunk.  One CTA per (query head, sequence) -- B x H CTAs, enough to fill the GPU even
+// when a GPU holds one kv head -- and thread d owns column d.  By the time this runs the partials
+// have usually left L2 (the split kernel streamed the whole cache through it after writing them),
+// so thread d first issues its column's loads for the first kCombineBatch chunks; meanwhile the
+// block takes the chunks' maximum and the weights exp2(m_c - M), and sum_c l_c w_c, by
+// reductions in a fixed order (deterministic), and only then are the columns summed, in chunk
+// order.
 constexpr int kMaxChunks = 128;
-constexpr int kCombineBatch = 8;   // chunks per batch of loads in flight (all heads at once)
+constexpr int kCombineBatch = 8;   // chunks per batch of loads in flight
+constexpr int kCombineThreads = 128;
+static_assert(kMaxChunks <= kCombineThreads, "a thread per chunk for the weights");
 
 template <int D>
-__global__ void __launch_bounds__(128) decode_combine_kernel(DecodeArgs a) {
-    __shared__ float s_m[kMaxGroup * kMaxChunks];   // m, then the chunk weight
-    __shared__ float s_l[kMaxGroup * kMaxChunks];
-    __shared__ float s_inv[kMaxGroup];
+__global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(DecodeArgs a) {
+    __shared__ float s_w[kMaxChunks];   // chunk weights exp2(m_c - M)
+    __shared__ float s_red[2][kCombineThreads / 32];
     pdl_wait();      // partials come from the split kernel launched just before
-    const int g = blockIdx.x, b = blockIdx.y;
+    const int g = blockIdx.x / a.n_rep, r = blockIdx.x - g * a.n_rep, b = blockIdx.y;
     // the split grid has finished handing out items: ready the counter for the next call
-    if (g == 0 && b == 0 && threadIdx.x == 0 && a.item_counter != nullptr) *a.item_counter = 0u;
+    if (blockIdx.x == 0 && b == 0 && threadIdx.x == 0 && a.item_counter != nullptr) *a.item_counter = 0u;
     int L = a.kv_lens ? a.kv_lens[b] : a.max_len;
     L = L < 0 ? 0 : (L > a.max_len ? a.max_len : L);
     const int nch_b = (L + a.chunk - 1) / a.chunk;
     if (nch_b <= 1) return;  // written directly by the split kernel
     const int64_t item0 = ((int64_t)b * a.Hkv + g) * a.nch;
-    const int d = threadIdx.x;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int64_t step = (int64_t)a.n_rep * D;   // next chunk, same head
-    const float* col = a.part_o + (item0 * a.n_rep) * D + d;
-    // the first batch of this thread's column loads, all heads, before anything else
-    float v[kMaxGroup][kCombineBatch];
+    const float* col = a.part_o + (item0 * a.n_rep + r) * D + t;
+    // the first batch of this thread's column loads, before anything else
+    float v[kCombineBatch];
     const int nb0 = nch_b < kCombineBatch ? nch_b : kCombineBatch;
 #pragma unroll
-    for (int r = 0; r < kMaxGroup; ++r)
-#pragma unroll
-        for (int c = 0; c < kCombineBatch; ++c)
-            v[r][c] = (d < D && r < a.n_rep && c < nb0) ? col[r * D + c * step] : 0.f;
-    const int n = a.n_rep * nch_b;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const int r = i / nch_b, c = i - r * nch_b;
-        const float2 ml = *reinterpret_cast<const float2*>(a.part_ml + ((item0 + c) * a.n_rep + r) * 2);
-        s_m[i] = ml.x;
-        s_l[i] = ml.y;
+    for (int c = 0; c < kCombineBatch; ++c) v[c] = (t < D && c < nb0) ? col[c * step] : 0.f;
+    // chunk t's (m, l) of this row
+    float m = -INFINITY, l = 0.f;
+    if (t < nch_b) {
+        const float2 ml = *reinterpret_cast<const float2*>(a.part_ml + ((item0 + t) * a.n_rep + r) * 2);
+        m = ml.x;
+        l = ml.y;
     }
-    __syncthreads();
-    if (threadIdx.x < a.n_rep) {
-        const int r = threadIdx.x;
-        float M = -INFINITY;
-        for (int c = 0; c < nch_b; ++c) M = fmaxf(M, s_m[r * nch_b + c]);
-        const float Mu = (M == -INFINITY) ? 0.f : M;
-        float Lt = 0.f;
-        for (int c = 0; c < nch_b; ++c) {
-            const float w = ex2_approx(s_m[r * nch_b + c] - Mu);
-            s_m[r * nch_b + c] = w;
-            Lt += s_l[r * nch_b + c] * w;
-        }
-        s_inv[r] = (Lt > 0.f) ? 1.f / Lt : 0.f;
-    }
-    __syncthreads();
-    if (d >= D) return;
-    float acc[kMaxGroup];
+    float mx = m;
 #pragma unroll
-    for (int r = 0; r < kMaxGroup; ++r) acc[r] = 0.f;
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) s_red[0][warp] = mx;
+    __syncthreads();
+    float M = s_red[0][0];
+#pragma unroll
+    for (int w = 1; w < kCombineThreads / 32; ++w) M = fmaxf(M, s_red[0][w]);
+    const float Mu = (M == -INFINITY) ? 0.f : M;
+    const float wgt = (t < nch_b) ? ex2_approx(m - Mu) : 0.f;
+    if (t < nch_b) s_w[t] = wgt;
+    float lw = l * wgt;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, o);
+    if (lane == 0) s_red[1][warp] = lw;
+    __syncthreads();
+    float Lt = s_red[1][0];
+#pragma unroll
+    for (int w = 1; w < kCombineThreads / 32; ++w) Lt += s_red[1][w];
+    const float inv = (Lt > 0.f) ? 1.f / Lt : 0.f;
+    if (t >= D) return;
+    float acc = 0.f;
     for (int c0 = 0; c0 < nch_b; c0 += kCombineBatch) {
         if (c0 > 0) {   // the next batch (sequences of more than kCombineBatch chunks)
 #pragma unroll
-            for (int r = 0; r < kMaxGroup; ++r)
-#pragma unroll
-                for (int c = 0; c < kCombineBatch; ++c)
-                    v[r][c] = (r < a.n_rep && c0 + c < nch_b) ? col[r * D + (c0 + c) * step] : 0.f;
+            for (int c = 0; c < kCombineBatch; ++c) v[c] = (c0 + c < nch_b) ? col[(c0 + c) * step] : 0.f;
         }
 #pragma unroll
-        for (int r = 0; r < kMaxGroup; ++r)
-#pragma unroll
-            for (int c = 0; c < kCombineBatch; ++c)
-                if (r < a.n_rep && c0 + c < nch_b) acc[r] += v[r][c] * s_m[r * nch_b + c0 + c];
+        for (int c = 0; c < kCombineBatch; ++c)
+            if (c0 + c < nch_b) acc += v[c] * s_w[c0 + c];
     }
-#pragma unroll
-    for (int r = 0; r < kMaxGroup; ++r)
-        if (r < a.n_rep)
-            a.out[((int64_t)b * a.H + (int64_t)g * a.n_rep + r) * D + d] = __float2bfloat16_rn(acc[r] * s_inv[r]);
+    a.out[((int64_t)b * a.H + (int64_t)g * a.n_rep + r) * D + t] = __float2bfloat16_rn(acc * inv);
 }
 
 // Chunking of the cache rows into work items, with chunks of at least 256 rows (amortises the
 // per-item merge).
 constexpr int kMinChunk = 256;
 constexpr double kCombineTiles = 4.0;   // the combine launch after a split grid, in tile-times
+// An item's set-up (its q rows, the first K/V tiles' latency) and its share of the merge, in
+// tile-times: fitted on the Qwen3-14B ragged batch (64 sequences of U[256, 32768] rows), where it
+// picks the fastest measured chunk counts with one and with eight kv heads.
+constexpr double kItemTiles = 2.0;
 
 int max_chunks(int max_len) { return std::min(kMaxChunks, std::max(1, (max_len + kMinChunk - 1) / kMinChunk)); }
 
 // Picks the chunk count per sequence for a grid of `grid` persistent CTAs, in units of one
 // CTA's time per 64-row tile.  One chunk per (sequence, kv head): every CTA takes at most
 // ceil(items / grid) items under the static schedule, no partials, no combine.  Several: the
-// CTAs take items from the counter, so the work (tiles plus about half a tile of merge per item)
+// CTAs take items from the counter, so the work (tiles plus kItemTiles per item)
 // spreads evenly over the grid, and the step ends about one item after the average CTA, plus
-// the combine launch (about four tile-times, measured).
+// the combine launch (about four tile-times, measured).  Each item costs kItemTiles beyond its
+// tiles.
 void plan_chunks(int B, int Hkv, int max_len, int grid, int& chunk, int& nch) {
     const int64_t pairs = (int64_t)B * Hkv;
     const int64_t tiles = (max_len + kTile - 1) / kTile;
@@ -666,8 +665,8 @@ void plan_chunks(int B, int Hkv, int max_len, int grid, int& chunk, int& nch) {
         const int64_t n_eff = (tiles + chunk_tiles - 1) / chunk_tiles;   // chunks actually used
         const int64_t items = pairs * n_eff;
         const double cost = n_eff == 1
-            ? (double)((items + grid - 1) / grid) * ((double)chunk_tiles + 0.5)
-            : (double)items * ((double)chunk_tiles + 0.5) / grid + (double)chunk_tiles + kCombineTiles;
+            ? (double)((items + grid - 1) / grid) * ((double)chunk_tiles + kItemTiles)
+            : (double)items * ((double)chunk_tiles + kItemTiles) / grid + (double)chunk_tiles + kCombineTiles;
         if (cost < best - 1e-9) {
             best = cost;
             best_n = (int)n_eff;
@@ -712,7 +711,8 @@ int launch_decode_d(DecodeArgs& a, const CUtensorMap& tmK, const CUtensorMap& tm
                             "decode_split_kernel launch"))
         return st;
     if (a.nch > 1) {
-        if (int st = check_cuda(launch_pdl(decode_combine_kernel<D>, dim3(a.Hkv, a.B), dim3(128), 0, s, a),
+        if (int st = check_cuda(launch_pdl(decode_combine_kernel<D>, dim3(a.Hkv * a.n_rep, a.B), dim3(kCombineThreads),
+                                           0, s, a),
                                 "decode_combine_kernel launch")) {
             // The split grid is queued and takes items from the counter, which only the combine
             // resets: zero it in stream order so the workspace's next call starts clean.

@@ -6,6 +6,8 @@ Cases (Qwen3-8B attention geometry: 32 q heads, 8 kv heads, head_dim 128, hidden
   epilogue   QK-RMSNorm + RoPE + cache append of B x S prefill tokens (qkv_epilogue_tma_kernel)
   prefill    causal attention of B x S rows over a cache of S rows (prefill_kernel)
   decode     one query row per sequence over L cache rows, B sequences (decode_split_kernel)
+  ragged     Qwen3-14B decode over 64 sequences of seeded lengths U[256, 32768], --kv-heads kv heads
+             (5 q heads each): 8 is one GPU's share at 1 GPU, 1 at 8 GPUs
   linear     q|k|v projection of T tokens, bf16 weights (linear_kernel)
   linear_fp8 the same with e4m3 weights and 128 x 128 block scales (linear_fp8_kernel)
 
@@ -74,6 +76,23 @@ def _decode(args, dev, g):
     return launch, {"batch": B, "kv_len": L, "bytes": 2 * B * HKV * L * D * 2}
 
 
+def _ragged(args, dev, g):
+    import numpy as np
+    B, rep = 64, 5
+    lens = np.random.default_rng(14).integers(256, 32768 + 1, size=B)
+    hkv = args.kv_heads
+    L = int(lens.max())
+    cache = rt.KVCache(B, hkv, D, L, device=dev)
+    cache.key_buf.normal_(generator=g)
+    cache.value_buf.normal_(generator=g)
+    cache.set_lengths([int(x) for x in lens])
+    q = torch.randn(B, hkv * rep, 1, D, device=dev, generator=g).bfloat16()
+
+    def launch():
+        rt.decode_attention(q, cache, hkv, max_kv_len=L)
+    return launch, {"kv_heads": hkv, "batch": B, "bytes": int(lens.sum()) * hkv * D * 2 * 2}
+
+
 def _linear(args, dev, g, fp8):
     """Launches cycle through a ring of weight sets larger than L2 (126 MB), so that every launch
     streams its weights from HBM."""
@@ -101,18 +120,19 @@ def _linear(args, dev, g, fp8):
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("case", choices=["epilogue", "prefill", "decode", "linear", "linear_fp8"])
+    ap.add_argument("case", choices=["epilogue", "prefill", "decode", "ragged", "linear", "linear_fp8"])
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--seq", type=int, default=8192)
     ap.add_argument("--kv-len", type=int, default=4096)
     ap.add_argument("--tokens", type=int, default=32)
+    ap.add_argument("--kv-heads", type=int, default=1, help="ragged: kv heads (Qwen3-14B has 8)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--graph", action=argparse.BooleanOptionalAction, default=None,
                     help="time the launches as one CUDA graph (default: on for linear and linear_fp8)")
     args = ap.parse_args(argv)
     if args.graph is None:
-        args.graph = args.case in ("linear", "linear_fp8")
+        args.graph = args.case in ("linear", "linear_fp8", "ragged")
     if args.batch is None:
         args.batch = 32 if args.case == "decode" else 4
     if not torch.cuda.is_available():
@@ -126,6 +146,8 @@ def main(argv=None):
         launch, info = _prefill(args, dev, g)
     elif args.case == "decode":
         launch, info = _decode(args, dev, g)
+    elif args.case == "ragged":
+        launch, info = _ragged(args, dev, g)
     else:
         launch, info = _linear(args, dev, g, args.case == "linear_fp8")
     for _ in range(args.warmup):

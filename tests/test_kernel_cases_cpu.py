@@ -9,7 +9,7 @@ def test_kernel_cases_refuses_without_a_gpu():
     if torch.cuda.is_available():
         pytest.skip("a GPU is present")
     from mllm_b200 import kernel_cases
-    for case in ("epilogue", "prefill", "decode", "linear", "linear_fp8"):
+    for case in ("epilogue", "prefill", "decode", "ragged", "linear", "linear_fp8"):
         with pytest.raises(SystemExit, match="needs a CUDA device"):
             kernel_cases.main([case, "--iters", "1"])
 
