@@ -373,7 +373,8 @@ __global__ void __launch_bounds__(256, (D == 128 && RPQ >= 4) ? 2 : 3) qkv_epilo
 // lane as the scalar multiply does), and every sum a scalar __fadd_rn / __fsub_rn, so that no
 // product is contracted into its sum.  The outputs are bit-identical to the other kernels'.
 // ---------------------------------------------------------------------------------------------
-constexpr int kStTokens = 4;
+constexpr int kStTokens = 4;        // tokens per group
+constexpr int kStTokensFew = 16;    // tokens per group when fewer than 16 q+k heads share the GPU
 constexpr int kStMaxThreads = 192;   // a thread per row up to 48 q+k heads; more heads loop
 constexpr int kStMinBlocks = 3;      // at least three blocks per SM: at most 113 registers a thread
 
@@ -415,29 +416,28 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void*
 // Shared memory of the TMA kernel for head dimension D, H q heads and Hkv kv heads: the boxes
 // (q, k, v; per tensor one region per 64-column half, each a multiple of 1 KB), then the angles,
 // gamma, inv_freq, the per-token cache rows (3 ints per token) and the mbarrier.
-template <int D>
+template <int D, int KT>
 struct TmaEpiSmem {
     static constexpr int kHalves = D / 64;
     // floats per token in the angle table (cos | sin | 4 of padding): the rows a warp transforms
     // belong to four tokens, whose table reads then fall in different bank groups
     static constexpr int kAng = 2 * D + 4;
-    __host__ __device__ static uint32_t region(int heads) { return ((uint32_t)kStTokens * heads * 128 + 1023) & ~1023u; }
+    __host__ __device__ static uint32_t region(int heads) { return ((uint32_t)KT * heads * 128 + 1023) & ~1023u; }
     __host__ __device__ static uint32_t stage_bytes(int H, int Hkv) { return kHalves * (region(H) + 2 * region(Hkv)); }
     __host__ __device__ static size_t bytes(int H, int Hkv) {
-        return 1024 + (size_t)stage_bytes(H, Hkv) + (size_t)kStTokens * kAng * 4 + 2 * D * 4 + (D / 2) * 4 +
-               kStTokens * 3 * 4 + 16;
+        return 1024 + (size_t)stage_bytes(H, Hkv) + (size_t)KT * kAng * 4 + 2 * D * 4 + (D / 2) * 4 + KT * 3 * 4 +
+               16;
     }
 };
 
-template <int D>
+template <int D, int KT>
 __global__ void __launch_bounds__(kStMaxThreads, kStMinBlocks) qkv_epilogue_tma_kernel(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmQo,
     const __grid_constant__ CUtensorMap tmKc, const __grid_constant__ CUtensorMap tmVc, EpilogueArgs a) {
-    using L = TmaEpiSmem<D>;
+    using L = TmaEpiSmem<D, KT>;
     constexpr int HALVES = L::kHalves;
     constexpr int NC = D / 8;                     // 16-byte chunks per row
-    constexpr int KT = kStTokens;
     extern __shared__ unsigned char tma_smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tma_smem_raw) + 1023) &
                                                          ~uintptr_t(1023));
@@ -548,8 +548,12 @@ __global__ void __launch_bounds__(kStMaxThreads, kStMinBlocks) qkv_epilogue_tma_
                 const int tl = idx / (D / 2), col = idx - tl * (D / 2);
                 const float angle = __fmul_rn(
                     (float)a.positions[(int64_t)b * a.pos_sb + (int64_t)(s0 + tl) * a.pos_ss], s_inv_freq[col]);
-                s_ang[tl * L::kAng + col] = cosf(angle);
-                s_ang[tl * L::kAng + D + col] = sinf(angle);
+                float sn, cs;
+                // one argument reduction for both; the GPU tests check that the rows equal those of
+                // the warp kernel, which calls cosf and sinf (rope_angle_cos_sin)
+                sincosf(angle, &sn, &cs);
+                s_ang[tl * L::kAng + col] = cs;
+                s_ang[tl * L::kAng + D + col] = sn;
             }
         }
         // this group's boxes landed (one thread waits; a timeout stops the whole block, its error
@@ -765,7 +769,7 @@ int epilogue_entry(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh, cons
     const int total_heads = num_heads + 2 * num_kv_heads;
     const int64_t tokens = (int64_t)batch * seq_len;
     cudaStream_t st = (cudaStream_t)stream;
-    // Many tokens, every row 16-byte aligned: TMA boxes of kStTokens tokens x all heads.
+    // Many tokens, every row 16-byte aligned: TMA boxes of a group of tokens x all heads.
     if (tokens >= 1024 && num_heads <= 256) {
         bool al = aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(q_out, 16) && aligned(k_cache, 16) &&
                   aligned(v_cache, 16);
@@ -774,17 +778,24 @@ int epilogue_entry(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh, cons
         for (int64_t st8 : {q_sb, k_sb, v_sb}) al = al && (batch == 1 || (st8 > 0 && st8 % 8 == 0));
         int sms = 0;
         if (int e = require_sm100(&sms)) return e;
-        const size_t smem = head_dim == 128 ? TmaEpiSmem<128>::bytes(num_heads, num_kv_heads)
-                                            : TmaEpiSmem<64>::bytes(num_heads, num_kv_heads);
+        // tokens per group: 4 with many heads; 16 when few heads share a GPU (a tensor-parallel
+        // rank's share), so that a group still gives its block several warps of rows
+        const bool wide = num_heads + num_kv_heads < 16;
+        const int kt_tokens = wide ? kStTokensFew : kStTokens;
+        const size_t smem = head_dim == 128
+            ? (wide ? TmaEpiSmem<128, kStTokensFew>::bytes(num_heads, num_kv_heads)
+                    : TmaEpiSmem<128, kStTokens>::bytes(num_heads, num_kv_heads))
+            : (wide ? TmaEpiSmem<64, kStTokensFew>::bytes(num_heads, num_kv_heads)
+                    : TmaEpiSmem<64, kStTokens>::bytes(num_heads, num_kv_heads));
         const int64_t cache_rows = lay.table ? lay.block_size : cache_capacity;
-        if (al && smem <= 200 * 1024 && seq_len >= kStTokens && cache_rows >= kStTokens) {
+        if (al && smem <= 200 * 1024 && seq_len >= kt_tokens && cache_rows >= kt_tokens) {
             // tensor maps {D, rows, heads, batch}: q/k/v by token (batch stride arbitrary for B = 1),
             // q_out [B, H, S, D], the cache by (sequence or block, kv head, row)
             const int64_t S = seq_len, D = head_dim;
             auto bstride = [&](int64_t sb, int64_t ss) { return batch == 1 ? S * ss : sb; };
             const int64_t cache_batch = lay.table ? lay.num_blocks : (cu_seqlens ? n_seqs : batch);
             CUtensorMap mq, mk, mv, mqo, mkc, mvc;
-            const uint32_t kt = kStTokens;
+            const uint32_t kt = (uint32_t)kt_tokens;
             if (int e = encode_kv_map(&mq, q, D, S, num_heads, batch, q_ss, q_sh, bstride(q_sb, q_ss), 64, kt,
                                       (uint32_t)num_heads))
                 return e;
@@ -803,35 +814,39 @@ int epilogue_entry(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh, cons
             if (int e = encode_kv_map(&mvc, v_cache, D, cache_rows, num_kv_heads, cache_batch, cache_st, cache_sh,
                                       cache_sb, 64, kt, (uint32_t)num_kv_heads))
                 return e;
-            const int threads = std::min(kStMaxThreads, (kStTokens * (num_heads + num_kv_heads) + 31) / 32 * 32);
-            const int64_t groups = (int64_t)batch * ((seq_len + kStTokens - 1) / kStTokens);
+            const int threads = std::min(kStMaxThreads, (kt_tokens * (num_heads + num_kv_heads) + 31) / 32 * 32);
+            const int64_t groups = (int64_t)batch * ((seq_len + kt_tokens - 1) / kt_tokens);
             auto launch = [&](auto kern) {
                 if (int e = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                             (int)smem),
                                        "qkv_epilogue smem"))
                     return e;
                 // persistent: as many blocks as fit on the GPU at once (registers and shared memory),
-                // queried once per device, head dimension, block size and shared-memory size
-                struct Fit { int dev = -1, d = 0, threads = 0; size_t smem = 0; int per_sm = 0; };
+                // queried once per device, head dimension, group size, block size and shared-memory size
+                struct Fit { int dev = -1, d = 0, kt = 0, threads = 0; size_t smem = 0; int per_sm = 0; };
                 static thread_local Fit fits[8];
                 int dev = 0;
                 if (int e = check_cuda(cudaGetDevice(&dev), "qkv_epilogue device")) return e;
                 int per_sm = 0;
                 for (const Fit& f : fits)
-                    if (f.dev == dev && f.d == head_dim && f.threads == threads && f.smem == smem) per_sm = f.per_sm;
+                    if (f.dev == dev && f.d == head_dim && f.kt == kt_tokens && f.threads == threads && f.smem == smem)
+                        per_sm = f.per_sm;
                 if (per_sm == 0) {
                     if (int e = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem),
                                            "qkv_epilogue occupancy"))
                         return e;
                     static thread_local int next = 0;
-                    fits[next] = Fit{dev, head_dim, threads, smem, per_sm};
+                    fits[next] = Fit{dev, head_dim, kt_tokens, threads, smem, per_sm};
                     next = (next + 1) % 8;
                 }
                 const unsigned blocks = (unsigned)std::min<int64_t>(groups, (int64_t)sms * std::max(per_sm, 1));
                 kern<<<blocks, threads, smem, st>>>(mq, mk, mv, mqo, mkc, mvc, a);
                 return check_cuda(cudaGetLastError(), "qkv_epilogue launch");
             };
-            const int e = head_dim == 128 ? launch(qkv_epilogue_tma_kernel<128>) : launch(qkv_epilogue_tma_kernel<64>);
+            const int e = head_dim == 128 ? (wide ? launch(qkv_epilogue_tma_kernel<128, kStTokensFew>)
+                                                  : launch(qkv_epilogue_tma_kernel<128, kStTokens>))
+                                          : (wide ? launch(qkv_epilogue_tma_kernel<64, kStTokensFew>)
+                                                  : launch(qkv_epilogue_tma_kernel<64, kStTokens>));
             if (e) return e;
             return ok();
         }

@@ -28,6 +28,7 @@ H, HKV, D, HIDDEN = 32, 8, 128, 4096
 
 def _epilogue(args, dev, g):
     B, S = args.batch, args.seq
+    H, HKV = (args.heads, args.kv_heads) if args.heads else (32, 8)   # --heads: one GPU's share
     row = (H + 2 * HKV) * D
     qkv = (torch.randn(B, S, row, device=dev, generator=g) * 0.5).bfloat16()
     q = qkv[..., : H * D].view(B, S, H, D).transpose(1, 2)
@@ -47,7 +48,7 @@ def _epilogue(args, dev, g):
                  v.stride(1), B, S, H, HKV, D, pos.data_ptr(), 0, 1, 1e6, None, None, 0, 0, gq.data_ptr(),
                  gk.data_ptr(), 1e-6, q_out.data_ptr(), cache.key_buf.data_ptr(), cache.value_buf.data_ptr(),
                  csb, csh, cst, S, start.data_ptr(), 0, abi.stream_handle())
-    return launch, {"batch": B, "seq": S, "bytes": 2 * B * S * row * 2}
+    return launch, {"batch": B, "seq": S, "heads": H, "kv_heads": HKV, "bytes": 2 * B * S * row * 2}
 
 
 def _prefill(args, dev, g):
@@ -125,7 +126,11 @@ def main(argv=None):
     ap.add_argument("--seq", type=int, default=8192)
     ap.add_argument("--kv-len", type=int, default=4096)
     ap.add_argument("--tokens", type=int, default=32)
-    ap.add_argument("--kv-heads", type=int, default=1, help="ragged: kv heads (Qwen3-14B has 8)")
+    ap.add_argument("--kv-heads", type=int, default=1,
+                    help="ragged: kv heads (Qwen3-14B has 8); epilogue: kv heads with --heads")
+    ap.add_argument("--heads", type=int, default=0,
+                    help="epilogue: q heads (0: the whole Qwen3-8B, 32 q / 8 kv heads; 4 with --kv-heads 1 is "
+                         "one GPU's share at 8 GPUs)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--graph", action=argparse.BooleanOptionalAction, default=None,
