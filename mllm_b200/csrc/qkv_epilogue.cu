@@ -344,26 +344,27 @@ __global__ void __launch_bounds__(256, (D == 128 && RPQ >= 4) ? 2 : 3) qkv_epilo
 }
 
 // ---------------------------------------------------------------------------------------------
-// Many tokens: the rows of kStTokens consecutive tokens of one sequence (a "group") move between
-// HBM and shared memory as TMA tensor boxes, and a thread per q/k row transforms them in place.
+// Many tokens: the rows of KT consecutive tokens of one sequence (a "group": KT = kStTokens, or
+// kStTokensFew when few heads share the GPU) move between HBM and shared memory as TMA tensor
+// boxes, and a thread per q/k row transforms them in place.
 //
 // A persistent block takes groups in turn.  Per group:
 //   1. One thread loads the group's q, k and v rows: per tensor and 64-column half, one box of
-//      {64 columns, kStTokens tokens, all heads} (128-byte swizzle), all completing on the
+//      {64 columns, KT tokens, all heads} (128-byte swizzle), all completing on the
 //      stage's mbarrier -- six copies for the whole group at head_dim 128.
 //   2. The block computes the group's RoPE angles once.
 //   3. A thread per q/k row norms and rotates its row in place: a first pass sums the squares,
 //      a second scales, rounds and rotates the pairs (d, d + D/2).  Row r of a box holds head
-//      r / kStTokens of token r % kStTokens, and its 16-byte chunk c sits at chunk c ^ (r % 8) of
+//      r / KT of token r % KT, and its 16-byte chunk c sits at chunk c ^ (r % 8) of
 //      its 128 bytes, so the 32 rows a warp reads at once fall in different bank groups.
 //   4. One thread stores the boxes: q to q_out ([B, H, S, D], the same box shape, rows past the
-//      sequence end clipped by the TMA unit), k and v to the cache when the group's four cache rows
+//      sequence end clipped by the TMA unit), k and v to the cache when the group's KT cache rows
 //      are consecutive rows of one sequence or block.  Otherwise (a group that ends a sequence,
 //      crosses a packed sequence or a cache block, or holds a refused row) the threads write the
 //      group's valid cache rows with 16-byte stores.
-// Three or four blocks per SM overlap one another's copies with their arithmetic.  (Two stages per block,
-// the next group's copies issued before the current group is computed, measured slower: the
-// second stage's shared memory leaves room for two blocks per SM only.)
+// Three or four blocks per SM overlap one another's copies with their arithmetic.  (Two stages per
+// block, the next group's copies issued before the current group is computed, measured slower:
+// the second stage's shared memory leaves room for two blocks per SM only.)
 //
 // One thread per row keeps the reference's reduction entirely in registers: element d of the row
 // belongs to accumulator P_k[j] with j = d % 8, k = (d / 8) % 4, visited in order of d / 32, then
